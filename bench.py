@@ -1,0 +1,358 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 router + expert-map path (one JSON line on rank 0).
+
+Step = one pass of the fused router + expert-map build (kb_router_maps) over one batch of
+T tokens of synthetic router logits (fp32 [T, 384] ~ N(0,1), bias ~ N(0, 0.1)); T = 65536
+per GPU (the large-T configuration of the metric).  With N GPUs every rank routes its own
+T tokens and the ranks exchange their per-expert counts (all-gather, the expert-parallel
+exchange step), so the work per GPU is fixed ("weak" scaling) and value = N*T / step time.
+
+  value     device-resident throughput: inputs already in HBM, steps replayed from CUDA
+            graphs, four rotating 100 MB input sets (together > the 126 MB L2)
+  e2e       the same op through the C ABI with pinned host buffers: H2D of the logits and
+            D2H of every output inside the timed region
+  roofline  algorithmic bytes of the router+map pass (1632 B/token + 6164 B/call) over its
+            measured device time, against MEASURED_PEAKS.json hbm_gbs
+  cpu_baseline  the reference's eager router + map path on the host cores (rank 0, N=1)
+
+--impl reference times the reference's eager CPU path alone (rank 0; other ranks exit).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "profiling-moe_b200"))
+
+METRIC = "router+expert-map Mtok/s (50-layer non-GEMM decode us/token reported alongside)"
+UNIT = "Mtok/s"
+E, K = 384, 6
+BYTES_PER_TOKEN = 1536 + 24 + 24 + 24 + 24      # logits, ids, w, p2u, u2p
+BYTES_PER_CALL = 384 * 4 + 385 * 8 + 384 * 4    # bias, offsets, counts
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--tokens", type=int, default=65536, help="tokens per GPU per step")
+    p.add_argument("--impl", choices=["kolibri", "reference"], default="kolibri")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML, every 2 ms)
+# ------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device: torch.device):
+        self.samples, self.reasons = [], 0
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = None
+            try:
+                props = torch.cuda.get_device_properties(device)
+                bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+            self.nv, self.h = pynvml, h
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: report no clocks rather than fail the bench
+            self.err = str(e)
+
+    def _reason_bits(self):
+        f = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(f(self.h))
+
+    def _run(self):
+        while not self.stop.is_set():
+            self.sample_once()
+            time.sleep(0.002)
+
+    def sample_once(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= self._reason_bits()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        if self.ok:
+            self.stop = threading.Event()
+            self.sample_once()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self.sample_once()
+            self.stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": self.err}
+        names = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+def measured_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(T: int):
+    """DRAM bytes per call of the router+map kernels from the committed ncu summary."""
+    p = REPO / "profiles" / "router_maps_dram.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    rec = d.get(str(T))
+    return None if rec is None else float(rec["dram_bytes_per_call"])
+
+
+# ------------------------------------------------------------------------------------
+# CPU baseline / reference arm
+# ------------------------------------------------------------------------------------
+def cpu_reference_rate(T: int, steps: int, warmup: int, budget_s: float):
+    from kolibri_b200 import workloads as wl
+    from oracle import kolibri_oracle as orc  # CPU baseline leg only
+    torch.set_num_threads(os.cpu_count() or 1)
+    logits, bias = wl.router_inputs(T, seed=1)
+    for _ in range(max(1, warmup)):
+        orc.router_maps_eager_reference(logits, bias)
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        orc.router_maps_eager_reference(logits, bias)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    med = statistics.median(times)
+    return {"value": T / med / 1e6, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{len(times)} reps of the eager router+map path at T={T} (median)",
+            "ms_per_step": med * 1e3}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cb = cpu_reference_rate(args.tokens, args.steps, args.warmup, budget_s=120.0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(cb["value"], 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(cb["ms_per_step"], 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": f"router+expert-maps T={args.tokens} E=384 k=6 (CPU eager)"},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(cb["value"], 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------
+# B200 arm
+# ------------------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+
+    from kolibri_b200 import _lib, ops
+    from kolibri_b200 import workloads as wl
+
+    T = args.tokens
+    nsets = 4
+    sets = []
+    for s in range(nsets):
+        logits, bias = wl.router_inputs(T, seed=1 + 100 * s + 1000 * rank)
+        sets.append((logits.to(dev), bias.to(dev)))
+    ids = torch.empty(T, K, dtype=torch.int32, device=dev)
+    w = torch.empty(T, K, dtype=torch.float32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int64, device=dev)
+    p2u = torch.empty(T * K, dtype=torch.int32, device=dev)
+    u2p = torch.empty(T * K, dtype=torch.int32, device=dev)
+    gathered = torch.empty(world, E, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws_bytes = lib.kb_router_maps_workspace_bytes(T, E, K)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(dev)
+
+    def step(i):
+        lg, bs = sets[i % nsets]
+        _lib.check(lib.kb_router_maps(lg.data_ptr(), bs.data_ptr(), ids.data_ptr(), w.data_ptr(),
+                                      counts.data_ptr(), offsets.data_ptr(), p2u.data_ptr(),
+                                      u2p.data_ptr(), ws.data_ptr(), ws_bytes, T, E, K, 0,
+                                      _lib.KB_MAPS_AUTO,
+                                      torch.cuda.current_stream(dev).cuda_stream),
+                   "kb_router_maps")
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, counts)
+
+    # Graphs: one per input set (router+maps, and the count all-gather for N>1).
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        for i in range(nsets):
+            step(i)
+    torch.cuda.synchronize(dev)
+    graphs = []
+    if world == 1:
+        for i in range(nsets):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(i)
+            graphs.append(g)
+    run = (lambda i: graphs[i % nsets].replay()) if graphs else step
+    launches_per_step = 2 if lib.kb_router_maps_workspace_bytes(T, E, K) else 1
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            run(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev)
+    with clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(args.steps):
+                run(i)
+            end.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * T / (ms * 1e-3) / 1e6
+
+    # Roofline of the router+map pass (1 GPU: the whole step is that pass).
+    peak, peak_kind = measured_peak()
+    alg_bytes = BYTES_PER_TOKEN * T + BYTES_PER_CALL
+    achieved = alg_bytes / (ms * 1e-3) / 1e9
+    traffic = ncu_traffic(T)
+
+    # e2e through the C ABI with host buffers.
+    e2e = None
+    if not args.no_e2e:
+        lg_h = sets[0][0].cpu().pin_memory()
+        bs_h = sets[0][1].cpu().pin_memory()
+        lg_d = torch.empty_like(sets[0][0])
+        bs_d = torch.empty_like(sets[0][1])
+        outs = [ids, w, counts, offsets, p2u, u2p]
+        outs_h = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+        h2d = lg_h.numel() * 4 + bs_h.numel() * 4
+        d2h = sum(o.numel() * o.element_size() for o in outs)
+
+        def e2e_step():
+            cs = torch.cuda.current_stream(dev)
+            lg_d.copy_(lg_h, non_blocking=True)
+            bs_d.copy_(bs_h, non_blocking=True)
+            _lib.check(lib.kb_router_maps(lg_d.data_ptr(), bs_d.data_ptr(), ids.data_ptr(),
+                                          w.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
+                                          p2u.data_ptr(), u2p.data_ptr(), ws.data_ptr(), ws_bytes,
+                                          T, E, K, 0, _lib.KB_MAPS_AUTO, cs.cuda_stream),
+                       "kb_router_maps")
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, counts)
+            for o, oh in zip(outs, outs_h):
+                oh.copy_(o, non_blocking=True)
+
+        e_steps = max(3, min(args.steps, 50))
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(e_steps):
+                e2e_step()
+            end.record(stream)
+        torch.cuda.synchronize(dev)
+        ems = start.elapsed_time(end) / e_steps
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": round(world * T / (ems * 1e-3) / 1e6, 4), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": round(ems, 4), "steps": e_steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_reference_rate(T, steps=20, warmup=1, budget_s=20.0)
+        cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if world > 1:
+        dist.barrier()
+        graphs.clear()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic",
+        "config": {"workload": f"fused router+expert-maps, T={T} tokens per GPU, E=384, k=6",
+                   "tokens_per_gpu": T, "experts": E, "top_k": K,
+                   "l2": "4 rotating input sets of 100 MB (> 126 MB L2 together)",
+                   "graph": bool(graphs) or world == 1,
+                   "parallelism": f"token-sharded x{world}" + (" + count all-gather" if world > 1 else "")},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "algorithmic_bytes": alg_bytes, "peak_source": peak_kind,
+                     "kernel": "kb_router_maps (router+histogram, scan+scatter)"},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,162 @@
+/*
+ * kolibri_b200.h — C ABI of libkolibri_b200.so, the sm_100a implementation of the
+ * non-GEMM MoE decode hot path of Kolibri-style decoders (router, expert maps,
+ * activation expansion, Q/K RMSNorm + RoPE, sandwich / post-MoE residual norms).
+ *
+ * Conventions shared by every entry point
+ *  - All pointers are device pointers unless stated otherwise; buffers are dense,
+ *    row-major and must not alias unless an entry point says so.
+ *  - Every call is asynchronous on `stream` (0 = legacy default stream), performs no
+ *    host synchronisation and no device allocation; every scratch buffer is passed in.
+ *  - Return value: KB_OK (0) on success; a negative KB_ERR_* for an invalid argument,
+ *    shape, dtype, alignment or workspace size (nothing was launched); a positive
+ *    value is a cudaError_t reported by the launch.
+ *  - Floating point: no fast-math.  expf/sqrtf/division are the IEEE-accurate CUDA
+ *    forms, so results track the PyTorch eager CPU path within the tolerances the
+ *    tests state.
+ */
+#ifndef KOLIBRI_B200_H
+#define KOLIBRI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KB_API __attribute__((visibility("default")))
+#else
+#define KB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t (driver_types.h declares `struct CUstream_st *`). */
+typedef struct CUstream_st *kb_stream_t;
+
+enum {
+    KB_OK = 0,
+    KB_ERR_INVALID_ARG = -1,  /* null pointer, negative size, bad flag           */
+    KB_ERR_UNSUPPORTED = -2,  /* shape / dtype / K / E outside the kernel's range */
+    KB_ERR_ALIGNMENT = -3,    /* pointer or row stride not aligned as required    */
+    KB_ERR_WORKSPACE = -4,    /* workspace missing or smaller than *_workspace_bytes */
+    KB_ERR_TOO_LARGE = -5     /* T*K or row count overflows the int32 index space */
+};
+
+/* Element types of activation tensors. */
+enum { KB_BF16 = 0, KB_F16 = 1, KB_F32 = 2 };
+
+/* Expert-map algorithm selection (`mode` argument). */
+enum { KB_MAPS_AUTO = 0, KB_MAPS_SINGLE_CTA = 1, KB_MAPS_MULTI_CTA = 2 };
+
+KB_API const char *kb_status_str(int status);
+KB_API int kb_version(void);
+/* Programmatic dependent launch on (1, default) or off (0) for every later launch
+ * made by this library in this process.  Returns the previous value. */
+KB_API int kb_set_pdl(int enable);
+
+/* ---------------------------------------------------------------------------------
+ * (a1) Router: scores = logits + bias; ids = top-K of scores (descending, the lower
+ * expert index wins ties, NaN ranks above +inf as in torch.sort); weights =
+ * sigmoid(logits[ids]) of the UN-biased logit; if renorm, weights /= (sum + 1e-20).
+ *   logits fp32 [T, E] (row stride E), bias fp32 [E] or NULL (= zero bias),
+ *   ids int32 [T, K], weights [T, K] in w_dtype (KB_F32, KB_BF16 or KB_F16).
+ *   1 <= K <= 32, K <= E <= 512.
+ * Replaces: kolibri_gate_forward (kernels/cuda/customKolibriRoutingKernels.cu:238-266,
+ * bound by kernels/cuda/router_bindings.cpp:60-104) and _fused_kolibri_router_kernel
+ * (kernels/triton/fused_kolibri_router.py:38-95, launched at :98-146); renorm=1 is the
+ * prologue router invokeKolibriRouter (fusions/03_moe_prologue/fused/custom_moe_prologue.cu:104-119).
+ */
+KB_API int kb_router(const float *logits, const float *bias, int32_t *ids, void *weights,
+              int w_dtype, int64_t T, int E, int K, int renorm, kb_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * (a2) Expert maps from top-K ids [T, K] (int32, row-major, selection s = t*K + k).
+ *   counts   int32 [E]     (may be NULL)   number of selections of each expert
+ *   offsets  int64 [E+1]   exclusive scan of counts; offsets[E] = number of valid ids
+ *   p2u      int32 [T*K]   permuted row -> unpermuted row, unpermuted row = k*T + t
+ *                          (slot-major), rows sorted by (expert, token, slot);
+ *                          entries past offsets[E] are set to -1
+ *   u2p      int32 [T*K]   (may be NULL) inverse: u2p[k*T + t] = permuted row; -1 for
+ *                          an id outside [0, E)
+ * Ids outside [0, E) are skipped, as the reference kernels skip them.
+ * The workspace must be zero-filled before its first use; every call leaves it
+ * zero-filled again (its arrival counters reset themselves).
+ * Replaces: invokeKolibriBuildExpertMaps (kernels/cuda/customKolibriBuildExpertMapsKernel.cu:37-89,
+ * bound at kernels/cuda/build_expert_maps_bindings.cpp:10-40), invokeKolibriMultiBlockBuildExpertMaps
+ * (kernels/cuda/multi_block_expert_maps/customKolibriMultiBlockBuildExpertMapsKernels.cu:36-213)
+ * and invokeDynamicBuildExpertMaps (fusions/03_moe_prologue/fused/custom_moe_prologue.cu:409-444).
+ */
+KB_API size_t kb_expert_maps_workspace_bytes(int64_t T, int E, int K);
+KB_API int kb_expert_maps(const int32_t *ids, int32_t *counts, int64_t *offsets, int32_t *p2u,
+                   int32_t *u2p, void *workspace, size_t workspace_bytes, int64_t T,
+                   int E, int K, int mode, kb_stream_t stream);
+
+/* (a1)+(a2) in one pass over the logits: router outputs (as kb_router, weights fp32)
+ * and the expert maps (as kb_expert_maps) of the ids it selects.
+ * Replaces the router + map stages of invokeFusedMoePrologue
+ * (fusions/03_moe_prologue/fused/custom_moe_prologue.cu:524-547). */
+KB_API size_t kb_router_maps_workspace_bytes(int64_t T, int E, int K);
+KB_API int kb_router_maps(const float *logits, const float *bias, int32_t *ids, float *weights,
+                   int32_t *counts, int64_t *offsets, int32_t *p2u, int32_t *u2p,
+                   void *workspace, size_t workspace_bytes, int64_t T, int E, int K,
+                   int renorm, int mode, kb_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * Activation expansion: out[r] = x[p2u[r] % T] for r in [0, rows); a row whose p2u
+ * is negative or >= rows_total_unpermuted is left untouched.  row_bytes is the row
+ * size in bytes (any element type).  16-byte aligned rows take the vector path.
+ * Replaces: invokeKolibriActivationExpansion (fusions/03_moe_prologue/fused/custom_moe_prologue.cu:481-501)
+ * and invokeKolibriActivationExpansionFromMap (kernels/cuda/customKolibriBuildExpertMapsKernel.cu:197-222).
+ */
+KB_API int kb_expand_rows(const void *x, void *out, const int32_t *p2u, int64_t T, int64_t rows,
+                   int64_t row_bytes, kb_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * (a4) Per-head Q/K RMSNorm fused with NeoX RoPE, bf16 in and out:
+ *   y = x * (1/sqrt(mean(x^2) + eps)) * gamma     (fp32, per head of D elements)
+ *   a_j = float(pos[t]) * inv_freq[j], j < D/2
+ *   out = [y1*cos(a) - y2*sin(a), y2*cos(a) + y1*sin(a)]  -> bf16 (one rounding)
+ * pos == NULL selects the RNoPE layers' identity rotation (pure per-head RMSNorm).
+ * q: [T, Hq, D] with token stride q_tok_stride elements (>= Hq*D), same for k.
+ * q_out/k_out may equal q_in/k_in (in place).  D = 128 (D % 8 == 0, D <= 256).
+ * inv_freq fp32 [D/2] on the device = 1/theta^(2j/D), computed by the caller.
+ * Replaces: TensorRT-LLM fusedQKNormRopeKernel as driven by Kolibri1Attention.apply_rope
+ * (benchmarks/02_benchmark_attention_norm.py:105-112); formula of
+ * scratch/diag_rope_fusion.py:31-38; RNoPE = per-head F.rms_norm of
+ * benchmarks/11_profile_2block_e2e.py:195-196.
+ */
+KB_API int kb_qk_norm_rope(const void *q_in, void *q_out, const void *k_in, void *k_out,
+                    const void *gamma_q, const void *gamma_k, const int32_t *pos,
+                    const float *inv_freq, int64_t T, int Hq, int Hkv, int D,
+                    int64_t q_tok_stride, int64_t k_tok_stride, float eps,
+                    kb_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * (a5)/(a6) Residual norm pair, rows of H elements of `dtype`:
+ *   sum_out  = residual + RMSNorm(a) * g1        (rounded to dtype, then reused)
+ *   norm_out = RMSNorm(sum_out) * g2
+ * As the sandwich norm: a = attn_out, residual = residual_in -> (updated_residual, moe_in)
+ *   Replaces invokeFusedSandwichNormReg (fusions/01_sandwich_norm/fused/custom_sandwich_norm.cu:120-158);
+ *   oracle fusions/01_sandwich_norm/baseline/trtllm_baseline.py:78-95.
+ * As the post-MoE + pre-attention norm: a = moe_out, residual = h -> (out, next)
+ *   (benchmarks/11_profile_2block_e2e.py:229-231 applied after :269-270).
+ * sum_out may alias residual; norm_out may alias a.
+ */
+KB_API int kb_residual_norm_pair(const void *a, const void *residual, const void *g1,
+                          const void *g2, void *sum_out, void *norm_out, int64_t T,
+                          int64_t H, float eps, int dtype, kb_stream_t stream);
+
+/* Add + RMSNorm: sum = a + b (rounded to dtype); out = RMSNorm(sum) * g;
+ * sum_out (may be NULL) receives sum.
+ * Replaces invokeFusedAddPostMoeNorm (fusions/02_post_moe_norm/fused/custom_post_moe_norm.cu:194-228);
+ * oracle fusions/02_post_moe_norm/baseline/trtllm_baseline.py:77-90.  With sum_out it is also
+ * the decoder's input_layernorm (benchmarks/11_profile_2block_e2e.py:229-231). */
+KB_API int kb_add_rms_norm(const void *a, const void *b, const void *g, void *out, void *sum_out,
+                    int64_t T, int64_t H, float eps, int dtype, kb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KOLIBRI_B200_H */

@@ -1,0 +1,356 @@
+// Residual RMSNorm fusions for sm_100a, one CTA per row, 16-byte vectors held in registers.
+//
+//   kb_residual_norm_pair: sum = residual + RMSNorm(a)*g1 ; norm = RMSNorm(sum)*g2
+//     = fused_sandwich_norm (fusions/01_sandwich_norm/fused/fused_sandwich_norm.py:46-72) and the
+//       post-MoE + next-layer pre-attention pair (benchmarks/11_profile_2block_e2e.py:229-231,269-270)
+//   kb_add_rms_norm:       sum = a + b ; out = RMSNorm(sum)*g
+//     = fused_add_post_moe_norm (fusions/02_post_moe_norm/fused/fused_post_moe_norm.py:54-77)
+//
+// Rounding follows the eager reference (fusions/01_sandwich_norm/baseline/trtllm_baseline.py:78-95,
+// fusions/02_post_moe_norm/baseline/trtllm_baseline.py:77-90): F.rms_norm computes
+// dtype((x_f32 * (1/sqrt(mean(x_f32^2) + eps))) * g_f32) with one rounding, the residual add is
+// rounded to the activation dtype, and the second norm reads the rounded sum.  Products use
+// __fmul_rn so that no FMA contraction changes the rounding.
+#include "kb_common.cuh"
+
+#include <algorithm>
+
+namespace kb {
+
+// Block-wide fp32 sum; `red` is a 33-float smem scratch.  All threads get the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nw = (blockDim.x + 31) >> 5;
+    v = warp_sum(v);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float s = (lane < nw) ? red[lane] : 0.0f;
+        s = warp_sum(s);
+        if (lane == 0) red[32] = s;
+    }
+    __syncthreads();
+    const float r = red[32];
+    __syncthreads();  // red is reused by the next reduction
+    return r;
+}
+
+__device__ __forceinline__ float rms_scale(float ss, int H, float eps) {
+    return 1.0f / sqrtf(ss / (float)H + eps);
+}
+
+template <typename T>
+__device__ __forceinline__ float rnd(float v) { return Elem<T>::to_f(Elem<T>::from_f(v)); }
+
+// ------------------------------------------------------------------------------------
+// Register kernels: each thread owns VPT 16-byte vectors v = tid + i*blockDim.
+// ------------------------------------------------------------------------------------
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) residual_norm_pair_kernel(
+    const T* __restrict__ a, const T* __restrict__ res, const T* __restrict__ g1,
+    const T* __restrict__ g2, T* sum_out, T* norm_out, int64_t rows, int H, float eps) {
+    pdl_wait();
+    pdl_launch();
+    using V = Vec16<T>;
+    constexpr int N = V::N;
+    __shared__ float red[33];
+    const int nvec = H / N;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const uint4* pa = reinterpret_cast<const uint4*>(a + row * H);
+        const uint4* pr = reinterpret_cast<const uint4*>(res + row * H);
+        V va[VPT], vr[VPT];
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nvec) {
+                va[i].u = ld_stream(pa + v);
+                vr[i].u = ld_stream(pr + v);
+            } else {
+                va[i].u = make_uint4(0, 0, 0, 0);
+                vr[i].u = make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int e = 0; e < N; ++e) {
+                const float x = Elem<T>::to_f(va[i].e[e]);
+                ss = fmaf(x, x, ss);
+            }
+        }
+        const float r1 = rms_scale(block_sum(ss, red), H, eps);
+        float ss2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nvec) {
+                V vg;
+                vg.u = __ldg(reinterpret_cast<const uint4*>(g1) + v);
+                V vh;
+#pragma unroll
+                for (int e = 0; e < N; ++e) {
+                    const float post = rnd<T>(__fmul_rn(__fmul_rn(Elem<T>::to_f(va[i].e[e]), r1),
+                                                       Elem<T>::to_f(vg.e[e])));
+                    const T h = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(vr[i].e[e]), post));
+                    vh.e[e] = h;
+                    const float hf = Elem<T>::to_f(h);
+                    ss2 = fmaf(hf, hf, ss2);
+                }
+                vr[i].u = vh.u;
+                reinterpret_cast<uint4*>(sum_out + row * H)[v] = vh.u;
+            }
+        }
+        const float r2 = rms_scale(block_sum(ss2, red), H, eps);
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nvec) {
+                V vg;
+                vg.u = __ldg(reinterpret_cast<const uint4*>(g2) + v);
+                V vx;
+#pragma unroll
+                for (int e = 0; e < N; ++e)
+                    vx.e[e] = Elem<T>::from_f(__fmul_rn(__fmul_rn(Elem<T>::to_f(vr[i].e[e]), r2),
+                                                        Elem<T>::to_f(vg.e[e])));
+                reinterpret_cast<uint4*>(norm_out + row * H)[v] = vx.u;
+            }
+        }
+    }
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(1024) add_rms_norm_kernel(
+    const T* __restrict__ a, const T* __restrict__ b, const T* __restrict__ g, T* out, T* sum_out,
+    int64_t rows, int H, float eps) {
+    pdl_wait();
+    pdl_launch();
+    using V = Vec16<T>;
+    constexpr int N = V::N;
+    __shared__ float red[33];
+    const int nvec = H / N;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const uint4* pa = reinterpret_cast<const uint4*>(a + row * H);
+        const uint4* pb = reinterpret_cast<const uint4*>(b + row * H);
+        V vs[VPT];
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nvec) {
+                V va, vb;
+                va.u = ld_stream(pa + v);
+                vb.u = ld_stream(pb + v);
+#pragma unroll
+                for (int e = 0; e < N; ++e) {
+                    vs[i].e[e] = Elem<T>::from_f(
+                        __fadd_rn(Elem<T>::to_f(va.e[e]), Elem<T>::to_f(vb.e[e])));
+                    const float x = Elem<T>::to_f(vs[i].e[e]);
+                    ss = fmaf(x, x, ss);
+                }
+                if (sum_out) reinterpret_cast<uint4*>(sum_out + row * H)[v] = vs[i].u;
+            } else {
+                vs[i].u = make_uint4(0, 0, 0, 0);
+            }
+        }
+        const float r = rms_scale(block_sum(ss, red), H, eps);
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int v = threadIdx.x + i * blockDim.x;
+            if (v < nvec) {
+                V vg, vo;
+                vg.u = __ldg(reinterpret_cast<const uint4*>(g) + v);
+#pragma unroll
+                for (int e = 0; e < N; ++e)
+                    vo.e[e] = Elem<T>::from_f(__fmul_rn(__fmul_rn(Elem<T>::to_f(vs[i].e[e]), r),
+                                                        Elem<T>::to_f(vg.e[e])));
+                reinterpret_cast<uint4*>(out + row * H)[v] = vo.u;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// Generic kernels (any H, any alignment): the row is staged in shared memory as fp32.
+// ------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(512) residual_norm_pair_generic(
+    const T* __restrict__ a, const T* __restrict__ res, const T* __restrict__ g1,
+    const T* __restrict__ g2, T* sum_out, T* norm_out, int64_t rows, int H, float eps) {
+    pdl_wait();
+    pdl_launch();
+    extern __shared__ float rowbuf[];
+    __shared__ float red[33];
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            const float x = Elem<T>::to_f(a[row * H + i]);
+            rowbuf[i] = x;
+            ss = fmaf(x, x, ss);
+        }
+        const float r1 = rms_scale(block_sum(ss, red), H, eps);
+        float ss2 = 0.0f;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            const float post = rnd<T>(__fmul_rn(__fmul_rn(rowbuf[i], r1), Elem<T>::to_f(g1[i])));
+            const T h = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(res[row * H + i]), post));
+            const float hf = Elem<T>::to_f(h);
+            rowbuf[i] = hf;
+            sum_out[row * H + i] = h;
+            ss2 = fmaf(hf, hf, ss2);
+        }
+        const float r2 = rms_scale(block_sum(ss2, red), H, eps);
+        for (int i = threadIdx.x; i < H; i += blockDim.x)
+            norm_out[row * H + i] =
+                Elem<T>::from_f(__fmul_rn(__fmul_rn(rowbuf[i], r2), Elem<T>::to_f(g2[i])));
+        __syncthreads();
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512) add_rms_norm_generic(
+    const T* __restrict__ a, const T* __restrict__ b, const T* __restrict__ g, T* out, T* sum_out,
+    int64_t rows, int H, float eps) {
+    pdl_wait();
+    pdl_launch();
+    extern __shared__ float rowbuf[];
+    __shared__ float red[33];
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            const T s = Elem<T>::from_f(
+                __fadd_rn(Elem<T>::to_f(a[row * H + i]), Elem<T>::to_f(b[row * H + i])));
+            if (sum_out) sum_out[row * H + i] = s;
+            const float x = Elem<T>::to_f(s);
+            rowbuf[i] = x;
+            ss = fmaf(x, x, ss);
+        }
+        const float r = rms_scale(block_sum(ss, red), H, eps);
+        for (int i = threadIdx.x; i < H; i += blockDim.x)
+            out[row * H + i] =
+                Elem<T>::from_f(__fmul_rn(__fmul_rn(rowbuf[i], r), Elem<T>::to_f(g[i])));
+        __syncthreads();
+    }
+}
+
+namespace {
+
+constexpr int kMaxGenericH = 48 * 1024;  // fp32 row in <= 192 KB of shared memory
+
+struct RowShape {
+    int vpt;
+    int threads;
+};
+
+// 16-byte vectors per thread and threads per CTA for a row of nvec vectors.
+inline RowShape row_shape(int nvec) {
+    int vpt = (nvec + 255) / 256;
+    if (vpt > 8) return {0, 0};
+    if (vpt == 5) vpt = 6;
+    if (vpt == 7) vpt = 8;
+    int threads = (nvec + vpt - 1) / vpt;
+    threads = (threads + 31) & ~31;
+    return {vpt, threads};
+}
+
+inline unsigned row_grid(int64_t rows) {
+    return (unsigned)std::min<int64_t>(rows, (int64_t)INT32_MAX);
+}
+
+template <typename T>
+int pair_launch(const void* a, const void* res, const void* g1, const void* g2, void* sum_out,
+                void* norm_out, int64_t rows, int H, float eps, cudaStream_t st) {
+    constexpr int N = 16 / sizeof(T);
+    const bool vec = (H % N == 0) && aligned16(a) && aligned16(res) && aligned16(g1) &&
+                     aligned16(g2) && aligned16(sum_out) && aligned16(norm_out);
+    const RowShape rs = vec ? row_shape(H / N) : RowShape{0, 0};
+    const T* A = static_cast<const T*>(a);
+    const T* R = static_cast<const T*>(res);
+    const T* G1 = static_cast<const T*>(g1);
+    const T* G2 = static_cast<const T*>(g2);
+    T* S = static_cast<T*>(sum_out);
+    T* O = static_cast<T*>(norm_out);
+    dim3 grid(row_grid(rows));
+#define KB_PAIR(V)                                                                           \
+    case V:                                                                                  \
+        return launch(residual_norm_pair_kernel<T, V>, grid, dim3(rs.threads), 0, st, A, R, G1, \
+                      G2, S, O, rows, H, eps);
+    switch (rs.vpt) {
+        KB_PAIR(1) KB_PAIR(2) KB_PAIR(3) KB_PAIR(4) KB_PAIR(6) KB_PAIR(8)
+        default: break;
+    }
+#undef KB_PAIR
+    if (H > kMaxGenericH) return KB_ERR_UNSUPPORTED;
+    const size_t smem = (size_t)H * sizeof(float);
+    int err = allow_smem(residual_norm_pair_generic<T>, smem);
+    if (err) return err;
+    return launch(residual_norm_pair_generic<T>, grid, dim3(512), smem, st, A, R, G1, G2, S, O,
+                  rows, H, eps);
+}
+
+template <typename T>
+int add_launch(const void* a, const void* b, const void* g, void* out, void* sum_out,
+               int64_t rows, int H, float eps, cudaStream_t st) {
+    constexpr int N = 16 / sizeof(T);
+    const bool vec = (H % N == 0) && aligned16(a) && aligned16(b) && aligned16(g) &&
+                     aligned16(out) && (sum_out == nullptr || aligned16(sum_out));
+    const RowShape rs = vec ? row_shape(H / N) : RowShape{0, 0};
+    const T* A = static_cast<const T*>(a);
+    const T* B = static_cast<const T*>(b);
+    const T* G = static_cast<const T*>(g);
+    T* O = static_cast<T*>(out);
+    T* S = static_cast<T*>(sum_out);
+    dim3 grid(row_grid(rows));
+#define KB_ADD(V)                                                                              \
+    case V:                                                                                    \
+        return launch(add_rms_norm_kernel<T, V>, grid, dim3(rs.threads), 0, st, A, B, G, O, S, \
+                      rows, H, eps);
+    switch (rs.vpt) {
+        KB_ADD(1) KB_ADD(2) KB_ADD(3) KB_ADD(4) KB_ADD(6) KB_ADD(8)
+        default: break;
+    }
+#undef KB_ADD
+    if (H > kMaxGenericH) return KB_ERR_UNSUPPORTED;
+    const size_t smem = (size_t)H * sizeof(float);
+    int err = allow_smem(add_rms_norm_generic<T>, smem);
+    if (err) return err;
+    return launch(add_rms_norm_generic<T>, grid, dim3(512), smem, st, A, B, G, O, S, rows, H, eps);
+}
+
+int check_rows(int64_t T, int64_t H, int dtype) {
+    if (T < 0 || H <= 0) return KB_ERR_INVALID_ARG;
+    if (H >= (int64_t)INT32_MAX) return KB_ERR_TOO_LARGE;
+    if (dtype != KB_BF16 && dtype != KB_F16 && dtype != KB_F32) return KB_ERR_UNSUPPORTED;
+    return KB_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" int kb_residual_norm_pair(const void* a, const void* residual, const void* g1,
+                                     const void* g2, void* sum_out, void* norm_out, int64_t T,
+                                     int64_t H, float eps, int dtype, kb_stream_t stream) {
+    int st = check_rows(T, H, dtype);
+    if (st) return st;
+    if (T == 0) return KB_OK;
+    if (!a || !residual || !g1 || !g2 || !sum_out || !norm_out) return KB_ERR_INVALID_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (dtype) {
+        case KB_BF16: return pair_launch<__nv_bfloat16>(a, residual, g1, g2, sum_out, norm_out, T, (int)H, eps, s);
+        case KB_F16: return pair_launch<__half>(a, residual, g1, g2, sum_out, norm_out, T, (int)H, eps, s);
+        default: return pair_launch<float>(a, residual, g1, g2, sum_out, norm_out, T, (int)H, eps, s);
+    }
+}
+
+extern "C" int kb_add_rms_norm(const void* a, const void* b, const void* g, void* out,
+                               void* sum_out, int64_t T, int64_t H, float eps, int dtype,
+                               kb_stream_t stream) {
+    int st = check_rows(T, H, dtype);
+    if (st) return st;
+    if (T == 0) return KB_OK;
+    if (!a || !b || !g || !out) return KB_ERR_INVALID_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (dtype) {
+        case KB_BF16: return add_launch<__nv_bfloat16>(a, b, g, out, sum_out, T, (int)H, eps, s);
+        case KB_F16: return add_launch<__half>(a, b, g, out, sum_out, T, (int)H, eps, s);
+        default: return add_launch<float>(a, b, g, out, sum_out, T, (int)H, eps, s);
+    }
+}

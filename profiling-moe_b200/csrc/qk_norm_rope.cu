@@ -1,0 +1,159 @@
+// Per-head Q/K RMSNorm fused with NeoX RoPE (bf16 in/out, fp32 math) for sm_100a.
+//
+// Math (scratch/diag_rope_fusion.py:31-38, the local statement of TensorRT-LLM's
+// fusedQKNormRopeKernel as driven from benchmarks/02_benchmark_attention_norm.py:105-112):
+//   y   = (x * (1/sqrt(mean(x^2) + eps))) * gamma              per head of D elements
+//   a_j = float(pos) * inv_freq[j]                              j < D/2
+//   out = [y1*cos(a) - y2*sin(a), y2*cos(a) + y1*sin(a)]  ->  bf16
+// RNoPE layers pass no positions (pos == NULL): the rotation is the identity and the kernel
+// is the harness's per-head F.rms_norm (benchmarks/11_profile_2block_e2e.py:195-196).
+//
+// Layout: one warp per (token, head), D/32 consecutive elements per lane, so the NeoX
+// partner of lane l is lane l^16.  A CTA covers HPC heads of one token and computes the
+// D/2 (cos, sin) pairs of that token once in shared memory with the accurate sincosf.
+// Products and sums use _rn intrinsics: no FMA contraction, same roundings as eager torch.
+#include "kb_common.cuh"
+
+#include <algorithm>
+
+namespace kb {
+
+template <int D, int HPC>
+__global__ void __launch_bounds__(HPC * 32) qk_norm_rope_kernel(
+    const __nv_bfloat16* q_in, __nv_bfloat16* q_out, const __nv_bfloat16* k_in,
+    __nv_bfloat16* k_out, const __nv_bfloat16* __restrict__ gq,
+    const __nv_bfloat16* __restrict__ gk, const int32_t* __restrict__ pos,
+    const float* __restrict__ inv_freq, int64_t T, int Hq, int Hkv, int64_t qs, int64_t ks,
+    float eps, int groups) {
+    constexpr int EPL = D / 32;  // elements per lane
+    static_assert(EPL == 2 || EPL == 4 || EPL == 8, "D must be 64, 128 or 256");
+    pdl_wait();
+    pdl_launch();
+    __shared__ float cs[D / 2], sn[D / 2];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t = blockIdx.x / groups;
+    const int head = (int)(blockIdx.x % groups) * HPC + warp;
+    const bool active = head < Hq + Hkv;
+    const bool is_q = head < Hq;
+    const __nv_bfloat16* src = is_q ? q_in + t * qs + (int64_t)head * D
+                                    : k_in + t * ks + (int64_t)(head - Hq) * D;
+    __nv_bfloat16* dst = is_q ? q_out + t * qs + (int64_t)head * D
+                              : k_out + t * ks + (int64_t)(head - Hq) * D;
+    const __nv_bfloat16* g = is_q ? gq : gk;
+
+    // Issue the head's loads before the trigonometry.
+    __nv_bfloat16 xv[EPL], gv[EPL];
+    if (active) {
+        if constexpr (EPL == 2) {
+            *reinterpret_cast<uint32_t*>(xv) = *reinterpret_cast<const uint32_t*>(src + lane * 2);
+            *reinterpret_cast<uint32_t*>(gv) = __ldg(reinterpret_cast<const unsigned*>(g + lane * 2));
+        } else if constexpr (EPL == 4) {
+            *reinterpret_cast<uint2*>(xv) = *reinterpret_cast<const uint2*>(src + lane * 4);
+            *reinterpret_cast<uint2*>(gv) = __ldg(reinterpret_cast<const uint2*>(g + lane * 4));
+        } else {
+            *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(src + lane * 8);
+            *reinterpret_cast<uint4*>(gv) = __ldg(reinterpret_cast<const uint4*>(g + lane * 8));
+        }
+    }
+    const bool rope = pos != nullptr;
+    if (rope) {
+        const float p = (float)__ldg(pos + t);
+        for (int j = threadIdx.x; j < D / 2; j += blockDim.x) {
+            float s_, c_;
+            sincosf(__fmul_rn(p, __ldg(inv_freq + j)), &s_, &c_);
+            cs[j] = c_;
+            sn[j] = s_;
+        }
+        __syncthreads();
+    }
+    if (!active) return;
+
+    float y[EPL];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        y[i] = __bfloat162float(xv[i]);
+        ss = fmaf(y[i], y[i], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) y[i] = __fmul_rn(__fmul_rn(y[i], r), __bfloat162float(gv[i]));
+
+    __nv_bfloat16 ov[EPL];
+    if (rope) {
+        const bool first_half = lane < 16;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const float other = __shfl_xor_sync(FULL_MASK, y[i], 16);
+            const int j = (lane * EPL + i) & (D / 2 - 1);
+            const float c = cs[j], s = sn[j];
+            const float o = first_half ? __fsub_rn(__fmul_rn(y[i], c), __fmul_rn(other, s))
+                                       : __fadd_rn(__fmul_rn(y[i], c), __fmul_rn(other, s));
+            ov[i] = __float2bfloat16_rn(o);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) ov[i] = __float2bfloat16_rn(y[i]);
+    }
+    if constexpr (EPL == 2) {
+        *reinterpret_cast<uint32_t*>(dst + lane * 2) = *reinterpret_cast<uint32_t*>(ov);
+    } else if constexpr (EPL == 4) {
+        *reinterpret_cast<uint2*>(dst + lane * 4) = *reinterpret_cast<uint2*>(ov);
+    } else {
+        *reinterpret_cast<uint4*>(dst + lane * 8) = *reinterpret_cast<uint4*>(ov);
+    }
+}
+
+namespace {
+
+template <int D>
+int qk_launch(const void* q_in, void* q_out, const void* k_in, void* k_out, const void* gq,
+              const void* gk, const int32_t* pos, const float* inv_freq, int64_t T, int Hq,
+              int Hkv, int64_t qs, int64_t ks, float eps, cudaStream_t st) {
+    constexpr int HPC = 8;
+    const int heads = Hq + Hkv;
+    const int groups = (heads + HPC - 1) / HPC;
+    const int64_t ctas = T * groups;
+    if (ctas > (int64_t)INT32_MAX) return KB_ERR_TOO_LARGE;
+    return launch(qk_norm_rope_kernel<D, HPC>, dim3((unsigned)ctas), dim3(HPC * 32), 0, st,
+                  static_cast<const __nv_bfloat16*>(q_in), static_cast<__nv_bfloat16*>(q_out),
+                  static_cast<const __nv_bfloat16*>(k_in), static_cast<__nv_bfloat16*>(k_out),
+                  static_cast<const __nv_bfloat16*>(gq), static_cast<const __nv_bfloat16*>(gk),
+                  pos, inv_freq, T, Hq, Hkv, qs, ks, eps, groups);
+}
+
+inline bool aligned_to(const void* p, unsigned a) {
+    return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+}  // namespace
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" int kb_qk_norm_rope(const void* q_in, void* q_out, const void* k_in, void* k_out,
+                               const void* gamma_q, const void* gamma_k, const int32_t* pos,
+                               const float* inv_freq, int64_t T, int Hq, int Hkv, int D,
+                               int64_t q_tok_stride, int64_t k_tok_stride, float eps,
+                               kb_stream_t stream) {
+    if (T < 0 || Hq < 0 || Hkv < 0) return KB_ERR_INVALID_ARG;
+    if (D != 64 && D != 128 && D != 256) return KB_ERR_UNSUPPORTED;
+    if (T == 0 || Hq + Hkv == 0) return KB_OK;
+    if ((Hq > 0 && (!q_in || !q_out || !gamma_q)) || (Hkv > 0 && (!k_in || !k_out || !gamma_k)))
+        return KB_ERR_INVALID_ARG;
+    if (pos && !inv_freq) return KB_ERR_INVALID_ARG;
+    if (q_tok_stride < (int64_t)Hq * D || k_tok_stride < (int64_t)Hkv * D) return KB_ERR_INVALID_ARG;
+    // Each lane moves D/32 bf16 = D/16 bytes: rows and strides must keep that alignment.
+    const unsigned al = (unsigned)(D / 16);
+    const int64_t se = al / 2;  // stride alignment in elements
+    if (Hq > 0 && (!aligned_to(q_in, al) || !aligned_to(q_out, al) || q_tok_stride % se)) return KB_ERR_ALIGNMENT;
+    if (Hkv > 0 && (!aligned_to(k_in, al) || !aligned_to(k_out, al) || k_tok_stride % se)) return KB_ERR_ALIGNMENT;
+    if ((Hq > 0 && !aligned_to(gamma_q, al)) || (Hkv > 0 && !aligned_to(gamma_k, al))) return KB_ERR_ALIGNMENT;
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (D) {
+        case 64: return qk_launch<64>(q_in, q_out, k_in, k_out, gamma_q, gamma_k, pos, inv_freq, T, Hq, Hkv, q_tok_stride, k_tok_stride, eps, st);
+        case 128: return qk_launch<128>(q_in, q_out, k_in, k_out, gamma_q, gamma_k, pos, inv_freq, T, Hq, Hkv, q_tok_stride, k_tok_stride, eps, st);
+        default: return qk_launch<256>(q_in, q_out, k_in, k_out, gamma_q, gamma_k, pos, inv_freq, T, Hq, Hkv, q_tok_stride, k_tok_stride, eps, st);
+    }
+}

@@ -1,0 +1,105 @@
+"""C-ABI library checks that need no GPU: it loads, exports exactly what include/kolibri_b200.h
+declares, and rejects bad arguments on the host before any CUDA call.  Also checks that the
+reference-named Python entry points keep the reference's signatures."""
+from __future__ import annotations
+
+import inspect
+import re
+import subprocess
+
+import pytest
+
+from conftest import REPO
+from kolibri_b200 import _lib
+
+HEADER = REPO / "include" / "kolibri_b200.h"
+
+
+def header_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^KB_API[^(]*?\b(kb_\w+)\s*\(", text, flags=re.M))
+
+
+def test_library_built_and_loads():
+    assert _lib.LIB_PATH.exists(), "run __graft_entry__.build() first"
+    lib = _lib.load()
+    assert lib.kb_version() == 10000
+
+
+def test_exports_match_header():
+    declared = header_symbols()
+    assert declared == set(_lib.SIGNATURES), "ctypes signatures and header disagree"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    assert declared <= exported, f"missing exports: {declared - exported}"
+    assert {s for s in exported if s.startswith("kb_")} == declared
+
+
+def test_status_strings():
+    lib = _lib.load()
+    for code in (_lib.KB_OK, _lib.KB_ERR_INVALID_ARG, _lib.KB_ERR_UNSUPPORTED,
+                 _lib.KB_ERR_ALIGNMENT, _lib.KB_ERR_WORKSPACE, _lib.KB_ERR_TOO_LARGE):
+        assert lib.kb_status_str(code)
+    with pytest.raises(_lib.KolibriError):
+        _lib.check(_lib.KB_ERR_UNSUPPORTED, "x")
+
+
+def test_host_validation_without_gpu():
+    lib = _lib.load()
+    # Each call is rejected by argument checks before touching CUDA.
+    assert lib.kb_router(None, None, None, None, _lib.KB_F32, -1, 384, 6, 0, None) == _lib.KB_ERR_INVALID_ARG
+    assert lib.kb_router(None, None, None, None, _lib.KB_F32, 4, 384, 40, 0, None) == _lib.KB_ERR_UNSUPPORTED
+    assert lib.kb_router(None, None, None, None, _lib.KB_F32, 4, 600, 6, 0, None) == _lib.KB_ERR_UNSUPPORTED
+    assert lib.kb_router(None, None, None, None, _lib.KB_F32, 4, 4, 6, 0, None) == _lib.KB_ERR_UNSUPPORTED
+    assert lib.kb_router(None, None, None, None, _lib.KB_F32, 4, 384, 6, 0, None) == _lib.KB_ERR_INVALID_ARG
+    assert lib.kb_router(None, None, None, None, _lib.KB_F32, 1 << 29, 384, 6, 0, None) == _lib.KB_ERR_TOO_LARGE
+    assert lib.kb_expert_maps(None, None, None, None, None, None, 0, 4, 384, 6, 9, None) == _lib.KB_ERR_INVALID_ARG
+    assert lib.kb_expand_rows(None, None, None, 4, -1, 16, None) == _lib.KB_ERR_INVALID_ARG
+    assert lib.kb_qk_norm_rope(None, None, None, None, None, None, None, None, 1, 64, 8, 96, 0, 0,
+                               1e-6, None) == _lib.KB_ERR_UNSUPPORTED
+    assert lib.kb_residual_norm_pair(None, None, None, None, None, None, 1, 64, 1e-6, 7, None) == _lib.KB_ERR_UNSUPPORTED
+    assert lib.kb_add_rms_norm(None, None, None, None, None, 1, 0, 1e-6, 0, None) == _lib.KB_ERR_INVALID_ARG
+
+
+def test_workspace_sizes():
+    lib = _lib.load()
+    assert lib.kb_expert_maps_workspace_bytes(0, 384, 6) == 0
+    prev = 0
+    for T in (1, 64, 4096, 65536, 262144):
+        ws = lib.kb_router_maps_workspace_bytes(T, 384, 6)
+        assert ws >= prev
+        prev = ws
+    assert lib.kb_expert_maps_workspace_bytes(65536, 384, 6) > 0
+
+
+def test_reference_signatures(api):
+    def params(f):
+        return [(n, p.default) for n, p in inspect.signature(f).parameters.items()]
+
+    # kernels/triton/fused_kolibri_router.py:98-104
+    assert params(api.fused_kolibri_router) == [
+        ("x", inspect.Parameter.empty), ("bias", None), ("k", 6), ("norm_topk_prob", False),
+        ("output_dtype", None)]
+    assert list(inspect.signature(api.fused_sandwich_norm).parameters) == [
+        "attn_out", "residual_in", "gamma1", "gamma2", "eps"]
+    assert inspect.signature(api.fused_sandwich_norm).parameters["eps"].default == 1e-5
+    assert list(inspect.signature(api.fused_add_post_moe_norm).parameters) == [
+        "routed_out", "shared_out", "gamma", "eps"]
+    assert list(inspect.signature(api.kolibri_dispatch_map).parameters) == [
+        "token_selected_experts", "num_experts", "force_single_block", "force_multi_block"]
+    assert list(inspect.signature(api.fused_moe_prologue).parameters)[:3] == [
+        "unpermuted_input", "router_logits", "router_bias"]
+    assert list(inspect.signature(api.kolibri_router).parameters)[:2] == ["scores", "bias"]
+    assert list(inspect.signature(api.kolibri_multi_block_build_expert_maps).parameters) == [
+        "token_selected_experts", "num_experts", "max_blocks", "return_inverse_map"]
+    for name in ("forward", "forward_vA", "forward_vB", "forward_vFloat4"):
+        assert list(inspect.signature(getattr(api.kolibri_cuda_ops, name)).parameters) == [
+            "logits", "bias", "topk"]
+
+
+def test_product_never_imports_oracle():
+    pkg = REPO / "profiling-moe_b200"
+    for p in pkg.rglob("*.py"):
+        src = p.read_text()
+        assert not re.search(r"^\s*(from|import)\s+oracle\b", src, re.M), p

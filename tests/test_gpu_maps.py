@@ -1,0 +1,155 @@
+"""Expert maps, fused router+maps, activation expansion and the prologue API on the GPU:
+bit-exact against the CPU oracle (counts, offsets, p2u, u2p; (expert, token, slot) order)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from kb_testutil import np_of
+from kolibri_b200 import ops
+from kolibri_b200 import workloads as wl
+from oracle import kolibri_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+MODES = [ops.KB_MAPS_AUTO, ops.KB_MAPS_SINGLE_CTA, ops.KB_MAPS_MULTI_CTA]
+
+
+def check_maps(ids_cpu, got, E=384):
+    c, off, p2u, u2p = got
+    rc, roff, rp2u, ru2p = orc.expert_maps_ref(ids_cpu, E)
+    if c is not None:
+        np.testing.assert_array_equal(np_of(c), rc)
+    np.testing.assert_array_equal(np_of(off), roff)
+    np.testing.assert_array_equal(np_of(p2u), rp2u)
+    if u2p is not None:
+        np.testing.assert_array_equal(np_of(u2p), ru2p)
+
+
+def ids_config1(T):
+    logits, bias = wl.router_inputs(T, seed=1)
+    return orc.router_ref(logits, bias)[0]
+
+
+@pytest.mark.parametrize("T", [1, 64, 4096, 65536])
+@pytest.mark.parametrize("mode", MODES)
+def test_maps_config1(T, mode):
+    ids = ids_config1(T)
+    if mode == ops.KB_MAPS_SINGLE_CTA and T * 6 > 12288:
+        with pytest.raises(Exception):
+            ops.expert_maps(ids.cuda(), 384, mode=mode)
+        return
+    check_maps(ids, ops.expert_maps(ids.cuda(), 384, mode=mode))
+
+
+@pytest.mark.parametrize("T", [1, 64, 4096])
+def test_maps_golden_offsets(T):
+    g = np.load(GOLDEN / f"maps_c1_T{T}.npz")
+    ids = torch.from_numpy(g["ids"]).cuda()
+    _, off, p2u, _ = ops.expert_maps(ids, 384)
+    np.testing.assert_array_equal(np_of(off), g["offsets"])
+    o = g["offsets"]
+    ref = g["p2u_expert_slot_token"]
+    got = np_of(p2u)
+    for e in range(384):
+        assert set(got[o[e]:o[e + 1]].tolist()) == set(ref[o[e]:o[e + 1]].tolist())
+
+
+@pytest.mark.parametrize("T", [16, 64, 512, 1152, 98304])
+def test_maps_reference_invariant_sizes(T):
+    torch.manual_seed(42)
+    ids = torch.randint(0, 384, (T, 6), dtype=torch.int32)
+    for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA):
+        check_maps(ids, ops.expert_maps(ids.cuda(), 384, mode=mode))
+
+
+def test_maps_edge_cases():
+    one = torch.full((5000, 6), 7, dtype=torch.int32)
+    for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA):
+        check_maps(one, ops.expert_maps(one.cuda(), 384, mode=mode))
+    bad = torch.from_numpy(np.random.default_rng(0).integers(-3, 390, size=(700, 6)).astype(np.int32))
+    for mode in MODES:
+        check_maps(bad, ops.expert_maps(bad.cuda(), 384, mode=mode))
+    empty = torch.zeros((0, 6), dtype=torch.int32)
+    c, off, p2u, u2p = ops.expert_maps(empty.cuda(), 384)
+    assert np.all(np_of(off) == 0) and np.all(np_of(c) == 0) and p2u.numel() == 0
+    # other E and k
+    g = torch.Generator().manual_seed(1)
+    for E, k in ((256, 6), (512, 8), (100, 3), (384, 1), (384, 32)):
+        ids = torch.randint(0, E, (999, k), generator=g, dtype=torch.int32)
+        for mode in MODES:
+            check_maps(ids, ops.expert_maps(ids.cuda(), E, mode=mode), E)
+
+
+def test_maps_repeated_calls_reuse_workspace():
+    # The arrival counters must reset themselves: alternate sizes many times.
+    for i in range(6):
+        T = (70000, 3000, 513)[i % 3]
+        ids = torch.randint(0, 384, (T, 6), dtype=torch.int32)
+        check_maps(ids, ops.expert_maps(ids.cuda(), 384, mode=ops.KB_MAPS_MULTI_CTA))
+
+
+@pytest.mark.parametrize("T", [1, 32, 33, 256, 4096, 65536])
+@pytest.mark.parametrize("mode", MODES)
+def test_router_maps_fused(T, mode):
+    logits, bias = wl.router_inputs(T, seed=1)
+    if mode == ops.KB_MAPS_SINGLE_CTA and T * 6 > 12288:
+        return
+    for renorm in (False, True):
+        ids, w, c, off, p2u, u2p = ops.router_maps(logits.cuda(), bias.cuda(), renorm=renorm,
+                                                   mode=mode)
+        rid, rw = orc.router_ref(logits, bias, renorm=renorm)
+        assert torch.equal(ids.cpu(), rid)
+        torch.testing.assert_close(w.cpu(), rw, rtol=1e-6, atol=0)
+        check_maps(rid, (c, off, p2u, u2p))
+
+
+def test_expansion_and_prologue(api):
+    T, H = 300, 6144
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    logits, bias = wl.router_inputs(T, seed=12)
+    xc = x.cuda()
+    out = api.fused_moe_prologue(xc, logits.cuda(), bias.cuda())
+    permuted, w, ids, off, p2u, u2p = out
+    rid, rw = orc.router_ref(logits, bias)
+    assert torch.equal(ids.cpu(), rid)
+    torch.testing.assert_close(w.cpu(), rw, rtol=1e-6, atol=0)
+    rc, roff, rp2u, ru2p = orc.expert_maps_ref(rid, 384)
+    np.testing.assert_array_equal(np_of(off), roff)
+    np.testing.assert_array_equal(np_of(p2u), rp2u)
+    np.testing.assert_array_equal(np_of(u2p), ru2p)
+    assert torch.equal(permuted.cpu(), orc.expansion_ref(x, rp2u))
+    # reference prologue invariants A-D (fusions/03_moe_prologue/benchmark_and_verify.py:66-86)
+    _, wn, *_ = api.fused_moe_prologue(xc, logits.cuda(), bias.cuda(), norm_topk_prob=True)
+    assert (wn.sum(-1) - 1).abs().max().item() < 1e-4
+    # stand-alone expansion on other dtypes / row sizes
+    for dt, h in ((torch.float16, 2560), (torch.bfloat16, 6144), (torch.float32, 7)):
+        xx = torch.randn(50, h, generator=g).to(dt)
+        pp = torch.from_numpy(orc.expert_maps_ref(torch.randint(0, 384, (50, 6), generator=g), 384)[2])
+        got = ops.expand_rows(xx.cuda(), pp.cuda())
+        assert torch.equal(got.cpu(), orc.expansion_ref(xx, pp.numpy()))
+
+
+def test_reference_map_entry_points(api):
+    ids = torch.randint(0, 384, (1152, 6), dtype=torch.int32)
+    rc, roff, rp2u, ru2p = orc.expert_maps_ref(ids, 384)
+    idc = ids.cuda()
+    for fn in (lambda: api.kolibri_build_expert_maps(idc, 384),
+               lambda: api.trtllm_build_expert_maps_b32(idc, 384),
+               lambda: api.kolibri_multi_block_build_expert_maps(idc, 384, max_blocks=128),
+               lambda: api.kolibri_multi_block_build_expert_maps(idc, 384, max_blocks=-64),
+               lambda: api.kolibri_dispatch_map(idc, 384),
+               lambda: api.kolibri_dispatch_map(idc, 384, force_multi_block=True)):
+        p2u, u2p, off = fn()
+        assert off.dtype == torch.int64 and off.numel() == 385
+        np.testing.assert_array_equal(np_of(off), roff)
+        np.testing.assert_array_equal(np_of(p2u), rp2u)
+        np.testing.assert_array_equal(np_of(u2p), ru2p)
+    p2u, u2p, off = api.kolibri_multi_block_build_expert_maps(idc, 384, return_inverse_map=False)
+    assert u2p.numel() == 0
+    small = ids[:40].contiguous()
+    p2u, u2p, off = api.kolibri_dispatch_map(small.cuda(), 384, force_single_block=True)
+    np.testing.assert_array_equal(np_of(p2u), orc.expert_maps_ref(small, 384)[2])
