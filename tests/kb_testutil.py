@@ -23,3 +23,25 @@ def bf16_ulp_diff(out: torch.Tensor, ref: torch.Tensor) -> int:
 
 def np_of(t):
     return t.detach().cpu().numpy() if isinstance(t, torch.Tensor) else np.asarray(t)
+
+
+def bf16_ulp(x: torch.Tensor) -> torch.Tensor:
+    """Spacing of bf16 numbers at |x| (8 significant bits)."""
+    a = x.detach().float().cpu().abs().clamp_min(2.0 ** -126)
+    return torch.pow(2.0, torch.floor(torch.log2(a)) - 7)
+
+
+def assert_chain_close(out: torch.Tensor, ref: torch.Tensor, inter: torch.Tensor,
+                       what: str = "") -> None:
+    """Bar for outputs computed through a rounded bf16 intermediate (h = res + bf16(norm(a))):
+    within 1 bf16 ulp / atol 1e-2 of the oracle, plus one ulp of the oracle's intermediate.
+    A 1-fp32-ulp difference in the rsqrt factor can move the intermediate by one bf16 ulp,
+    which survives the residual add when it cancels."""
+    o = out.detach().float().cpu()
+    r = ref.detach().float().cpu()
+    allow = 1e-2 + 2.0 ** -7 * r.abs() + bf16_ulp(inter)
+    d = (o - r).abs()
+    bad = d > allow
+    assert not bool(bad.any()), (
+        f"{what}: {int(bad.sum())} of {d.numel()} elements outside the bar; "
+        f"worst {float((d - allow).max()):.3g} over at {tuple(torch.nonzero(bad)[0].tolist())}")

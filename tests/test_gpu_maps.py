@@ -80,6 +80,8 @@ def test_maps_edge_cases():
     for E, k in ((256, 6), (512, 8), (100, 3), (384, 1), (384, 32)):
         ids = torch.randint(0, E, (999, k), generator=g, dtype=torch.int32)
         for mode in MODES:
+            if mode == ops.KB_MAPS_SINGLE_CTA and ids.numel() > 12288:
+                continue  # the single-CTA path holds at most 12288 selections
             check_maps(ids, ops.expert_maps(ids.cuda(), E, mode=mode), E)
 
 
