@@ -243,7 +243,13 @@ def main():
                 step(i)
             graphs.append(g)
     run = (lambda i: graphs[i % nsets].replay()) if graphs else step
-    launches_per_step = 2 if lib.kb_router_maps_workspace_bytes(T, E, K) else 1
+    import ctypes
+    path_c, launch_c, grid_c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _lib.check(lib.kb_maps_describe(T, E, K, 1, _lib.KB_MAPS_AUTO, ctypes.byref(path_c),
+                                    ctypes.byref(launch_c), ctypes.byref(grid_c)),
+               "kb_maps_describe")
+    launches_per_step = launch_c.value
+    path_name = {1: "single-CTA", 2: "persistent cooperative", 3: "two-kernel"}[path_c.value]
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -345,7 +351,7 @@ def main():
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "algorithmic_bytes": alg_bytes, "peak_source": peak_kind,
-                     "kernel": "kb_router_maps (router+histogram, scan+scatter)"},
+                     "kernel": f"kb_router_maps ({path_name}, grid {grid_c.value})"},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,

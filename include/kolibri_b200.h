@@ -47,7 +47,12 @@ enum {
 enum { KB_BF16 = 0, KB_F16 = 1, KB_F32 = 2 };
 
 /* Expert-map algorithm selection (`mode` argument). */
-enum { KB_MAPS_AUTO = 0, KB_MAPS_SINGLE_CTA = 1, KB_MAPS_MULTI_CTA = 2 };
+enum {
+    KB_MAPS_AUTO = 0,        /* single CTA at small T, persistent multi-CTA kernel above   */
+    KB_MAPS_SINGLE_CTA = 1,  /* one CTA, everything in shared memory (T*K <= 12288)         */
+    KB_MAPS_MULTI_CTA = 2,   /* persistent cooperative kernel (two-kernel path if it cannot hold T) */
+    KB_MAPS_TWO_KERNEL = 3   /* tile histograms + per-super-tile scatter, two launches      */
+};
 
 KB_API const char *kb_status_str(int status);
 KB_API int kb_version(void);
@@ -102,6 +107,13 @@ KB_API int kb_router_maps(const float *logits, const float *bias, int32_t *ids, 
                    void *workspace, size_t workspace_bytes, int64_t T, int E, int K,
                    int renorm, int mode, kb_stream_t stream);
 
+/* The path kb_expert_maps (route = 0) or kb_router_maps (route = 1) takes for this shape:
+ * *path = KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA (persistent kernel) or KB_MAPS_TWO_KERNEL,
+ * *launches = kernel launches per call, *grid = CTAs of the (first) launch.  Any output
+ * pointer may be NULL.  Library introspection; no counterpart in the reference. */
+KB_API int kb_maps_describe(int64_t T, int E, int K, int route, int mode, int *path,
+                            int *launches, int *grid);
+
 /* ---------------------------------------------------------------------------------
  * Activation expansion: out[r] = x[p2u[r] % T] for r in [0, rows); a row whose p2u
  * is negative or >= rows_total_unpermuted is left untouched.  row_bytes is the row
@@ -119,7 +131,7 @@ KB_API int kb_expand_rows(const void *x, void *out, const int32_t *p2u, int64_t 
  *   out = [y1*cos(a) - y2*sin(a), y2*cos(a) + y1*sin(a)]  -> bf16 (one rounding)
  * pos == NULL selects the RNoPE layers' identity rotation (pure per-head RMSNorm).
  * q: [T, Hq, D] with token stride q_tok_stride elements (>= Hq*D), same for k.
- * q_out/k_out may equal q_in/k_in (in place).  D = 128 (D % 8 == 0, D <= 256).
+ * q_out/k_out may equal q_in/k_in (in place).  D is 64, 128 or 256.
  * inv_freq fp32 [D/2] on the device = 1/theta^(2j/D), computed by the caller.
  * Replaces: TensorRT-LLM fusedQKNormRopeKernel as driven by Kolibri1Attention.apply_rope
  * (benchmarks/02_benchmark_attention_norm.py:105-112); formula of

@@ -11,28 +11,45 @@
 //           with the (expert, token, slot) order of the CUB rank kernel
 //           kernels/cuda/customKolibriBuildExpertMapsKernel.cu:96-156 instead of atomic order.
 //
-// Design (B200): one warp per token with the 384 logits register-resident (3 x float4 per
-// lane).  A lane-local top-3 plus K warp-wide redux.sync rounds picks the top-K; ties, NaN
-// rows and lanes holding more than three winners fall back to an exact key-based path.
-// Maps: per-tile smem histograms; the last CTA of each super-tile (arrival counter, no spin)
-// folds its tiles into one row; a second kernel (one CTA per super-tile) scans the super-tile
-// rows and ranks selections stably with __match_any_sync in input order.
+// Design (B200):
+//  * Router: one warp per token, the row of E logits spread over the lanes as float4s.  Rows
+//    stream through a per-warp cp.async double buffer in shared memory, so the next row is
+//    in flight while the current one is ranked and the raw logit of a pick is a shared-memory
+//    read.  Ranking: lane-local top-3 (min/max network), then K warp rounds of redux.sync over
+//    the lanes' current candidates; a row with a NaN, a tie between lanes, or a lane holding
+//    more than three picks is re-ranked by an exact key-based path.  Both give the same answer.
+//  * Maps at large T: one persistent cooperative kernel.  Phase 1 routes (or loads ids) and
+//    builds a per-CTA histogram; phase 2 scans each expert's column of CTA histograms; phase 3
+//    ranks the CTA's selections stably with __match_any_sync in input order and scatters.
+//    Phases are separated by a grid barrier whose wait is bounded (on timeout the kernel sets
+//    an error flag in the workspace and returns; later calls then poison the offsets).
+//  * Small T: one CTA does everything in shared memory.  A two-kernel variant (tile
+//    histograms, last-arriving CTA folds super-tiles, one CTA per super-tile scatters) remains
+//    as the path for shapes the persistent kernel cannot hold.
 #include "kb_common.cuh"
 
 #include <algorithm>
 #include <math.h>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 namespace kb {
 
 // ------------------------------------------------------------------------------------
-// Ordering key: a larger float gives a larger key, NaN gives the largest key (torch.sort
-// puts NaN first in a descending sort), -0 and +0 share a key.  Key 0 marks "taken".
+// Ordering keys.  okey: a larger float gives a larger key, NaN the largest (torch.sort puts
+// NaN first in a descending sort), -0 and +0 share a key; key 0 marks "taken".
+// fkey: the same map for values known to be neither NaN nor -0.
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t okey(float s) {
     uint32_t u = __float_as_uint(s);
     if (u == 0x80000000u) u = 0u;
     uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return (s != s) ? 0xffffffffu : k;
+}
+__device__ __forceinline__ uint32_t fkey(float s) {
+    const uint32_t u = __float_as_uint(s);
+    return u ^ ((uint32_t)((int32_t)u >> 31) | 0x80000000u);
 }
 
 __device__ __forceinline__ float fmax_nan(float a, float b) {
@@ -66,7 +83,7 @@ __device__ __forceinline__ void load_row(const float* __restrict__ row, int E, i
     }
 }
 
-// Bias registers; b + 0.0f turns a -0 bias into +0 so that no score is ever -0.
+// Bias registers; b + 0.0f turns a -0 bias into +0, so that no score x + b is ever -0.
 template <int VPL, bool VEC>
 __device__ __forceinline__ void load_bias(const float* __restrict__ bias, int E, int lane,
                                           float (&b)[VPL]) {
@@ -81,13 +98,19 @@ __device__ __forceinline__ void load_bias(const float* __restrict__ bias, int E,
 }
 
 // Exact top-K: K rounds of (lane argmax over keys, warp max, lowest index among equal keys).
-// Writes sel[r] (r < K) = expert id of the r-th pick.
+// Reads the row again from `row` (shared or global memory) and the bias from `bias` (or
+// zero), so no register array crosses the call.  Writes sel[r] (r < K) = r-th pick.
 template <int VPL, bool VEC>
-__device__ __noinline__ void route_exact(const float (&s)[VPL], int E, int K, int lane,
-                                         int* sel) {
+__device__ __noinline__ void route_exact(const float* row, const float* __restrict__ bias, int E,
+                                         int K, int lane, int* sel) {
     uint32_t key[VPL];
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) key[j] = (expert_of<VEC>(lane, j) < E) ? okey(s[j]) : 0u;
+    for (int j = 0; j < VPL; ++j) {
+        const int e = expert_of<VEC>(lane, j);
+        float v = 0.0f;
+        if (e < E) v = row[e] + (bias ? bias[e] + 0.0f : 0.0f);
+        key[j] = (e < E) ? okey(v) : 0u;
+    }
     for (int r = 0; r < K; ++r) {
         uint32_t best = 0u;
         int bj = 0;
@@ -108,12 +131,16 @@ __device__ __noinline__ void route_exact(const float (&s)[VPL], int E, int K, in
     __syncwarp();
 }
 
-// Fast top-K (VEC layout, K <= 8): lane-local top-3 by value (min/max network), then K warp
-// rounds over the lanes' current candidates.  Returns false (nothing written) when the row
-// holds a NaN, when two lanes offer equal values in a round, or when a lane would need its
-// fourth value; the caller then runs route_exact.  Both paths produce the same result.
-template <int VPL>
-__device__ __forceinline__ bool route_fast(const float (&s)[VPL], int K, int lane, int* sel) {
+// Fast top-K (VEC layout, K <= 8; KT = K at compile time, or 0 for a runtime K).  Lane-local
+// top-3 values by a min/max network, then K warp rounds: the lane holding the largest
+// current candidate consumes it and offers its next one.  Each lane only records which rounds
+// it won; the register positions of its picks are recovered once at the end.  Returns false
+// (nothing written) if the row holds a NaN, two lanes offered equal values in a round, or a
+// lane ran out of its three values before the last round -- route_exact then decides.
+template <int VPL, int KT>
+__device__ __forceinline__ bool route_fast(const float (&s)[VPL], int K_rt, int lane, int* sel) {
+    const int K = KT ? KT : K_rt;
+    constexpr int KMAX = KT ? KT : 8;
     float b1 = s[0], b2 = -INFINITY, b3 = -INFINITY;
 #pragma unroll
     for (int j = 1; j < VPL; ++j) {
@@ -125,73 +152,60 @@ __device__ __forceinline__ bool route_fast(const float (&s)[VPL], int K, int lan
         b3 = fmaxf(b3, t2);
     }
     if (__any_sync(FULL_MASK, b1 != b1)) return false;
-    const uint32_t k1 = okey(b1), k2 = okey(b2), k3 = okey(b3);
-    uint32_t cur = k1;
-    int c = 0, r0 = 0, r1 = 0, r2 = 0;
-    bool exhausted_early = false;
+    uint32_t cur = fkey(b1), nx2 = fkey(b2), nx3 = fkey(b3);
+    unsigned won = 0u, clash = 0u;
+    bool exhausted = false;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-        if (r >= K) break;
-        const uint32_t wmax = __reduce_max_sync(FULL_MASK, cur);
-        const bool eq = (cur == wmax);
-        const unsigned m = __ballot_sync(FULL_MASK, eq);
-        if (m & (m - 1u)) return false;  // two lanes offer the same value
-        if (eq) {
-            if (c == 0) { r0 = r; cur = k2; }
-            else if (c == 1) { r1 = r; cur = k3; }
-            else { r2 = r; cur = 0u; exhausted_early = (r + 1 < K); }
-            ++c;
+    for (int r = 0; r < KMAX; ++r) {
+        if (KT || r < K) {
+            if (KT ? (r == KT - 1) : (r == K - 1)) exhausted = __any_sync(FULL_MASK, cur == 0u);
+            const uint32_t wmax = __reduce_max_sync(FULL_MASK, cur);
+            const bool eq = (cur == wmax);
+            const unsigned m = __ballot_sync(FULL_MASK, eq);
+            clash |= m & (m - 1u);
+            if (eq) {
+                won |= 1u << r;
+                cur = nx2;
+                nx2 = nx3;
+                nx3 = 0u;
+            }
         }
     }
-    if (__any_sync(FULL_MASK, exhausted_early)) return false;
-    // Register positions of the taken values: the first occurrence of b1, the first other
-    // occurrence of b2, then of b3 (equal values inside a lane keep index order).
+    if (clash != 0u || exhausted) return false;
+    const int nwon = __popc(won);
     int i1 = 0, i2 = 0, i3 = 0;
 #pragma unroll
     for (int j = VPL - 1; j >= 0; --j)
         if (s[j] == b1) i1 = j;
-    if (__any_sync(FULL_MASK, c >= 2)) {
+    if (__any_sync(FULL_MASK, nwon >= 2)) {
 #pragma unroll
         for (int j = VPL - 1; j >= 0; --j)
             if (s[j] == b2 && j != i1) i2 = j;
-        if (__any_sync(FULL_MASK, c >= 3)) {
+        if (__any_sync(FULL_MASK, nwon >= 3)) {
 #pragma unroll
             for (int j = VPL - 1; j >= 0; --j)
                 if (s[j] == b3 && j != i1 && j != i2) i3 = j;
         }
     }
-    if (c >= 1) sel[r0] = expert_of<true>(lane, i1);
-    if (c >= 2) sel[r1] = expert_of<true>(lane, i2);
-    if (c >= 3) sel[r2] = expert_of<true>(lane, i3);
+    if (won) {
+        unsigned wv = won;
+        sel[__ffs(wv) - 1] = expert_of<true>(lane, i1);
+        wv &= wv - 1u;
+        if (wv) {
+            sel[__ffs(wv) - 1] = expert_of<true>(lane, i2);
+            wv &= wv - 1u;
+            if (wv) sel[__ffs(wv) - 1] = expert_of<true>(lane, i3);
+        }
+    }
     __syncwarp();
     return true;
 }
 
-// Route one token: sel[0..K) <- expert ids, best first.
-template <int VPL, bool VEC>
-__device__ __forceinline__ void route_token(const float* __restrict__ row, const float (&b)[VPL],
-                                            int E, int K, int lane, int* sel) {
-    float s[VPL];
-    {
-        float x[VPL];
-        load_row<VPL, VEC>(row, E, lane, x);
-#pragma unroll
-        for (int j = 0; j < VPL; ++j) s[j] = x[j] + b[j];
-    }
-    bool done = false;
-    if constexpr (VEC) {
-        if (K <= 8) done = route_fast<VPL>(s, K, lane, sel);
-    }
-    if (!done) route_exact<VPL, VEC>(s, E, K, lane, sel);
-}
-
 __device__ __forceinline__ float sigmoid_acc(float x) { return 1.0f / (1.0f + expf(-x)); }
 
-// Lane r < K: weight of the r-th pick from the raw (un-biased) logit; optional renorm.
-__device__ __forceinline__ float pick_weight(const float* __restrict__ row, int id, int K,
-                                             int lane, int renorm) {
-    float w = 0.0f;
-    if (lane < K) w = sigmoid_acc(row[id]);
+// Lane r < K holds pick r: weight = sigmoid(raw logit); optional renorm over the K picks.
+__device__ __forceinline__ float pick_weight(float x, int K, int lane, int renorm) {
+    float w = (lane < K) ? sigmoid_acc(x) : 0.0f;
     if (renorm) {
         const float sum = warp_sum(w);
         w = w * (1.0f / (sum + 1e-20f));
@@ -199,13 +213,106 @@ __device__ __forceinline__ float pick_weight(const float* __restrict__ row, int 
     return w;
 }
 
-template <typename WT>
-__device__ __forceinline__ void store_w(WT* p, float v) { *p = Elem<WT>::from_f(v); }
+// Where the picks of a token go.  Lanes < K hold pick `lane`.  MAPS additionally appends
+// the id to this CTA's shared-memory selection list and histogram.
+template <typename WT, bool SEL, bool HIST>
+struct RouteSink {
+    int32_t* ids;    // global [T, K]
+    WT* w;           // global [T, K]
+    int* sel;        // shared memory, selections of tokens sel_t0.. (SEL)
+    int64_t sel_t0;
+    int* hist;       // shared memory histogram (HIST)
+    __device__ __forceinline__ void put(int64_t t, int K, int lane, int id, float wv) const {
+        if (lane < K) {
+            const int64_t o = t * K + lane;
+            ids[o] = id;
+            w[o] = Elem<WT>::from_f(wv);
+            if constexpr (SEL) sel[(int)(t - sel_t0) * K + lane] = id;
+            if constexpr (HIST) atomicAdd(&hist[id], 1);
+        }
+    }
+};
 
 // ------------------------------------------------------------------------------------
-// kb_router kernel: 8 warps per CTA, one token per warp per iteration.
+// cp.async helpers (16-byte global -> shared copies, L1 bypass)
 // ------------------------------------------------------------------------------------
-template <int VPL, bool VEC, typename WT>
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+#include "trouter.cuh"
+
+// ------------------------------------------------------------------------------------
+// Warp router loop over tokens t_begin, t_begin+t_step, ... < t_end.
+// VEC: rows stream through ring[2][E] (this warp's shared-memory double buffer); the next
+// row's copy is issued before the current row is ranked.  sel: a 32-int scratch per warp.
+// ------------------------------------------------------------------------------------
+template <int VPL, bool VEC, int KT, typename Sink>
+__device__ __forceinline__ void route_tokens(const float* __restrict__ logits,
+                                             const float* __restrict__ bias,
+                                             const float (&b)[VPL], int E, int K, int renorm,
+                                             int64_t t_begin, int64_t t_end, int64_t t_step,
+                                             float* ring, int* sel, const Sink& sink) {
+    const int lane = threadIdx.x & 31;
+    if constexpr (VEC) {
+        const float* src = logits + t_begin * E + 4 * lane;
+        const int64_t src_step = t_step * E;
+        float* dst0 = ring + 4 * lane;
+        if (t_begin < t_end) {
+#pragma unroll
+            for (int q = 0; q < VPL / 4; ++q) cp_async16(dst0 + 128 * q, src + 128 * q);
+        }
+        cp_async_commit();
+        int slot = 0;
+        for (int64_t t = t_begin; t < t_end; t += t_step, slot ^= 1) {
+            src += src_step;
+            if (t + t_step < t_end) {
+                float* dst = dst0 + (slot ^ 1) * E;
+#pragma unroll
+                for (int q = 0; q < VPL / 4; ++q) cp_async16(dst + 128 * q, src + 128 * q);
+            }
+            cp_async_commit();
+            cp_async_wait<1>();
+            __syncwarp();
+            const float* rb = ring + slot * E;
+            float s[VPL];
+#pragma unroll
+            for (int q = 0; q < VPL / 4; ++q) {
+                const float4 v = reinterpret_cast<const float4*>(rb)[lane + 32 * q];
+                s[4 * q + 0] = v.x + b[4 * q + 0];
+                s[4 * q + 1] = v.y + b[4 * q + 1];
+                s[4 * q + 2] = v.z + b[4 * q + 2];
+                s[4 * q + 3] = v.w + b[4 * q + 3];
+            }
+            bool done = false;
+            if (KT || K <= 8) done = route_fast<VPL, KT>(s, K, lane, sel);
+            if (!done) route_exact<VPL, true>(rb, bias, E, K, lane, sel);
+            const int id = (lane < K) ? sel[lane] : 0;
+            const float wv = pick_weight((lane < K) ? rb[id] : 0.0f, K, lane, renorm);
+            sink.put(t, K, lane, id, wv);
+            __syncwarp();
+        }
+        cp_async_wait<0>();
+    } else {
+        for (int64_t t = t_begin; t < t_end; t += t_step) {
+            const float* row = logits + t * E;
+            route_exact<VPL, false>(row, bias, E, K, lane, sel);
+            const int id = (lane < K) ? sel[lane] : 0;
+            const float wv = pick_weight((lane < K) ? __ldg(row + id) : 0.0f, K, lane, renorm);
+            sink.put(t, K, lane, id, wv);
+            __syncwarp();
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// kb_router kernel: 8 warps per CTA, grid-stride over tokens, one token per warp at a time.
+// ------------------------------------------------------------------------------------
+template <int VPL, bool VEC, int KT, typename WT>
 __global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ logits,
                                                      const float* __restrict__ bias,
                                                      int32_t* __restrict__ ids,
@@ -213,30 +320,24 @@ __global__ void __launch_bounds__(256) router_kernel(const float* __restrict__ l
                                                      int K, int renorm) {
     pdl_wait();
     pdl_launch();
+    extern __shared__ __align__(16) float rsmem[];
     __shared__ int sel_sm[8][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int* sel = sel_sm[warp];
     float b[VPL];
     load_bias<VPL, VEC>(bias, E, lane, b);
-    for (int64_t t = (int64_t)blockIdx.x * 8 + warp; t < T; t += (int64_t)gridDim.x * 8) {
-        const float* row = logits + t * E;
-        route_token<VPL, VEC>(row, b, E, K, lane, sel);
-        const int id = (lane < K) ? sel[lane] : 0;
-        const float wv = pick_weight(row, id, K, lane, renorm);
-        if (lane < K) {
-            ids[t * K + lane] = id;
-            store_w(w + t * K + lane, wv);
-        }
-        __syncwarp();
-    }
+    float* ring = VEC ? rsmem + (size_t)warp * 2 * E : nullptr;
+    const int64_t first = (int64_t)blockIdx.x * 8 + warp;
+    const int64_t step = (int64_t)gridDim.x * 8;
+    const RouteSink<WT, false, false> sink{ids, w, nullptr, 0, nullptr};
+    route_tokens<VPL, VEC, KT>(logits, bias, b, E, K, renorm, first, T, step, ring, sel_sm[warp],
+                               sink);
 }
 
 // ------------------------------------------------------------------------------------
 // Expert-map building blocks (block-wide; blockDim a multiple of 32).
 // ------------------------------------------------------------------------------------
 
-// Phase A: per-warp histograms of the selections sel[0..n) (contiguous warp ranges of
-// 32-wide chunks).  whist: [nwarps][E] in smem, zeroed here.
+// Contiguous range of 32-wide selection chunks handled by this warp.
 __device__ __forceinline__ void warp_ranges(int n, int& c0, int& c1) {
     const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5;
     const int chunks = (n + 31) >> 5;
@@ -245,6 +346,7 @@ __device__ __forceinline__ void warp_ranges(int n, int& c0, int& c1) {
     c1 = min(chunks, c0 + per);
 }
 
+// Per-warp histograms of sel[0..n) over each warp's chunk range.  whist: [nwarps][E].
 __device__ void count_per_warp(const int* sel, int n, int E, int* whist) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* h = whist + warp * E;
@@ -263,8 +365,7 @@ __device__ void count_per_warp(const int* sel, int n, int E, int* whist) {
     }
 }
 
-// Phase B (after __syncthreads): whist[w][e] <- sum_{w'<w} whist[w'][e] (exclusive over
-// warps); tot[e] <- column total.
+// whist[w][e] <- sum_{w'<w} whist[w'][e] (exclusive over warps); tot[e] <- column total.
 __device__ void scan_over_warps(int E, int* whist, int* tot) {
     const int nwarps = blockDim.x >> 5;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -278,38 +379,37 @@ __device__ void scan_over_warps(int E, int* whist, int* tot) {
     }
 }
 
-// Exclusive block scan of tot[0..E) into offs[0..E], offs[E] = sum.  Uses the first
-// ceil(E/32) warps; needs __syncthreads before and after.  scratch: >= 16 ints.
+// Exclusive block scan of tot[0..E) into offs[0..E], offs[E] = sum, for any blockDim (each
+// thread scans a contiguous run of experts).  Needs __syncthreads before and after.
+// scratch: >= 64 ints.
 __device__ void scan_experts(const int* tot, int E, int* offs, int* scratch) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nw = (E + 31) >> 5;
-    int v = 0, incl = 0;
-    if (warp < nw) {
-        const int e = warp * 32 + lane;
-        v = (e < E) ? tot[e] : 0;
-        incl = warp_incl_scan(v, lane);
-        if (lane == 31) scratch[warp] = incl;
-    }
+    const int nthr = blockDim.x, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31, nw = nthr >> 5;
+    const int per = (E + nthr - 1) / nthr;
+    const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
+    int sum = 0;
+    for (int e = e0; e < e1; ++e) sum += tot[e];
+    const int incl = warp_incl_scan(sum, lane);
+    if (lane == 31) scratch[warp] = incl;
     __syncthreads();
     if (warp == 0) {
         int s = (lane < nw) ? scratch[lane] : 0;
         s = warp_incl_scan(s, lane);
-        if (lane < nw) scratch[16 + lane] = s;  // inclusive warp totals
+        if (lane < nw) scratch[32 + lane] = s;  // inclusive warp totals
     }
     __syncthreads();
-    if (warp < nw) {
-        const int e = warp * 32 + lane;
-        const int before = (warp > 0) ? scratch[16 + warp - 1] : 0;
-        if (e < E) offs[e] = before + incl - v;
-        if (e == E - 1) offs[E] = before + incl;
+    int run = incl - sum + ((warp > 0) ? scratch[32 + warp - 1] : 0);
+    for (int e = e0; e < e1; ++e) {
+        offs[e] = run;
+        run += tot[e];
     }
+    if (tid == 0) offs[E] = scratch[32 + nw - 1];
 }
 
-// Phase C: stable ranks and scatter.  whist[w][e] holds the first permuted row of warp
-// w's selections of expert e (base already added).  sel0 = global index of sel[0].
-__device__ void rank_scatter(const int* sel, int n, int64_t sel0, int64_t T, int E, int K,
-                             int* whist, int32_t* __restrict__ p2u,
-                             int32_t* __restrict__ u2p) {
+// Stable ranks and scatter.  whist[w][e] holds the first permuted row of warp w's
+// selections of expert e (base already added).  sel0 = global index of sel[0] = t0*K.
+__device__ void rank_scatter(const int* sel, int n, int64_t t0, int64_t T, int E, int K,
+                             int* whist, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* h = whist + warp * E;
     const unsigned lt = (1u << lane) - 1u;
@@ -326,10 +426,9 @@ __device__ void rank_scatter(const int* sel, int n, int64_t sel0, int64_t T, int
         if (valid && lane == leader) h[e] = base + __popc(peers);
         __syncwarp();
         if (i < n) {
-            const int64_t g = sel0 + i;
-            const int64_t tok = g / K;
-            const int slot = (int)(g - tok * K);
-            const int32_t u = (int32_t)(slot * T + tok);
+            const unsigned tl = (unsigned)i / (unsigned)K;
+            const int slot = i - (int)tl * K;
+            const int32_t u = (int32_t)((int64_t)slot * T + t0 + tl);
             if (valid) {
                 const int rank = base + __popc(peers & lt);
                 p2u[rank] = u;
@@ -353,9 +452,9 @@ __device__ void write_offsets(const int* offs, const int* tot, int E, int64_t ns
 
 // ------------------------------------------------------------------------------------
 // Single-CTA maps (small T): optional routing, then all phases in shared memory.
-// smem: sel[T*K] | whist[32][E] | tot[E] | offs[E+1] | scratch[32]
+// smem: sel[T*K] | whist[32][E] | tot[E] | offs[E+1] | scratch[64] | ring[32][2][E] (VEC route)
 // ------------------------------------------------------------------------------------
-template <int VPL, bool VEC, bool ROUTE>
+template <int VPL, bool VEC, bool ROUTE, int KT>
 __global__ void __launch_bounds__(1024) maps_single_kernel(
     const float* __restrict__ logits, const float* __restrict__ bias,
     const int32_t* __restrict__ ids_in, int32_t* __restrict__ ids_out, float* __restrict__ w,
@@ -363,7 +462,7 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
     int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p) {
     pdl_wait();
     pdl_launch();
-    extern __shared__ int smem[];
+    extern __shared__ __align__(16) int smem[];
     const int n = (int)(T * K);
     const int nwarps = blockDim.x >> 5;
     int* sel = smem;
@@ -371,23 +470,17 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
     int* tot = whist + nwarps * E;
     int* offs = tot + E;
     int* scratch = offs + E + 1;
+    float* ring = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(scratch + 64) + 15) & ~uintptr_t(15));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if constexpr (ROUTE) {
+        __shared__ int sel_sm[32][32];
         float b[VPL];
         load_bias<VPL, VEC>(bias, E, lane, b);
-        __shared__ int sel_sm[32][32];
-        for (int64_t t = warp; t < T; t += nwarps) {
-            const float* row = logits + t * E;
-            route_token<VPL, VEC>(row, b, E, K, lane, sel_sm[warp]);
-            const int id = (lane < K) ? sel_sm[warp][lane] : 0;
-            const float wv = pick_weight(row, id, K, lane, renorm);
-            if (lane < K) {
-                sel[t * K + lane] = id;
-                ids_out[t * K + lane] = id;
-                w[t * K + lane] = wv;
-            }
-            __syncwarp();
-        }
+        const RouteSink<float, true, false> sink{ids_out, w, sel, 0, nullptr};
+        route_tokens<VPL, VEC, KT>(logits, bias, b, E, K, renorm, warp, T, nwarps,
+                                   VEC ? ring + (size_t)warp * 2 * E : nullptr, sel_sm[warp],
+                                   sink);
     } else {
         for (int i = threadIdx.x; i < n; i += blockDim.x) sel[i] = ids_in[i];
     }
@@ -408,9 +501,254 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
 }
 
 // ------------------------------------------------------------------------------------
-// Multi-CTA maps, kernel 1: per-tile histogram (optionally routing the tile first).
-// Tile = TT tokens; super-tile = tiles_per_super consecutive tiles.  The last CTA of a
-// super-tile to arrive sums the super-tile's rows into super_hist and resets the counter.
+// Persistent cooperative maps kernel (large T).
+// ------------------------------------------------------------------------------------
+struct PersistWs {
+    unsigned* bar;   // arrival counter; 0 between calls (the last CTA out resets it)
+    int* err;        // non-zero after a barrier wait gave up; the workspace must be re-zeroed
+    int* colhist;    // [E][grid] per-CTA histograms, expert-major
+    int* colpre;     // [E][grid] exclusive prefix over CTAs
+    int* tot;        // [E]
+};
+
+constexpr int kPW = 8;                    // warps per persistent CTA
+constexpr long long kSpinLimit = 20000000;  // bounded barrier wait (~2 s with nanosleep)
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier over co-resident CTAs (cooperative launch).  Returns false if the wait gave
+// up; the error flag is then set for the host and for later calls.
+__device__ bool grid_barrier(const PersistWs& ws, unsigned target) {
+    __shared__ int ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(ws.bar, 1u);
+        unsigned v = ld_acquire_gpu(ws.bar);
+        long long it = 0;
+        while (v < target && it < kSpinLimit) {
+            __nanosleep(64);
+            v = ld_acquire_gpu(ws.bar);
+            ++it;
+        }
+        if (v < target) atomicExch(ws.err, 1);
+        ok = (v >= target) && (*(volatile int*)ws.err == 0);
+        __threadfence();
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+// Exclusive scan of col[0..n) (n <= 4*blockDim) into pre[]; *total <- sum.
+__device__ void column_scan(const int* col, int* pre, int n, int* total, int* scratch) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nw = blockDim.x >> 5;
+    int v[4];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int idx = threadIdx.x * 4 + i;
+        v[i] = (idx < n) ? __ldcg(col + idx) : 0;
+        sum += v[i];
+    }
+    const int incl = warp_incl_scan(sum, lane);
+    if (lane == 31) scratch[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int s = (lane < nw) ? scratch[lane] : 0;
+        s = warp_incl_scan(s, lane);
+        if (lane < nw) scratch[32 + lane] = s;
+    }
+    __syncthreads();
+    int run = incl - sum + ((warp > 0) ? scratch[32 + warp - 1] : 0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int idx = threadIdx.x * 4 + i;
+        if (idx < n) pre[idx] = run;
+        run += v[i];
+    }
+    if (threadIdx.x == 0) *total = scratch[32 + nw - 1];
+    __syncthreads();
+}
+
+// Phases 2 and 3 of the persistent maps kernels, after this CTA's selections sel[0..n)
+// (tokens t0..) and histogram hist[] are in shared memory.
+__device__ void maps_finish(const PersistWs& ws, int64_t T, int E, int K, int64_t t0, int n,
+                            int* sel, int* hist, int* totsm, int* offs, int* scratch, int* whist,
+                            int32_t* counts, int64_t* offsets, int32_t* p2u, int32_t* u2p) {
+    const int grid = gridDim.x, c = blockIdx.x;
+    const int nwarps = blockDim.x >> 5;
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) ws.colhist[(size_t)e * grid + c] = hist[e];
+    if (!grid_barrier(ws, (unsigned)grid)) return;
+
+    // Phase 2: exclusive scan of each expert's column of CTA histograms.
+    for (int e = c; e < E; e += grid)
+        column_scan(ws.colhist + (size_t)e * grid, ws.colpre + (size_t)e * grid, grid,
+                    ws.tot + e, scratch);
+    if (!grid_barrier(ws, 2u * (unsigned)grid)) return;
+    pdl_launch();
+
+    // Phase 3: global offsets, this CTA's bases, stable ranks, scatter.
+    for (int e = threadIdx.x; e < E; e += blockDim.x) totsm[e] = __ldcg(ws.tot + e);
+    __syncthreads();
+    scan_experts(totsm, E, offs, scratch);
+    __syncthreads();
+    if (c == 0) write_offsets(offs, totsm, E, T * K, counts, offsets, p2u);
+    count_per_warp(sel, n, E, whist);
+    __syncthreads();
+    scan_over_warps(E, whist, hist);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int base = offs[e] + __ldcg(ws.colpre + (size_t)e * grid + c);
+        for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += base;
+    }
+    __syncthreads();
+    rank_scatter(sel, n, t0, T, E, K, whist, p2u, u2p);
+
+    // Last CTA out resets the arrival counter for the next call.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(ws.bar, 1u);
+        if (prev == 3u * (unsigned)grid - 1u) atomicExch(ws.bar, 0u);
+    }
+}
+
+// A workspace whose earlier barrier gave up stays poisoned until re-zeroed: report it
+// through offsets (all -1) and do nothing else.
+__device__ __forceinline__ bool ws_poisoned(const PersistWs& ws, int E, int64_t* offsets) {
+    if (*(volatile int*)ws.err == 0) return false;
+    if (blockIdx.x == 0)
+        for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = -1;
+    return true;
+}
+
+// Warp-per-token persistent kernel (any E <= 512, any K <= 32; also the ids-only maps).
+// smem: sel[tpc*K] | hist[E] | totsm[E] | offs[E+1] | scratch[64] | ring (phase 1) = whist (phase 3)
+template <int VPL, bool VEC, bool ROUTE, int KT>
+__global__ void __launch_bounds__(kPW * 32) maps_persistent_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias,
+    const int32_t* __restrict__ ids_in, int32_t* __restrict__ ids_out, float* __restrict__ w,
+    int64_t T, int E, int K, int renorm, int tpc, int32_t* __restrict__ counts,
+    int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p,
+    PersistWs ws) {
+    pdl_wait();
+    extern __shared__ __align__(16) int smem[];
+    const int c = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int selcap = (tpc * K + 3) & ~3;
+    int* sel = smem;
+    int* hist = sel + selcap;
+    int* totsm = hist + E;
+    int* offs = totsm + E;
+    int* scratch = offs + ((E + 1 + 3) & ~3);
+    float* ring = reinterpret_cast<float*>(scratch + 64);  // phase 1
+    int* whist = scratch + 64;                             // phase 3 (aliases the ring)
+    if (ws_poisoned(ws, E, offsets)) return;
+    const int64_t t0 = (int64_t)c * tpc;
+    const int64_t t1 = min(T, t0 + tpc);
+    const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+
+    // Phase 1: route (or load ids) and histogram this CTA's tokens.
+    if constexpr (ROUTE) {
+        __shared__ int sel_sm[kPW][32];
+        float b[VPL];
+        load_bias<VPL, VEC>(bias, E, lane, b);
+        const RouteSink<float, true, true> sink{ids_out, w, sel, t0, hist};
+        route_tokens<VPL, VEC, KT>(logits, bias, b, E, K, renorm, t0 + warp, t1, kPW,
+                                   VEC ? ring + (size_t)warp * 2 * E : nullptr, sel_sm[warp],
+                                   sink);
+    } else {
+        const int32_t* src = ids_in + t0 * K;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const int e = __ldg(src + i);
+            sel[i] = e;
+            if (e >= 0 && e < E) atomicAdd(&hist[e], 1);
+        }
+    }
+    maps_finish(ws, T, E, K, t0, n, sel, hist, totsm, offs, scratch, whist, counts, offsets, p2u,
+                u2p);
+}
+
+// Hybrid-router persistent kernel (see trouter.cuh).
+// smem: bias[E] | wsm[nw][hwarp] (phase 1) = whist[nw][E] (phase 3) | sel_tmp[nw][32]
+//       | sel[tpc*K] | hist[E] | totsm[E] | offs[E+1] | scratch[64]
+template <int E_, int KT>
+__global__ void __launch_bounds__(256) maps_tpersist_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int32_t* __restrict__ ids_out,
+    float* __restrict__ w, int64_t T, int K, int renorm, int tpc, int32_t* __restrict__ counts,
+    int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p,
+    PersistWs ws) {
+    pdl_wait();
+    extern __shared__ __align__(16) float tsm[];
+    constexpr size_t HW = hwarp_smem_floats<E_>();
+    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* bias_sm = tsm;
+    float* wsm = bias_sm + E_;
+    int* whist = reinterpret_cast<int*>(wsm);
+    int* sel_tmp = reinterpret_cast<int*>(wsm + nw * HW);
+    int* sel = sel_tmp + nw * 32;
+    const int selcap = (tpc * K + 3) & ~3;
+    int* hist = sel + selcap;
+    int* totsm = hist + E_;
+    int* offs = totsm + E_;
+    int* scratch = offs + ((E_ + 1 + 3) & ~3);
+    if (ws_poisoned(ws, E_, offsets)) return;
+    const int c = blockIdx.x;
+    const int64_t t0 = (int64_t)c * tpc;
+    const int64_t t1 = min(T, t0 + tpc);
+    const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
+    for (int e = threadIdx.x; e < E_; e += blockDim.x) hist[e] = 0;
+    troute_setup<E_>(bias, bias_sm);
+    float b[E_ / 32];
+    load_bias<E_ / 32, true>(bias, E_, lane, b);
+
+    // Phase 1: this warp's contiguous share of the CTA's tokens.
+    const int64_t tpw = (t1 - t0 + nw - 1) / nw;
+    const int64_t tb0 = t0 + warp * tpw;
+    const int64_t te = min(t1, tb0 + tpw);
+    troute_range<E_, KT, true, true, float>(logits, b, bias_sm, K, renorm, tb0, te,
+                                            wsm + warp * HW, sel_tmp + warp * 32, ids_out, w, sel,
+                                            t0, hist);
+    maps_finish(ws, T, E_, K, t0, n, sel, hist, totsm, offs, scratch, whist, counts, offsets, p2u,
+                u2p);
+}
+
+// Hybrid router for kb_router: each warp takes a contiguous range of tokens.
+// smem: bias[E] | wsm[nw][hwarp] | sel_tmp[nw][32]
+template <int E_, int KT, typename WT>
+__global__ void __launch_bounds__(256) router_t_kernel(const float* __restrict__ logits,
+                                                       const float* __restrict__ bias,
+                                                       int32_t* __restrict__ ids,
+                                                       WT* __restrict__ w, int64_t T, int K,
+                                                       int renorm, int64_t tpw) {
+    pdl_wait();
+    pdl_launch();
+    extern __shared__ __align__(16) float tsm[];
+    constexpr size_t HW = hwarp_smem_floats<E_>();
+    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* bias_sm = tsm;
+    float* wsm = bias_sm + E_;
+    int* sel_tmp = reinterpret_cast<int*>(wsm + nw * HW);
+    troute_setup<E_>(bias, bias_sm);
+    float b[E_ / 32];
+    load_bias<E_ / 32, true>(bias, E_, lane, b);
+    const int64_t tb0 = ((int64_t)blockIdx.x * nw + warp) * tpw;
+    const int64_t te = min(T, tb0 + tpw);
+    troute_range<E_, KT, false, false, WT>(logits, b, bias_sm, K, renorm, tb0, te, wsm + warp * HW,
+                                           sel_tmp + warp * 32, ids, w, nullptr, 0, nullptr);
+}
+
+// ------------------------------------------------------------------------------------
+// Two-kernel maps (fallback).  Kernel 1: per-tile histogram (optionally routing the tile);
+// the last CTA of a super-tile to arrive sums its tiles into super_hist and resets the
+// counter.  Kernel 2: one CTA per super-tile scans the super-tile rows and scatters.
 // ------------------------------------------------------------------------------------
 struct MapsWs {
     unsigned* arrive;   // [S]      zero between calls
@@ -418,7 +756,7 @@ struct MapsWs {
     int* super_hist;    // [S][E]
 };
 
-template <int VPL, bool VEC, bool ROUTE>
+template <int VPL, bool VEC, bool ROUTE, int KT>
 __global__ void __launch_bounds__(256) maps_count_kernel(
     const float* __restrict__ logits, const float* __restrict__ bias,
     const int32_t* __restrict__ ids_in, int32_t* __restrict__ ids_out, float* __restrict__ w,
@@ -426,6 +764,7 @@ __global__ void __launch_bounds__(256) maps_count_kernel(
     MapsWs ws) {
     pdl_wait();
     pdl_launch();
+    extern __shared__ __align__(16) float csmem[];
     __shared__ int hist[E_MAX];
     __shared__ int sel_sm[8][32];
     __shared__ int is_last;
@@ -438,18 +777,10 @@ __global__ void __launch_bounds__(256) maps_count_kernel(
     if constexpr (ROUTE) {
         float b[VPL];
         load_bias<VPL, VEC>(bias, E, lane, b);
-        for (int64_t t = t0 + warp; t < t1; t += 8) {
-            const float* row = logits + t * E;
-            route_token<VPL, VEC>(row, b, E, K, lane, sel_sm[warp]);
-            const int id = (lane < K) ? sel_sm[warp][lane] : 0;
-            const float wv = pick_weight(row, id, K, lane, renorm);
-            if (lane < K) {
-                ids_out[t * K + lane] = id;
-                w[t * K + lane] = wv;
-                atomicAdd(&hist[id], 1);
-            }
-            __syncwarp();
-        }
+        const RouteSink<float, false, true> sink{ids_out, w, nullptr, 0, hist};
+        route_tokens<VPL, VEC, KT>(logits, bias, b, E, K, renorm, t0 + warp, t1, 8,
+                                   VEC ? csmem + (size_t)warp * 2 * E : nullptr, sel_sm[warp],
+                                   sink);
     } else {
         for (int64_t i = t0 * K + threadIdx.x; i < t1 * K; i += blockDim.x) {
             const int e = __ldg(ids_in + i);
@@ -481,16 +812,14 @@ __global__ void __launch_bounds__(256) maps_count_kernel(
     }
 }
 
-// Multi-CTA maps, kernel 2: one CTA per super-tile.  Scans the super-tile rows, writes
-// counts/offsets (CTA 0), ranks the super-tile's selections and scatters p2u/u2p.
-// smem: sel[G*K] | whist[32][E] | tot[E] | pre[E] | offs[E+1] | scratch[32]
+// smem: sel[G*K] | whist[32][E] | tot[E] | pre[E] | offs[E+1] | scratch[64]
 __global__ void __launch_bounds__(1024) maps_scatter_kernel(
     const int32_t* __restrict__ ids, int64_t T, int E, int K, int super_tokens, int S,
     const int* __restrict__ super_hist, int32_t* __restrict__ counts,
     int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p) {
     pdl_wait();
     pdl_launch();
-    extern __shared__ int smem[];
+    extern __shared__ __align__(16) int smem[];
     const int s = blockIdx.x;
     const int nwarps = blockDim.x >> 5;
     const int64_t tok0 = (int64_t)s * super_tokens;
@@ -503,7 +832,6 @@ __global__ void __launch_bounds__(1024) maps_scatter_kernel(
     int* pre = tot + E;
     int* offs = pre + E;
     int* scratch = offs + E + 1;
-    // Selections of this super-tile (contiguous in ids).
     const int32_t* src = ids + tok0 * K;
     for (int i = threadIdx.x; i < n; i += blockDim.x) sel[i] = __ldcg(src + i);
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -530,7 +858,7 @@ __global__ void __launch_bounds__(1024) maps_scatter_kernel(
         for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += base;
     }
     __syncthreads();
-    rank_scatter(sel, n, tok0 * K, T, E, K, whist, p2u, u2p);
+    rank_scatter(sel, n, tok0, T, E, K, whist, p2u, u2p);
 }
 
 // ------------------------------------------------------------------------------------
@@ -541,39 +869,107 @@ namespace {
 constexpr int kSingleThreads = 1024;
 constexpr int kScatterThreads = 1024;
 constexpr int kTargetSupers = 64;
-constexpr int kMaxSingleSel = 12288;  // single-CTA path: T*K selections held in smem
-
-struct MapsPlan {
-    bool single;
-    int TT;               // tokens per tile (kernel 1)
-    int num_tiles;
-    int tiles_per_super;
-    int S;
-    int super_tokens;
-    size_t ws_bytes;
-    size_t smem_single;
-    size_t smem_scatter;
-};
+constexpr int kMaxSingleSel = 12288;   // single-CTA path: T*K selections held in smem
+constexpr int kMaxPersistSel = 16384;  // persistent path: selections per CTA held in smem
+constexpr int kMaxPersistGrid = 1024;  // column_scan handles up to 4*256 CTAs
+constexpr size_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-size_t single_smem(int64_t T, int E, int K) {
-    const size_t n = (size_t)T * K;
-    return (((n + 3) & ~size_t(3)) + (size_t)32 * E + 2 * E + 1 + 32) * sizeof(int);
+struct DevInfo {
+    int sms = 0;
+};
+
+DevInfo dev_info() {
+    static std::mutex mu;
+    static DevInfo cache[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    DevInfo& d = cache[dev & 63];
+    if (d.sms == 0) {
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        if (d.sms <= 0) d.sms = 148;
+    }
+    return d;
 }
 
-MapsPlan make_plan(int64_t T, int E, int K, int mode, bool route) {
-    MapsPlan p{};
-    const int64_t n = T * K;
-    const bool fits_single = n <= kMaxSingleSel;
-    const int64_t auto_single_T = route ? 32 : 768;
-    p.single = (mode == KB_MAPS_SINGLE_CTA) ? fits_single
-             : (mode == KB_MAPS_MULTI_CTA) ? false
-             : (fits_single && T <= auto_single_T);
-    p.smem_single = single_smem(T, E, K);
-    if (p.single) return p;
+enum class Path { Single, Persistent, TPersistent, TwoKernel };
+
+struct MapsPlan {
+    Path path;
+    // single
+    size_t smem_single;
+    // persistent (warp-per-token or transposed)
+    int grid, tpc, tnw;
+    size_t smem_persist;
+    // two-kernel
+    int TT, num_tiles, tiles_per_super, S, super_tokens;
+    size_t smem_scatter, smem_count;
+    size_t ws_bytes;   // workspace for the chosen multi-CTA path
+};
+
+size_t single_smem(int64_t T, int E, int K, bool route, bool vec) {
+    const size_t n = (size_t)T * K;
+    size_t words = ((n + 3) & ~size_t(3)) + (size_t)32 * E + E + (E + 1) + 64 + 8;
+    size_t bytes = words * sizeof(int) + 16;
+    if (route && vec) bytes += (size_t)32 * 2 * E * sizeof(float);
+    return bytes;
+}
+
+// Hybrid-router shared memory: bias[E] | wsm[nw][hwarp] | sel_tmp[nw][32]
+// [ | sel[tpc*K] | hist[E] | totsm[E] | offs[E+1] | scratch[64]  when persistent; whist[nw][E]
+//   aliases wsm ]
+template <int E_>
+size_t troute_smem(int nw, int tpc, int K) {
+    const size_t wsm = std::max((size_t)nw * hwarp_smem_floats<E_>(), (size_t)nw * E_);
+    size_t b = (size_t)E_ * sizeof(float) + wsm * sizeof(float) + (size_t)nw * 32 * sizeof(int);
+    if (tpc > 0)
+        b += ((((size_t)tpc * K + 3) & ~size_t(3)) + 2 * (size_t)E_ + ((E_ + 1 + 3) & ~3) + 64) *
+             sizeof(int);
+    return b;
+}
+
+// sel | hist | totsm | offs | scratch | union { ring (phase 1), whist (phase 3) }
+size_t persist_smem(int tpc, int E, int K, bool route, bool vec) {
+    size_t words = (((size_t)tpc * K + 3) & ~size_t(3)) + 2 * (size_t)E + ((E + 1 + 3) & ~3) + 64;
+    const size_t whist = (size_t)kPW * E * sizeof(int);
+    const size_t ring = (route && vec) ? (size_t)kPW * 2 * E * sizeof(float) : 0;
+    return words * sizeof(int) + std::max(whist, ring);
+}
+
+size_t persist_ws_bytes(int grid, int E) {
+    return align256(2 * sizeof(int)) + 2 * align256((size_t)E * grid * sizeof(int)) +
+           align256((size_t)E * sizeof(int));
+}
+
+PersistWs carve_persist(void* ws, int grid, int E) {
+    char* b = static_cast<char*>(ws);
+    PersistWs w;
+    w.bar = reinterpret_cast<unsigned*>(b);
+    w.err = reinterpret_cast<int*>(b + sizeof(int));
+    b += align256(2 * sizeof(int));
+    w.colhist = reinterpret_cast<int*>(b);
+    b += align256((size_t)E * grid * sizeof(int));
+    w.colpre = reinterpret_cast<int*>(b);
+    b += align256((size_t)E * grid * sizeof(int));
+    w.tot = reinterpret_cast<int*>(b);
+    return w;
+}
+
+// Largest cooperative grid for a persistent kernel instance (per device, cached by the
+// caller's static).  Returns CTAs per SM.
+template <typename KernelT>
+int coop_blocks_per_sm(KernelT kern, size_t smem) {
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kPW * 32, smem) != cudaSuccess)
+        return 0;
+    return nb;
+}
+
+// Two-kernel plan (also the workspace bound).
+void plan_two_kernel(MapsPlan& p, int64_t T, int E, int K, bool route, bool vec) {
     if (route) {
-        // 8 warps per tile; tokens per warp grows with T so that ~2 CTAs per SM remain.
         int64_t tpw = (T + 148 * 2 * 8 - 1) / (148 * 2 * 8);
         tpw = std::max<int64_t>(1, std::min<int64_t>(16, tpw));
         p.TT = (int)(8 * tpw);
@@ -581,21 +977,21 @@ MapsPlan make_plan(int64_t T, int E, int K, int mode, bool route) {
         p.TT = 256;
     }
     p.num_tiles = (int)((T + p.TT - 1) / p.TT);
-    // Kernel 2 holds a super-tile's selections in shared memory: cap them at 24576 (96 KB);
-    // beyond that the number of super-tiles grows instead.
     const int max_tps = std::max(1, 24576 / (K * p.TT));
     p.tiles_per_super = std::min(max_tps, (p.num_tiles + kTargetSupers - 1) / kTargetSupers);
     p.S = (p.num_tiles + p.tiles_per_super - 1) / p.tiles_per_super;
     p.super_tokens = p.TT * p.tiles_per_super;
-    p.ws_bytes = align256((size_t)p.S * sizeof(unsigned)) +
-                 align256((size_t)p.num_tiles * E * sizeof(int)) +
-                 align256((size_t)p.S * E * sizeof(int));
     const size_t cap = (size_t)p.super_tokens * K;
-    p.smem_scatter = (((cap + 3) & ~size_t(3)) + (size_t)(kScatterThreads / 32) * E + 3 * E + 1 + 32) * sizeof(int);
-    return p;
+    p.smem_scatter = (((cap + 3) & ~size_t(3)) + (size_t)(kScatterThreads / 32) * E + 3 * E + 1 + 64) * sizeof(int);
+    p.smem_count = (route && vec) ? (size_t)8 * 2 * E * sizeof(float) : 0;
 }
 
-MapsWs carve(void* ws, const MapsPlan& p, int E) {
+size_t two_kernel_ws(const MapsPlan& p, int E) {
+    return align256((size_t)p.S * sizeof(unsigned)) + align256((size_t)p.num_tiles * E * sizeof(int)) +
+           align256((size_t)p.S * E * sizeof(int));
+}
+
+MapsWs carve_two(void* ws, const MapsPlan& p, int E) {
     char* b = static_cast<char*>(ws);
     MapsWs w;
     w.arrive = reinterpret_cast<unsigned*>(b);
@@ -625,48 +1021,265 @@ int with_layout(int E, Args&&... args) {
 
 template <int VPL, bool VEC>
 struct RouterLaunch {
-    static int run(const float* logits, const float* bias, int32_t* ids, void* w, int w_dtype,
-                   int64_t T, int E, int K, int renorm, cudaStream_t st) {
-        const int64_t ctas = std::min<int64_t>((T + 7) / 8, 148 * 64);
+    template <int KT>
+    static int run_kt(const float* logits, const float* bias, int32_t* ids, void* w, int w_dtype,
+                      int64_t T, int E, int K, int renorm, cudaStream_t st) {
+        const int64_t ctas = std::min<int64_t>((T + 7) / 8, (int64_t)dev_info().sms * 8);
         dim3 grid((unsigned)std::max<int64_t>(1, ctas)), block(256);
+        const size_t smem = VEC ? (size_t)8 * 2 * E * sizeof(float) : 0;
         switch (w_dtype) {
             case KB_F32:
-                return launch(router_kernel<VPL, VEC, float>, grid, block, 0, st, logits, bias,
-                              ids, static_cast<float*>(w), T, E, K, renorm);
+                return launch(router_kernel<VPL, VEC, KT, float>, grid, block, smem, st, logits,
+                              bias, ids, static_cast<float*>(w), T, E, K, renorm);
             case KB_BF16:
-                return launch(router_kernel<VPL, VEC, __nv_bfloat16>, grid, block, 0, st, logits,
-                              bias, ids, static_cast<__nv_bfloat16*>(w), T, E, K, renorm);
+                return launch(router_kernel<VPL, VEC, KT, __nv_bfloat16>, grid, block, smem, st,
+                              logits, bias, ids, static_cast<__nv_bfloat16*>(w), T, E, K, renorm);
             case KB_F16:
-                return launch(router_kernel<VPL, VEC, __half>, grid, block, 0, st, logits, bias,
-                              ids, static_cast<__half*>(w), T, E, K, renorm);
+                return launch(router_kernel<VPL, VEC, KT, __half>, grid, block, smem, st, logits,
+                              bias, ids, static_cast<__half*>(w), T, E, K, renorm);
             default:
                 return KB_ERR_UNSUPPORTED;
         }
     }
+    // Lane-per-token router (trouter.cuh) for E = 32*VPL in {128, 256, 384, 512}, K <= 8.
+    template <int KT, typename WT>
+    static int run_t(const float* logits, const float* bias, int32_t* ids, WT* w, int64_t T,
+                     int K, int renorm, cudaStream_t st) {
+        constexpr int E_ = 32 * VPL;
+        constexpr int nw = 8;
+        const int sms = dev_info().sms;
+        auto* kern = router_t_kernel<E_, KT, WT>;
+        const size_t smem = troute_smem<E_>(nw, 0, 0);
+        int err = allow_smem(kern, smem);
+        if (err) return err;
+        static int bps = 0;  // co-resident CTAs per SM (per instance)
+        if (bps == 0) {
+            int v = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, 32 * nw, smem);
+            bps = v > 0 ? v : 1;
+        }
+        const int64_t slots = (int64_t)sms * bps * nw;   // resident warps
+        const int64_t tpw = std::max<int64_t>(std::min<int64_t>(32, T), (T + slots - 1) / slots);
+        const int64_t warps = (T + tpw - 1) / tpw;
+        const int64_t ctas = (warps + nw - 1) / nw;
+        return launch(kern, dim3((unsigned)ctas), dim3(32 * nw), smem, st, logits, bias, ids, w, T,
+                      K, renorm, tpw);
+    }
+    template <typename WT>
+    static int run_t_any(const float* logits, const float* bias, int32_t* ids, WT* w, int64_t T,
+                         int K, int renorm, cudaStream_t st) {
+        if (K == 6) return run_t<6, WT>(logits, bias, ids, w, T, K, renorm, st);
+        return run_t<0, WT>(logits, bias, ids, w, T, K, renorm, st);
+    }
+    static int run(const float* logits, const float* bias, int32_t* ids, void* w, int w_dtype,
+                   int64_t T, int E, int K, int renorm, cudaStream_t st) {
+        if constexpr (VEC) {
+            if (K <= 8) {
+                switch (w_dtype) {
+                    case KB_F32: return run_t_any<float>(logits, bias, ids, static_cast<float*>(w), T, K, renorm, st);
+                    case KB_BF16: return run_t_any<__nv_bfloat16>(logits, bias, ids, static_cast<__nv_bfloat16*>(w), T, K, renorm, st);
+                    case KB_F16: return run_t_any<__half>(logits, bias, ids, static_cast<__half*>(w), T, K, renorm, st);
+                    default: return KB_ERR_UNSUPPORTED;
+                }
+            }
+        }
+        if (VEC && K == 6) return run_kt<6>(logits, bias, ids, w, w_dtype, T, E, K, renorm, st);
+        return run_kt<0>(logits, bias, ids, w, w_dtype, T, E, K, renorm, st);
+    }
 };
+
+template <typename... KArgs, typename... Args>
+int launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 template <bool ROUTE>
 struct MapsLaunchT {
     template <int VPL, bool VEC>
     struct Impl {
-        static int run(const float* logits, const float* bias, const int32_t* ids_in,
-                       int32_t* ids_out, float* w, int32_t* counts, int64_t* offsets,
-                       int32_t* p2u, int32_t* u2p, void* ws, size_t ws_bytes, int64_t T,
-                       int E, int K, int renorm, int mode, cudaStream_t st) {
-            const MapsPlan p = make_plan(T, E, K, mode, ROUTE);
-            if (p.single) {
-                auto* kern = maps_single_kernel<VPL, VEC, ROUTE>;
+        template <int KT>
+        static auto persistent_kernel() { return maps_persistent_kernel<VPL, VEC, ROUTE, KT>; }
+
+        // Co-resident CTAs per SM of the persistent kernel at a given shared-memory size.
+        static int blocks_per_sm(int E, int K, size_t smem) {
+            static std::mutex mu;
+            static std::map<std::tuple<int, int, int, size_t>, int> cache;
+            int dev = 0;
+            cudaGetDevice(&dev);
+            std::lock_guard<std::mutex> lk(mu);
+            int& v = cache[std::make_tuple(dev, E, K, smem)];
+            if (v == 0) {
+                int occ = 0;
+                if (VEC && ROUTE && K == 6) {
+                    auto* kern = persistent_kernel<6>();
+                    allow_smem(kern, smem);
+                    occ = coop_blocks_per_sm(kern, smem);
+                } else {
+                    auto* kern = persistent_kernel<0>();
+                    allow_smem(kern, smem);
+                    occ = coop_blocks_per_sm(kern, smem);
+                }
+                v = occ > 0 ? occ : -1;
+            }
+            return v;
+        }
+
+        // Largest co-resident grid (<= 8 CTAs/SM) whose footprint still fits at that occupancy.
+        static bool plan_persist(MapsPlan& p, int64_t T, int E, int K) {
+            const int sms = dev_info().sms;
+            const int64_t min_tpc = 2 * kPW;
+            for (int bps = 8; bps >= 1; --bps) {
+                int grid = (int)std::min<int64_t>(std::min(kMaxPersistGrid, bps * sms),
+                                                  (T + min_tpc - 1) / min_tpc);
+                grid = std::max(grid, 1);
+                const int64_t tpc = (T + grid - 1) / grid;
+                if (tpc * K > kMaxPersistSel) return false;
+                const size_t smem = persist_smem((int)tpc, E, K, ROUTE, VEC);
+                if (smem > kMaxSmem) return false;
+                const int occ = blocks_per_sm(E, K, smem);
+                if (occ <= 0) return false;
+                if ((int64_t)occ * sms >= grid) {
+                    p.grid = (int)((T + tpc - 1) / tpc);
+                    p.tpc = (int)tpc;
+                    p.smem_persist = smem;
+                    return true;
+                }
+            }
+            return false;
+        }
+
+        // Transposed-router persistent kernel (routing, E = 32*VPL, K <= 8): one CTA per SM,
+        // up to 4 router warps, whatever fits in shared memory.
+        static bool plan_tpersist(MapsPlan& p, int64_t T, int E, int K) {
+            if constexpr (!(ROUTE && VEC)) {
+                return false;
+            } else {
+                constexpr int E_ = 32 * VPL;
+                constexpr int nw = 8;
+                if (K > 8 || E != E_) return false;
+                const int sms = dev_info().sms;
+                for (int bps = 4; bps >= 1; --bps) {
+                    int grid = (int)std::min<int64_t>(std::min(kMaxPersistGrid, bps * sms),
+                                                      (T + 31) / 32);
+                    grid = std::max(grid, 1);
+                    const int64_t tpc = (T + grid - 1) / grid;
+                    if (tpc * K > kMaxPersistSel) return false;
+                    const size_t smem = troute_smem<E_>(nw, (int)tpc, K);
+                    if (smem > kMaxSmem) return false;
+                    const int occ = tblocks_per_sm(K, smem);
+                    if (occ <= 0) return false;
+                    if ((int64_t)occ * sms >= grid) {
+                        p.grid = (int)((T + tpc - 1) / tpc);
+                        p.tpc = (int)tpc;
+                        p.tnw = nw;
+                        p.smem_persist = smem;
+                        return true;
+                    }
+                }
+                return false;
+            }
+        }
+
+        // Co-resident CTAs per SM of the transposed persistent kernel.
+        static int tblocks_per_sm(int K, size_t smem) {
+            if constexpr (!(ROUTE && VEC)) {
+                return 0;
+            } else {
+                constexpr int E_ = 32 * VPL;
+                static std::mutex mu;
+                static std::map<std::tuple<int, int, size_t>, int> cache;
+                int dev = 0;
+                cudaGetDevice(&dev);
+                std::lock_guard<std::mutex> lk(mu);
+                int& v = cache[std::make_tuple(dev, K == 6 ? 6 : 0, smem)];
+                if (v == 0) {
+                    int occ = 0;
+                    if (K == 6) {
+                        auto* kern = maps_tpersist_kernel<E_, 6>;
+                        allow_smem(kern, smem);
+                        occ = coop_blocks_per_sm(kern, smem);
+                    } else {
+                        auto* kern = maps_tpersist_kernel<E_, 0>;
+                        allow_smem(kern, smem);
+                        occ = coop_blocks_per_sm(kern, smem);
+                    }
+                    v = occ > 0 ? occ : -1;
+                }
+                return v;
+            }
+        }
+
+        static MapsPlan plan(int64_t T, int E, int K, int mode) {
+            MapsPlan p{};
+            const bool fits_single = T * K <= kMaxSingleSel;
+            const int64_t auto_single_T = ROUTE ? 32 : 768;
+            if (mode == KB_MAPS_SINGLE_CTA || (mode == KB_MAPS_AUTO && fits_single && T <= auto_single_T)) {
+                p.path = Path::Single;
+                p.smem_single = single_smem(T, E, K, ROUTE, VEC);
+                return p;
+            }
+            plan_two_kernel(p, T, E, K, ROUTE, VEC);
+            if (mode != KB_MAPS_TWO_KERNEL && plan_tpersist(p, T, E, K)) {
+                p.path = Path::TPersistent;
+                p.ws_bytes = persist_ws_bytes(p.grid, E);
+            } else if (mode != KB_MAPS_TWO_KERNEL && plan_persist(p, T, E, K)) {
+                p.path = Path::Persistent;
+                p.ws_bytes = persist_ws_bytes(p.grid, E);
+            } else {
+                p.path = Path::TwoKernel;
+                p.ws_bytes = two_kernel_ws(p, E);
+            }
+            return p;
+        }
+
+        template <int KT>
+        static int run_kt(const MapsPlan& p, const float* logits, const float* bias,
+                          const int32_t* ids_in, int32_t* ids_out, float* w, int32_t* counts,
+                          int64_t* offsets, int32_t* p2u, int32_t* u2p, void* ws, int64_t T, int E,
+                          int K, int renorm, cudaStream_t st) {
+            if (p.path == Path::Single) {
+                auto* kern = maps_single_kernel<VPL, VEC, ROUTE, KT>;
                 int err = allow_smem(kern, p.smem_single);
                 if (err) return err;
                 return launch(kern, dim3(1), dim3(kSingleThreads), p.smem_single, st, logits, bias,
                               ids_in, ids_out, w, T, E, K, renorm, counts, offsets, p2u, u2p);
             }
-            if (ws == nullptr || ws_bytes < p.ws_bytes) return KB_ERR_WORKSPACE;
-            if (!aligned16(ws)) return KB_ERR_ALIGNMENT;
-            const MapsWs w_ = carve(ws, p, E);
-            int err = launch(maps_count_kernel<VPL, VEC, ROUTE>, dim3(p.num_tiles), dim3(256), 0,
-                             st, logits, bias, ids_in, ids_out, w, T, E, K, renorm, p.TT,
-                             p.tiles_per_super, p.num_tiles, w_);
+            if constexpr (ROUTE && VEC) {
+                if (p.path == Path::TPersistent) {
+                    constexpr int E_ = 32 * VPL;
+                    auto* kern = maps_tpersist_kernel<E_, (KT == 6 ? 6 : 0)>;
+                    int err = allow_smem(kern, p.smem_persist);
+                    if (err) return err;
+                    return launch_coop(kern, dim3(p.grid), dim3(32 * p.tnw), p.smem_persist, st,
+                                       logits, bias, ids_out, w, T, K, renorm, p.tpc, counts,
+                                       offsets, p2u, u2p, carve_persist(ws, p.grid, E));
+                }
+            }
+            if (p.path == Path::Persistent) {
+                auto* kern = persistent_kernel<KT>();
+                int err = allow_smem(kern, p.smem_persist);
+                if (err) return err;
+                return launch_coop(kern, dim3(p.grid), dim3(kPW * 32), p.smem_persist, st, logits,
+                                   bias, ids_in, ids_out, w, T, E, K, renorm, p.tpc, counts,
+                                   offsets, p2u, u2p, carve_persist(ws, p.grid, E));
+            }
+            const MapsWs w_ = carve_two(ws, p, E);
+            auto* k1 = maps_count_kernel<VPL, VEC, ROUTE, KT>;
+            int err = allow_smem(k1, p.smem_count);
+            if (err) return err;
+            err = launch(k1, dim3(p.num_tiles), dim3(256), p.smem_count, st, logits, bias, ids_in,
+                         ids_out, w, T, E, K, renorm, p.TT, p.tiles_per_super, p.num_tiles, w_);
             if (err) return err;
             err = allow_smem(maps_scatter_kernel, p.smem_scatter);
             if (err) return err;
@@ -675,6 +1288,51 @@ struct MapsLaunchT {
                           ids_src, T, E, K, p.super_tokens, p.S,
                           static_cast<const int*>(w_.super_hist), counts, offsets, p2u, u2p);
         }
+
+        static int run(const float* logits, const float* bias, const int32_t* ids_in,
+                       int32_t* ids_out, float* w, int32_t* counts, int64_t* offsets,
+                       int32_t* p2u, int32_t* u2p, void* ws, size_t ws_bytes, int64_t T,
+                       int E, int K, int renorm, int mode, cudaStream_t st) {
+            const MapsPlan p = plan(T, E, K, mode);
+            if (p.path == Path::Single) {
+                if (T * K > kMaxSingleSel || p.smem_single > kMaxSmem) return KB_ERR_UNSUPPORTED;
+            } else {
+                if (ws == nullptr || ws_bytes < p.ws_bytes) return KB_ERR_WORKSPACE;
+                if (!aligned16(ws)) return KB_ERR_ALIGNMENT;
+            }
+            if (VEC && ROUTE && K == 6)
+                return run_kt<6>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
+                                 ws, T, E, K, renorm, st);
+            if (p.path == Path::TPersistent)  // runtime-K transposed kernel (K <= 8)
+                return run_kt<0>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
+                                 ws, T, E, K, renorm, st);
+            return run_kt<0>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p, ws,
+                             T, E, K, renorm, st);
+        }
+
+        // Workspace large enough for every multi-CTA path at this T.
+        static size_t ws_bound(int64_t T, int E, int K) {
+            MapsPlan p{};
+            plan_two_kernel(p, T, E, K, ROUTE, VEC);
+            size_t b = two_kernel_ws(p, E);
+            MapsPlan q{};
+            if (plan_persist(q, T, E, K)) b = std::max(b, persist_ws_bytes(q.grid, E));
+            MapsPlan r{};
+            if (plan_tpersist(r, T, E, K)) b = std::max(b, persist_ws_bytes(r.grid, E));
+            return b;
+        }
+
+        // Path, launches and grid the library would use (introspection for benchmarks).
+        static void describe(int64_t T, int E, int K, int mode, int* path, int* launches,
+                             int* grid) {
+            const MapsPlan p = plan(T, E, K, mode);
+            const bool pers = p.path == Path::Persistent || p.path == Path::TPersistent;
+            const int pk = p.path == Path::Single ? KB_MAPS_SINGLE_CTA
+                         : pers ? KB_MAPS_MULTI_CTA : KB_MAPS_TWO_KERNEL;
+            if (path) *path = pk;
+            if (launches) *launches = (p.path == Path::TwoKernel) ? 2 : 1;
+            if (grid) *grid = p.path == Path::Single ? 1 : pers ? p.grid : p.num_tiles;
+        }
     };
 };
 
@@ -682,6 +1340,24 @@ template <int VPL, bool VEC>
 using MapsOnly = MapsLaunchT<false>::Impl<VPL, VEC>;
 template <int VPL, bool VEC>
 using RouterMaps = MapsLaunchT<true>::Impl<VPL, VEC>;
+
+template <template <int, bool> class Fn>
+void describe_for(int64_t T, int E, int K, int mode, int* path, int* launches, int* grid) {
+    if (E == 384) return Fn<12, true>::describe(T, E, K, mode, path, launches, grid);
+    if (E == 256) return Fn<8, true>::describe(T, E, K, mode, path, launches, grid);
+    if (E == 512) return Fn<16, true>::describe(T, E, K, mode, path, launches, grid);
+    if (E == 128) return Fn<4, true>::describe(T, E, K, mode, path, launches, grid);
+    return Fn<16, false>::describe(T, E, K, mode, path, launches, grid);
+}
+
+template <template <int, bool> class Fn>
+size_t ws_bound_for(int64_t T, int E, int K) {
+    if (E == 384) return Fn<12, true>::ws_bound(T, E, K);
+    if (E == 256) return Fn<8, true>::ws_bound(T, E, K);
+    if (E == 512) return Fn<16, true>::ws_bound(T, E, K);
+    if (E == 128) return Fn<4, true>::ws_bound(T, E, K);
+    return Fn<16, false>::ws_bound(T, E, K);
+}
 
 // T == 0: offsets are all zero.
 __global__ void zero_offsets_kernel(int64_t* offsets, int32_t* counts, int E) {
@@ -710,14 +1386,16 @@ extern "C" int kb_router(const float* logits, const float* bias, int32_t* ids, v
                                      (cudaStream_t)stream);
 }
 
+// The workspace bound covers every multi-CTA path (host-only computation; it queries the
+// device's occupancy only when a GPU is present).
 extern "C" size_t kb_expert_maps_workspace_bytes(int64_t T, int E, int K) {
     if (check_common(T, E, K) != KB_OK || T == 0) return 0;
-    return make_plan(T, E, K, KB_MAPS_MULTI_CTA, false).ws_bytes;
+    return ws_bound_for<MapsOnly>(T, E, K);
 }
 
 extern "C" size_t kb_router_maps_workspace_bytes(int64_t T, int E, int K) {
     if (check_common(T, E, K) != KB_OK || T == 0) return 0;
-    return make_plan(T, E, K, KB_MAPS_MULTI_CTA, true).ws_bytes;
+    return ws_bound_for<RouterMaps>(T, E, K);
 }
 
 extern "C" int kb_expert_maps(const int32_t* ids, int32_t* counts, int64_t* offsets, int32_t* p2u,
@@ -725,7 +1403,7 @@ extern "C" int kb_expert_maps(const int32_t* ids, int32_t* counts, int64_t* offs
                               int E, int K, int mode, kb_stream_t stream) {
     int st = check_common(T, E, K);
     if (st) return st;
-    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_MULTI_CTA) return KB_ERR_INVALID_ARG;
+    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_TWO_KERNEL) return KB_ERR_INVALID_ARG;
     if (!offsets) return KB_ERR_INVALID_ARG;
     if (T == 0)
         return launch(zero_offsets_kernel, dim3(1), dim3(512), 0, (cudaStream_t)stream, offsets,
@@ -743,7 +1421,7 @@ extern "C" int kb_router_maps(const float* logits, const float* bias, int32_t* i
                               int renorm, int mode, kb_stream_t stream) {
     int st = check_common(T, E, K);
     if (st) return st;
-    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_MULTI_CTA) return KB_ERR_INVALID_ARG;
+    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_TWO_KERNEL) return KB_ERR_INVALID_ARG;
     if (!offsets) return KB_ERR_INVALID_ARG;
     if (T == 0)
         return launch(zero_offsets_kernel, dim3(1), dim3(512), 0, (cudaStream_t)stream, offsets,
@@ -754,4 +1432,20 @@ extern "C" int kb_router_maps(const float* logits, const float* bias, int32_t* i
     return with_layout<RouterMaps>(E, logits, bias, nullptr, ids, weights, counts, offsets, p2u,
                                    u2p, workspace, workspace_bytes, T, E, K, renorm, mode,
                                    (cudaStream_t)stream);
+}
+
+extern "C" int kb_maps_describe(int64_t T, int E, int K, int route, int mode, int* path,
+                                int* launches, int* grid) {
+    int st = check_common(T, E, K);
+    if (st) return st;
+    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_TWO_KERNEL) return KB_ERR_INVALID_ARG;
+    if (T == 0) {
+        if (path) *path = KB_MAPS_SINGLE_CTA;
+        if (launches) *launches = 1;
+        if (grid) *grid = 1;
+        return KB_OK;
+    }
+    if (route) describe_for<RouterMaps>(T, E, K, mode, path, launches, grid);
+    else describe_for<MapsOnly>(T, E, K, mode, path, launches, grid);
+    return KB_OK;
 }

@@ -19,7 +19,7 @@ KB_ERR_WORKSPACE = -4
 KB_ERR_TOO_LARGE = -5
 
 KB_BF16, KB_F16, KB_F32 = 0, 1, 2
-KB_MAPS_AUTO, KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA = 0, 1, 2
+KB_MAPS_AUTO, KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA, KB_MAPS_TWO_KERNEL = 0, 1, 2, 3
 
 # name -> (restype, argtypes); must match include/kolibri_b200.h one for one.
 SIGNATURES = {
@@ -35,6 +35,8 @@ SIGNATURES = {
     "kb_router_maps": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_void_p, c_void_p, c_void_p, c_size_t, c_int64, c_int, c_int,
                                c_int, c_int, c_void_p]),
+    "kb_maps_describe": (c_int, [c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                 c_void_p]),
     "kb_expand_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                c_void_p]),
     "kb_qk_norm_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

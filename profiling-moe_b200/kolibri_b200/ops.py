@@ -12,12 +12,12 @@ from typing import Optional, Tuple
 import torch
 
 from ._lib import (KB_BF16, KB_F16, KB_F32, KB_MAPS_AUTO, KB_MAPS_MULTI_CTA, KB_MAPS_SINGLE_CTA,
-                   check, load)
+                   KB_MAPS_TWO_KERNEL, check, load)
 
 __all__ = [
     "router", "expert_maps", "router_maps", "expand_rows", "qk_norm_rope", "rope_inv_freq",
     "residual_norm_pair", "add_rms_norm", "reserve_workspace", "set_pdl",
-    "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA",
+    "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA", "KB_MAPS_TWO_KERNEL",
 ]
 
 _DTYPE_CODE = {torch.bfloat16: KB_BF16, torch.float16: KB_F16, torch.float32: KB_F32}

@@ -14,7 +14,7 @@ from oracle import kolibri_oracle as orc
 
 pytestmark = pytest.mark.gpu
 
-MODES = [ops.KB_MAPS_AUTO, ops.KB_MAPS_SINGLE_CTA, ops.KB_MAPS_MULTI_CTA]
+MODES = [ops.KB_MAPS_AUTO, ops.KB_MAPS_SINGLE_CTA, ops.KB_MAPS_MULTI_CTA, ops.KB_MAPS_TWO_KERNEL]
 
 
 def check_maps(ids_cpu, got, E=384):
@@ -61,13 +61,13 @@ def test_maps_golden_offsets(T):
 def test_maps_reference_invariant_sizes(T):
     torch.manual_seed(42)
     ids = torch.randint(0, 384, (T, 6), dtype=torch.int32)
-    for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA):
+    for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA, ops.KB_MAPS_TWO_KERNEL):
         check_maps(ids, ops.expert_maps(ids.cuda(), 384, mode=mode))
 
 
 def test_maps_edge_cases():
     one = torch.full((5000, 6), 7, dtype=torch.int32)
-    for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA):
+    for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA, ops.KB_MAPS_TWO_KERNEL):
         check_maps(one, ops.expert_maps(one.cuda(), 384, mode=mode))
     bad = torch.from_numpy(np.random.default_rng(0).integers(-3, 390, size=(700, 6)).astype(np.int32))
     for mode in MODES:
@@ -90,7 +90,8 @@ def test_maps_repeated_calls_reuse_workspace():
     for i in range(6):
         T = (70000, 3000, 513)[i % 3]
         ids = torch.randint(0, 384, (T, 6), dtype=torch.int32)
-        check_maps(ids, ops.expert_maps(ids.cuda(), 384, mode=ops.KB_MAPS_MULTI_CTA))
+        for mode in (ops.KB_MAPS_MULTI_CTA, ops.KB_MAPS_TWO_KERNEL):
+            check_maps(ids, ops.expert_maps(ids.cuda(), 384, mode=mode))
 
 
 @pytest.mark.parametrize("T", [1, 32, 33, 256, 4096, 65536])

@@ -59,6 +59,21 @@ def test_router_ties_exact_path():
     run_and_check(torch.zeros(8, 384), None)
 
 
+def test_router_displaced_ties_keep_index_order():
+    # Equal scores at low indices, larger scores at higher indices: the larger picks arrive
+    # later and displace the equal ones, which must keep their index order.
+    x = torch.zeros(64, 384)
+    x[:, :40] = 3.0
+    for r in range(64):
+        x[r, 100 + r % 200] = 5.0 + (r % 3)
+        x[r, 300 + r % 80] = 4.0
+    run_and_check(x, None)
+    run_and_check(x, torch.zeros(384), k=8)
+    g = torch.Generator().manual_seed(5)
+    logits = torch.randint(-3, 4, (1024, 384), generator=g).float()
+    run_and_check(logits, torch.randint(-1, 2, (384,), generator=g).float())
+
+
 def test_router_winners_in_one_lane():
     # Lane 0 of the float4 layout holds experts 0-3, 128-131, 256-259: give it the top 6..12.
     x = torch.randn(64, 384) - 10.0
