@@ -40,7 +40,8 @@ enum {
     KB_ERR_UNSUPPORTED = -2,  /* shape / dtype / K / E outside the kernel's range */
     KB_ERR_ALIGNMENT = -3,    /* pointer or row stride not aligned as required    */
     KB_ERR_WORKSPACE = -4,    /* workspace missing or smaller than *_workspace_bytes */
-    KB_ERR_TOO_LARGE = -5     /* T*K or row count overflows the int32 index space */
+    KB_ERR_TOO_LARGE = -5,    /* T*K or row count overflows the int32 index space */
+    KB_ERR_SCRATCH_LIMIT = -6 /* kb_expert_maps_noalloc: request exceeds its static scratch */
 };
 
 /* Element types of activation tensors. */
@@ -113,6 +114,33 @@ KB_API int kb_router_maps(const float *logits, const float *bias, int32_t *ids, 
  * pointer may be NULL.  Library introspection; no counterpart in the reference. */
 KB_API int kb_maps_describe(int64_t T, int E, int K, int route, int mode, int *path,
                             int *launches, int *grid);
+
+/* kb_expert_maps (mode KB_MAPS_AUTO, same outputs and rules) for callers that may not
+ * allocate device memory: its workspace is a static 8 MiB device array inside this
+ * library (one per device), so neither the caller nor the library allocates anything.
+ * No counterpart in the reference (which allocates its scratch with torch per call).
+ *   Who needs it: hosts whose contract forbids allocation in the launch path, e.g. an
+ *   inference engine that hands all free HBM to its KV cache after a profiling pass (a
+ *   later cudaMalloc fails or fragments), or a plugin enqueue() that may only use the
+ *   workspace its host sized up front.
+ *   Limits: T <= 524288 tokens and a workspace bound (kb_expert_maps_workspace_bytes)
+ *   <= 8 MiB, which holds for every E <= 512, K <= 32 at that T; a larger request
+ *   returns KB_ERR_SCRATCH_LIMIT and launches nothing.
+ *   First call on each device: resolves the scratch address with cudaGetSymbolAddress
+ *   (the CUDA runtime loads this library's device code then if it has not yet) and
+ *   zero-fills the scratch on `stream`.  Make it before any stream capture; a call with
+ *   T = 0 does only this set-up and zeroes offsets (and counts).
+ *   Zero state: the scratch must hold zeros when a call starts; every completed call
+ *   leaves it so.  If a bounded wait inside the kernel gave up (offsets all -1), pass
+ *   flags = KB_NOALLOC_REZERO on the next call to zero-fill it again first.
+ *   Concurrency: all calls on one device share the scratch.  Calls must be ordered
+ *   (one stream, or streams joined by events); two calls in flight at once on the same
+ *   device race on the scratch and give wrong maps.
+ */
+enum { KB_NOALLOC_REZERO = 1 };
+KB_API int kb_expert_maps_noalloc(const int32_t *ids, int32_t *counts, int64_t *offsets,
+                                  int32_t *p2u, int32_t *u2p, int64_t T, int E, int K,
+                                  int flags, kb_stream_t stream);
 
 /* ---------------------------------------------------------------------------------
  * Activation expansion: out[r] = x[p2u[r] % T] for r in [0, rows); a row whose p2u

@@ -28,6 +28,9 @@ extern "C" const char* kb_status_str(int status) {
         case KB_ERR_ALIGNMENT: return "pointer or stride not aligned as the kernel requires";
         case KB_ERR_WORKSPACE: return "workspace missing or smaller than the *_workspace_bytes size";
         case KB_ERR_TOO_LARGE: return "size overflows the int32 index space";
+        case KB_ERR_SCRATCH_LIMIT:
+            return "request exceeds the static scratch of kb_expert_maps_noalloc "
+                   "(T <= 524288 tokens, workspace <= 8 MiB)";
         default: break;
     }
     if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));

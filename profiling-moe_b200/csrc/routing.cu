@@ -1449,3 +1449,76 @@ extern "C" int kb_maps_describe(int64_t T, int E, int K, int route, int mode, in
     else describe_for<MapsOnly>(T, E, K, mode, path, launches, grid);
     return KB_OK;
 }
+
+// ------------------------------------------------------------------------------------
+// kb_expert_maps_noalloc: kb_expert_maps (mode AUTO) with its workspace in a static
+// device array, for callers that may not allocate device memory.
+// ------------------------------------------------------------------------------------
+namespace kb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB on each device
+constexpr int64_t kNoAllocMaxTokens = int64_t(1) << 19;   // 524288 tokens per call
+
+// Workspace of every kb_expert_maps_noalloc call on a device.  The CUDA runtime reserves
+// one copy in each device context when it loads this library's device code; the library
+// never allocates it.  It must hold zeros before the first call (the first call on each
+// device fills it), and every completed call leaves it zero-filled again.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+__global__ void zero_scratch_kernel(uint4* __restrict__ p, size_t n16) {
+    pdl_wait();
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16;
+         i += (size_t)gridDim.x * blockDim.x)
+        p[i] = z;
+    pdl_launch();
+}
+
+// Device address of the scratch for the current device, resolved once per device with
+// cudaGetSymbolAddress; the first call on a device (and any call with KB_NOALLOC_REZERO)
+// zero-fills it on `st` before the maps kernels run.
+int noalloc_scratch(cudaStream_t st, int flags, void** out) {
+    static std::mutex mu;
+    static void* ptrs[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (dev < 0 || dev >= 64) return KB_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lk(mu);
+    void* p = ptrs[dev];
+    const bool first = (p == nullptr);
+    if (first) {
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        if (p == nullptr || !aligned16(p)) return KB_ERR_ALIGNMENT;
+    }
+    if (first || (flags & KB_NOALLOC_REZERO)) {
+        const int err = launch(zero_scratch_kernel, dim3((unsigned)dev_info().sms * 4), dim3(256),
+                               0, st, static_cast<uint4*>(p), kNoAllocScratchBytes / 16);
+        if (err) return err;
+    }
+    ptrs[dev] = p;  // published only once the zero fill is enqueued
+    *out = p;
+    return KB_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" int kb_expert_maps_noalloc(const int32_t* ids, int32_t* counts, int64_t* offsets,
+                                      int32_t* p2u, int32_t* u2p, int64_t T, int E, int K,
+                                      int flags, kb_stream_t stream) {
+    int st = check_common(T, E, K);
+    if (st) return st;
+    if ((flags & ~KB_NOALLOC_REZERO) != 0 || !offsets) return KB_ERR_INVALID_ARG;
+    if (T > 0 && (!ids || !p2u)) return KB_ERR_INVALID_ARG;
+    if (T > kNoAllocMaxTokens) return KB_ERR_SCRATCH_LIMIT;
+    const size_t need = T > 0 ? ws_bound_for<MapsOnly>(T, E, K) : 0;
+    if (need > kNoAllocScratchBytes) return KB_ERR_SCRATCH_LIMIT;
+    void* scratch = nullptr;
+    st = noalloc_scratch(static_cast<cudaStream_t>(stream), flags, &scratch);
+    if (st) return st;
+    return kb_expert_maps(ids, counts, offsets, p2u, u2p, scratch, kNoAllocScratchBytes, T, E, K,
+                          KB_MAPS_AUTO, stream);
+}

@@ -17,6 +17,8 @@ KB_ERR_UNSUPPORTED = -2
 KB_ERR_ALIGNMENT = -3
 KB_ERR_WORKSPACE = -4
 KB_ERR_TOO_LARGE = -5
+KB_ERR_SCRATCH_LIMIT = -6
+KB_NOALLOC_REZERO = 1
 
 KB_BF16, KB_F16, KB_F32 = 0, 1, 2
 KB_MAPS_AUTO, KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA, KB_MAPS_TWO_KERNEL = 0, 1, 2, 3
@@ -37,6 +39,8 @@ SIGNATURES = {
                                c_int, c_int, c_void_p]),
     "kb_maps_describe": (c_int, [c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                  c_void_p]),
+    "kb_expert_maps_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_int64, c_int, c_int, c_int, c_void_p]),
     "kb_expand_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                c_void_p]),
     "kb_qk_norm_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -12,11 +12,11 @@ from typing import Optional, Tuple
 import torch
 
 from ._lib import (KB_BF16, KB_F16, KB_F32, KB_MAPS_AUTO, KB_MAPS_MULTI_CTA, KB_MAPS_SINGLE_CTA,
-                   KB_MAPS_TWO_KERNEL, check, load)
+                   KB_MAPS_TWO_KERNEL, KB_NOALLOC_REZERO, check, load)
 
 __all__ = [
     "router", "expert_maps", "router_maps", "expand_rows", "qk_norm_rope", "rope_inv_freq",
-    "residual_norm_pair", "add_rms_norm", "reserve_workspace", "set_pdl",
+    "residual_norm_pair", "add_rms_norm", "reserve_workspace", "set_pdl", "expert_maps_noalloc",
     "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA", "KB_MAPS_TWO_KERNEL",
 ]
 
@@ -145,6 +145,33 @@ def expert_maps(ids: torch.Tensor, num_experts: int = 384, mode: int = KB_MAPS_A
                              0 if ws is None else ws.numel(), T, E, k, int(mode), _stream(dev)),
           "kb_expert_maps")
     return c, off, p2u, u2p
+
+
+def expert_maps_noalloc(ids: torch.Tensor, c: torch.Tensor, off: torch.Tensor,
+                        p2u: torch.Tensor, u2p: Optional[torch.Tensor] = None,
+                        num_experts: int = 384, rezero: bool = False) -> None:
+    """expert_maps into caller-provided outputs through kb_expert_maps_noalloc: the
+    library's static device scratch replaces the workspace, so the call allocates no
+    device memory.  c int32 [E] (or None), off int64 [E+1], p2u/u2p int32 [T*k]."""
+    _cuda(ids, "token_selected_experts")
+    if ids.dtype != torch.int32 or ids.dim() != 2:
+        raise ValueError("token_selected_experts must be 2D int32 [num_tokens, top_k]")
+    _contig(ids, "token_selected_experts")
+    T, k = ids.shape
+    E = int(num_experts)
+    for t, n, dt, name in ((c, E, torch.int32, "counts"), (off, E + 1, torch.int64, "offsets"),
+                           (p2u, T * k, torch.int32, "p2u"), (u2p, T * k, torch.int32, "u2p")):
+        if t is None:
+            if name in ("offsets", "p2u"):
+                raise ValueError(f"{name} is required")
+            continue
+        _cuda(t, name)
+        _contig(t, name)
+        if t.dtype != dt or t.numel() != n:
+            raise ValueError(f"{name} must be {dt} with {n} elements")
+    check(load().kb_expert_maps_noalloc(_p(ids), _p(c), _p(off), _p(p2u), _p(u2p), T, E, k,
+                                        KB_NOALLOC_REZERO if rezero else 0, _stream(ids.device)),
+          "kb_expert_maps_noalloc")
 
 
 def router_maps(logits: torch.Tensor, bias: Optional[torch.Tensor] = None, k: int = 6,
