@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--impl", choices=["kolibri", "reference"], default="kolibri")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--chain-tokens", default="1,32,256,8192",
+                   help="batch sizes of the 50-layer decode chain ('' = skip)")
+    p.add_argument("--chain-layers", type=int, default=50)
     return p.parse_args()
 
 
@@ -178,6 +181,45 @@ def run_reference(args):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------
+# 50-layer decode chain (replicas only: every rank times its own copy at N>1)
+# ------------------------------------------------------------------------------------
+def decode_chain_times(dev, tokens, n_layers, stream, steps=20, warmup=3):
+    from kolibri_b200 import decode_chain as dc
+    layers = dc.make_layers(n_layers, dev)
+    out = {"layers": n_layers, "rnope_layers": sum(L.rnope for L in layers),
+           "stages": "sandwich, qk_norm_rope, gate GEMM (cuBLAS) + fp32 cast, router+maps, "
+                     "expansion, post-MoE+pre-attn norm",
+           "graph": True, "by_T": {}}
+    for T in tokens:
+        rec = {}
+        for gemm in (True, False):
+            ch = dc.DecodeChain(T, layers, dev, gate_gemm=gemm, expansion=True)
+            g = ch.capture(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(warmup):
+                    g.replay()
+            torch.cuda.synchronize(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                a.record(stream)
+                for _ in range(steps):
+                    g.replay()
+                b.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = a.elapsed_time(b) / steps
+            key = "with_gate_gemm" if gemm else "non_gemm_only"
+            rec[key] = {"us_per_step": round(ms * 1e3, 2),
+                        "us_per_token": round(ms * 1e3 / T, 4),
+                        "kb_launches_per_step": ch.launches_per_layer() * n_layers}
+            del g, ch
+        out["by_T"][str(T)] = rec
+    t1 = out["by_T"].get("1")
+    if t1:
+        out["us_per_token_bs1"] = t1["with_gate_gemm"]["us_per_token"]
+    return out
 
 
 # ------------------------------------------------------------------------------------
@@ -327,6 +369,11 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(ems, 4), "steps": e_steps}
 
+    chain = None
+    if args.chain_tokens:
+        chain = decode_chain_times(dev, [int(t) for t in args.chain_tokens.split(",") if t],
+                                   args.chain_layers, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_reference_rate(T, steps=20, warmup=1, budget_s=20.0)
@@ -354,6 +401,7 @@ def main():
                      "kernel": f"kb_router_maps ({path_name}, grid {grid_c.value})"},
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "decode_chain": chain,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }

@@ -1,0 +1,206 @@
+"""The 50-layer non-GEMM decode chain of a Kolibri-style MoE decoder on one GPU.
+
+It follows the layer loop of the reference's end-to-end harness
+(benchmarks/11_profile_2block_e2e.py:215-280, decoder_layer and forward) restricted to the
+stages between the GEMMs, with the layer schedule of config.json:29-80 (every fifth layer is
+full attention without RoPE).  Per layer i, on one stream:
+
+  1. sandwich norm      h = r + RMSNorm(attn_out)*g_post_attn ; moe_in = RMSNorm(h)*g_pre_moe
+                        (R1_sandwich_norm, :232-234)
+  2. Q/K norm + RoPE    q', k' = per-head RMSNorm then NeoX RoPE at the token positions, or
+                        the RNoPE identity on full-attention layers (attention(), :190-199)
+  3. router GEMM        logits = (moe_in @ W_g[i]).float()        (gate_gemm, :236-238)
+  4. router + maps      top-6 of logits + bias, sigmoid weights, counts/offsets/p2u/u2p
+                        (R2_moe_prologue, :240-246)
+  5. expansion          permuted[r] = moe_in[p2u[r] % T]            (R2, optional)
+  6. post-MoE + next    r = h + RMSNorm(moe_out)*g_post_ffn ; nxt = RMSNorm(r)*g_input_ln
+                        (R3_post_moe_norm :264-266 fused with the next layer's
+                        input_layernorm :222-227)
+
+The attention and expert GEMMs are outside this path: attn_out, moe_out and the projected
+q/k are fixed synthetic stand-ins (one buffer each, shared by all layers), while the residual
+stream r and the router inputs flow from layer to layer, so every layer depends on the one
+before.  The router GEMM is a cuBLAS call (torch.matmul); everything else is a
+libkolibri_b200 kernel launched through the C ABI.  `capture()` records the whole chain in
+one CUDA graph; launches keep programmatic-dependent-launch edges inside it.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, List, Optional
+
+import torch
+
+from . import _lib
+from . import ops
+from . import workloads as wl
+
+
+@dataclass
+class LayerWeights:
+    g_post_attn: torch.Tensor   # bf16 [H]
+    g_pre_moe: torch.Tensor     # bf16 [H]
+    g_post_ffn: torch.Tensor    # bf16 [H]
+    g_input_ln: torch.Tensor    # bf16 [H]  (the next layer's input_layernorm)
+    g_q: torch.Tensor           # bf16 [D]
+    g_k: torch.Tensor           # bf16 [D]
+    w_gate: torch.Tensor        # bf16 [H, E]
+    gate_bias: torch.Tensor     # fp32 [E]
+    rnope: bool
+
+
+def make_layers(n_layers: int, device: torch.device, seed: int = 4, H: int = wl.HIDDEN,
+                E: int = wl.NUM_EXPERTS, D: int = wl.HEAD_DIM) -> List[LayerWeights]:
+    """Random-init layer weights with the benchmark distributions (gammas 1+N(0,0.02),
+    W_g N(0,0.02), gate bias N(0,0.1)), drawn from one generator on `device`."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    bf = torch.bfloat16
+
+    def gamma(n):
+        return (1.0 + 0.02 * torch.randn(n, generator=g, device=device)).to(bf)
+
+    layers = []
+    for i in range(n_layers):
+        layers.append(LayerWeights(
+            g_post_attn=gamma(H), g_pre_moe=gamma(H), g_post_ffn=gamma(H), g_input_ln=gamma(H),
+            g_q=gamma(D), g_k=gamma(D),
+            w_gate=(0.02 * torch.randn(H, E, generator=g, device=device)).to(bf).contiguous(),
+            gate_bias=(0.1 * torch.randn(E, generator=g, device=device)).contiguous(),
+            rnope=wl.is_rnope_layer(i)))
+    return layers
+
+
+class DecodeChain:
+    """Buffers and launch sequence of the chain for a fixed batch of T tokens."""
+
+    def __init__(self, T: int, layers: List[LayerWeights], device: torch.device,
+                 seed: int = 5, expansion: bool = True, gate_gemm: bool = True,
+                 H: int = wl.HIDDEN, Hq: int = wl.HQ, Hkv: int = wl.HKV, D: int = wl.HEAD_DIM,
+                 E: int = wl.NUM_EXPERTS, K: int = wl.TOP_K, eps: float = wl.EPS,
+                 theta: float = wl.ROPE_THETA):
+        self.T, self.H, self.Hq, self.Hkv, self.D, self.E, self.K = T, H, Hq, Hkv, D, E, K
+        self.eps, self.layers, self.device = float(eps), layers, device
+        self.expansion, self.gate_gemm = expansion, gate_gemm
+        self.lib = _lib.load()
+        g = torch.Generator(device=device).manual_seed(seed)
+        bf = torch.bfloat16
+
+        def rnd(*shape, scale=1.0):
+            return (scale * torch.randn(*shape, generator=g, device=device)).to(bf).contiguous()
+
+        # Synthetic stand-ins for the GEMM outputs, and the residual stream.
+        self.attn_out = rnd(T, H)
+        self.moe_out = rnd(T, H, scale=0.5)
+        self.q = rnd(T, Hq, D)
+        self.k = rnd(T, Hkv, D)
+        self.pos = torch.randint(0, wl.MAX_POSITION, (T,), generator=g, device=device,
+                                 dtype=torch.int32)
+        self.r0 = rnd(T, H)
+        self.r = torch.empty_like(self.r0)
+        self.h = torch.empty_like(self.r0)
+        self.moe_in = torch.empty_like(self.r0)
+        self.nxt = torch.empty_like(self.r0)
+        self.q_out = torch.empty_like(self.q)
+        self.k_out = torch.empty_like(self.k)
+        self.logits_bf = torch.empty(T, E, dtype=bf, device=device)
+        # Without the gate GEMM the router reads fixed logits (non-GEMM-only timing).
+        self.logits = (torch.randn(T, E, generator=g, device=device) if not gate_gemm
+                       else torch.empty(T, E, dtype=torch.float32, device=device))
+        self.ids = torch.empty(T, K, dtype=torch.int32, device=device)
+        self.w = torch.empty(T, K, dtype=torch.float32, device=device)
+        self.counts = torch.empty(E, dtype=torch.int32, device=device)
+        self.offsets = torch.empty(E + 1, dtype=torch.int64, device=device)
+        self.p2u = torch.empty(T * K, dtype=torch.int32, device=device)
+        self.u2p = torch.empty(T * K, dtype=torch.int32, device=device)
+        self.permuted = torch.empty(T * K, H, dtype=bf, device=device) if expansion else None
+        self.ws_bytes = int(self.lib.kb_router_maps_workspace_bytes(T, E, K))
+        self.ws = torch.zeros(max(self.ws_bytes, 256), dtype=torch.uint8, device=device)
+        self.inv_freq = ops.rope_inv_freq(theta, D, device)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+    # ------------------------------------------------------------------------------------
+    def launches_per_layer(self) -> int:
+        """Kernels of this library launched per layer (the cuBLAS GEMM and cast excluded)."""
+        _, launches, _ = self._describe()
+        return 3 + launches + (1 if self.expansion else 0)
+
+    def _describe(self):
+        import ctypes
+        p, n, gsz = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _lib.check(self.lib.kb_maps_describe(self.T, self.E, self.K, 1, _lib.KB_MAPS_AUTO,
+                                             ctypes.byref(p), ctypes.byref(n), ctypes.byref(gsz)),
+                   "kb_maps_describe")
+        return p.value, n.value, gsz.value
+
+    def run_layers(self, stream: torch.cuda.Stream,
+                   record: Optional[Callable[[int, str, dict], None]] = None) -> None:
+        """Enqueue the whole chain on `stream`.  record(i, stage, tensors) is called after
+        each stage with the stage's inputs and outputs (eager runs only)."""
+        lib, T, H, E, K = self.lib, self.T, self.H, self.E, self.K
+        st = stream.cuda_stream
+        bf16 = _lib.KB_BF16
+        with torch.cuda.stream(stream):
+            self.r.copy_(self.r0)
+            for i, L in enumerate(self.layers):
+                if record:
+                    r_in = self.r.clone()
+                _lib.check(lib.kb_residual_norm_pair(
+                    self.attn_out.data_ptr(), self.r.data_ptr(), L.g_post_attn.data_ptr(),
+                    L.g_pre_moe.data_ptr(), self.h.data_ptr(), self.moe_in.data_ptr(), T, H,
+                    self.eps, bf16, st), "kb_residual_norm_pair")
+                if record:
+                    record(i, "sandwich", dict(a=self.attn_out, residual=r_in, g1=L.g_post_attn,
+                                               g2=L.g_pre_moe, sum=self.h, norm=self.moe_in))
+                pos = None if L.rnope else self.pos
+                inv = None if L.rnope else self.inv_freq
+                _lib.check(lib.kb_qk_norm_rope(
+                    self.q.data_ptr(), self.q_out.data_ptr(), self.k.data_ptr(),
+                    self.k_out.data_ptr(), L.g_q.data_ptr(), L.g_k.data_ptr(),
+                    None if pos is None else pos.data_ptr(),
+                    None if inv is None else inv.data_ptr(), T, self.Hq, self.Hkv, self.D,
+                    self.Hq * self.D, self.Hkv * self.D, self.eps, st), "kb_qk_norm_rope")
+                if record:
+                    record(i, "qk", dict(q=self.q, k=self.k, gq=L.g_q, gk=L.g_k, pos=pos,
+                                         q_out=self.q_out, k_out=self.k_out))
+                if self.gate_gemm:
+                    torch.matmul(self.moe_in, L.w_gate, out=self.logits_bf)
+                    self.logits.copy_(self.logits_bf)
+                    if record:
+                        record(i, "gate", dict(x=self.moe_in, w=L.w_gate, logits=self.logits))
+                _lib.check(lib.kb_router_maps(
+                    self.logits.data_ptr(), L.gate_bias.data_ptr(), self.ids.data_ptr(),
+                    self.w.data_ptr(), self.counts.data_ptr(), self.offsets.data_ptr(),
+                    self.p2u.data_ptr(), self.u2p.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
+                    T, E, K, 0, _lib.KB_MAPS_AUTO, st), "kb_router_maps")
+                if record:
+                    record(i, "router_maps", dict(logits=self.logits, bias=L.gate_bias,
+                                                  ids=self.ids, w=self.w, counts=self.counts,
+                                                  offsets=self.offsets, p2u=self.p2u,
+                                                  u2p=self.u2p))
+                if self.expansion:
+                    _lib.check(lib.kb_expand_rows(self.moe_in.data_ptr(),
+                                                  self.permuted.data_ptr(), self.p2u.data_ptr(),
+                                                  T, T * K, H * 2, st), "kb_expand_rows")
+                    if record:
+                        record(i, "expansion", dict(x=self.moe_in, p2u=self.p2u,
+                                                    permuted=self.permuted))
+                if record:
+                    h_in = self.h.clone()
+                _lib.check(lib.kb_residual_norm_pair(
+                    self.moe_out.data_ptr(), self.h.data_ptr(), L.g_post_ffn.data_ptr(),
+                    L.g_input_ln.data_ptr(), self.r.data_ptr(), self.nxt.data_ptr(), T, H,
+                    self.eps, bf16, st), "kb_residual_norm_pair")
+                if record:
+                    record(i, "post_moe", dict(a=self.moe_out, residual=h_in, g1=L.g_post_ffn,
+                                               g2=L.g_input_ln, sum=self.r, norm=self.nxt))
+
+    def capture(self, stream: torch.cuda.Stream) -> torch.cuda.CUDAGraph:
+        """Run the chain once eagerly (library set-up, cuBLAS handles), then record it in one
+        CUDA graph on `stream`."""
+        self.run_layers(stream)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            self.run_layers(stream)
+        self.graph = g
+        return g

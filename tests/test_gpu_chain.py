@@ -1,0 +1,95 @@
+"""The decode chain on the GPU: every stage of every layer checked against the CPU oracle on
+the inputs that stage actually received (the router GEMM is a cuBLAS call, checked to bf16
+rounding; everything after it is checked on its GPU output), for SWA and RNoPE layers, and
+the CUDA-graph replay checked against the eager run."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from kb_testutil import assert_bf16_close, assert_chain_close, np_of
+from kolibri_b200 import decode_chain as dc
+from kolibri_b200 import workloads as wl
+from oracle import kolibri_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _cpu(t):
+    return None if t is None else t.detach().cpu()
+
+
+def make_checker(seen):
+    def check(i, stage, t):
+        c = {k: _cpu(v) for k, v in t.items()}
+        seen.append((i, stage))
+        if stage in ("sandwich", "post_moe"):
+            rs, rn = (orc.sandwich_ref if stage == "sandwich" else orc.post_moe_pre_attn_ref)(
+                c["a"], c["residual"], c["g1"], c["g2"], eps=wl.EPS)
+            inter = F.rms_norm(c["a"], (c["a"].shape[-1],), c["g1"], eps=wl.EPS)
+            assert_chain_close(c["sum"], rs, inter, f"layer {i} {stage} sum")
+            assert_chain_close(c["norm"], rn, inter, f"layer {i} {stage} norm")
+        elif stage == "qk":
+            rq, rk = orc.qk_norm_rope_ref(c["q"], c["k"], c["gq"], c["gk"], c["pos"], eps=wl.EPS)
+            assert_bf16_close(c["q_out"], rq, f"layer {i} q")
+            assert_bf16_close(c["k_out"], rk, f"layer {i} k")
+        elif stage == "gate":
+            ref = orc.router_logits_ref(c["x"].float(), c["w"].float())
+            # cuBLAS accumulates in another order; both round to bf16 before the cast.
+            torch.testing.assert_close(c["logits"], ref, rtol=2.0 ** -7, atol=2e-3)
+            assert torch.equal(c["logits"], c["logits"].to(torch.bfloat16).float())
+        elif stage == "router_maps":
+            rid, rw = orc.router_ref(c["logits"], c["bias"])
+            assert torch.equal(c["ids"], rid), f"layer {i} ids"
+            torch.testing.assert_close(c["w"], rw, rtol=1e-6, atol=0)
+            rc, roff, rp2u, ru2p = orc.expert_maps_ref(rid, wl.NUM_EXPERTS)
+            np.testing.assert_array_equal(np_of(c["counts"]), rc)
+            np.testing.assert_array_equal(np_of(c["offsets"]), roff)
+            np.testing.assert_array_equal(np_of(c["p2u"]), rp2u)
+            np.testing.assert_array_equal(np_of(c["u2p"]), ru2p)
+        elif stage == "expansion":
+            assert torch.equal(c["permuted"], orc.expansion_ref(c["x"], np_of(c["p2u"])))
+    return check
+
+
+@pytest.mark.parametrize("T", [1, 3, 40])
+def test_chain_stages_match_oracle(T):
+    dev = torch.device("cuda")
+    layers = dc.make_layers(5, dev)   # layer 4 is the RNoPE (full-attention) layer
+    assert [L.rnope for L in layers] == [False, False, False, False, True]
+    chain = dc.DecodeChain(T, layers, dev)
+    seen = []
+    chain.run_layers(torch.cuda.current_stream(), record=make_checker(seen))
+    torch.cuda.synchronize()
+    assert len(seen) == 5 * 6
+
+
+def test_chain_graph_replay_matches_eager():
+    dev = torch.device("cuda")
+    layers = dc.make_layers(10, dev)
+    chain = dc.DecodeChain(2, layers, dev)
+    s = torch.cuda.Stream()
+    chain.run_layers(s)
+    torch.cuda.synchronize()
+    eager = [chain.r.clone(), chain.nxt.clone(), chain.ids.clone(), chain.p2u.clone(),
+             chain.permuted.clone()]
+    g = chain.capture(s)
+    chain.r.zero_()
+    chain.ids.zero_()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(eager, [chain.r, chain.nxt, chain.ids, chain.p2u, chain.permuted]):
+        assert torch.equal(a, b)
+
+
+def test_chain_without_gate_gemm():
+    dev = torch.device("cuda")
+    chain = dc.DecodeChain(4, dc.make_layers(5, dev), dev, gate_gemm=False, expansion=False)
+    seen = []
+    chain.run_layers(torch.cuda.current_stream(), record=make_checker(seen))
+    torch.cuda.synchronize()
+    assert len(seen) == 5 * 4
+    assert chain.launches_per_layer() == 4
