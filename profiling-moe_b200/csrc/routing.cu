@@ -506,12 +506,12 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
 struct PersistWs {
     unsigned* bar;   // arrival counter; 0 between calls (the last CTA out resets it)
     int* err;        // non-zero after a barrier wait gave up; the workspace must be re-zeroed
-    int* colhist;    // [E][grid] per-CTA histograms, expert-major
-    int* colpre;     // [E][grid] exclusive prefix over CTAs
-    int* tot;        // [E]
+    int* rowhist;    // [grid][E] per-CTA histograms, CTA-major
+    int* gsum;       // [ceil(grid/kGS)][E] histogram sums of kGS-CTA groups; zero between calls
 };
 
-constexpr int kPW = 8;                    // warps per persistent CTA
+constexpr int kPW = 8;                      // warps per persistent CTA
+constexpr int kGS = 16;                     // CTAs per group of the two-level CTA prefix
 constexpr long long kSpinLimit = 20000000;  // bounded barrier wait (~2 s with nanosleep)
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
@@ -543,78 +543,71 @@ __device__ bool grid_barrier(const PersistWs& ws, unsigned target) {
     return ok != 0;
 }
 
-// Exclusive scan of col[0..n) (n <= 4*blockDim) into pre[]; *total <- sum.
-__device__ void column_scan(const int* col, int* pre, int n, int* total, int* scratch) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nw = blockDim.x >> 5;
-    int v[4];
-    int sum = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int idx = threadIdx.x * 4 + i;
-        v[i] = (idx < n) ? __ldcg(col + idx) : 0;
-        sum += v[i];
-    }
-    const int incl = warp_incl_scan(sum, lane);
-    if (lane == 31) scratch[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        int s = (lane < nw) ? scratch[lane] : 0;
-        s = warp_incl_scan(s, lane);
-        if (lane < nw) scratch[32 + lane] = s;
-    }
-    __syncthreads();
-    int run = incl - sum + ((warp > 0) ? scratch[32 + warp - 1] : 0);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int idx = threadIdx.x * 4 + i;
-        if (idx < n) pre[idx] = run;
-        run += v[i];
-    }
-    if (threadIdx.x == 0) *total = scratch[32 + nw - 1];
-    __syncthreads();
-}
-
-// Phases 2 and 3 of the persistent maps kernels, after this CTA's selections sel[0..n)
-// (tokens t0..) and histogram hist[] are in shared memory.
+// Maps phases of the persistent kernels, after this CTA's selections sel[0..n) (tokens
+// t0..) are in shared memory.
+//   before the barrier  stable ranks inside the CTA (per-warp histograms, exclusive over
+//                       warps) and its histogram: published as row c of rowhist and added
+//                       into the sum of its group of kGS CTAs
+//   one grid barrier
+//   after it            CTA base of expert e = sum of the groups before this CTA's group +
+//                       the rows of the CTAs of its group before it (at most
+//                       ceil(grid/kGS) + kGS - 1 independent L2 reads per expert); expert
+//                       totals = sum of all groups; global offsets; scatter
+// The last CTA out zeroes the group sums and resets the arrival counter.
 __device__ void maps_finish(const PersistWs& ws, int64_t T, int E, int K, int64_t t0, int n,
                             int* sel, int* hist, int* totsm, int* offs, int* scratch, int* whist,
                             int32_t* counts, int64_t* offsets, int32_t* p2u, int32_t* u2p) {
     const int grid = gridDim.x, c = blockIdx.x;
     const int nwarps = blockDim.x >> 5;
+    const int g = c / kGS, ng = (grid + kGS - 1) / kGS;
+    __syncthreads();  // selections complete; the phase-1 buffers aliased by whist are free
+    count_per_warp(sel, n, E, whist);
     __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x) ws.colhist[(size_t)e * grid + c] = hist[e];
+    scan_over_warps(E, whist, hist);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int v = hist[e];
+        __stcg(ws.rowhist + (size_t)c * E + e, v);
+        if (v) atomicAdd(ws.gsum + (size_t)g * E + e, v);
+    }
     if (!grid_barrier(ws, (unsigned)grid)) return;
-
-    // Phase 2: exclusive scan of each expert's column of CTA histograms.
-    for (int e = c; e < E; e += grid)
-        column_scan(ws.colhist + (size_t)e * grid, ws.colpre + (size_t)e * grid, grid,
-                    ws.tot + e, scratch);
-    if (!grid_barrier(ws, 2u * (unsigned)grid)) return;
     pdl_launch();
 
-    // Phase 3: global offsets, this CTA's bases, stable ranks, scatter.
-    for (int e = threadIdx.x; e < E; e += blockDim.x) totsm[e] = __ldcg(ws.tot + e);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int before = 0, total = 0;
+        for (int q = 0; q < ng; ++q) {
+            const int v = __ldcg(ws.gsum + (size_t)q * E + e);
+            total += v;
+            before += (q < g) ? v : 0;
+        }
+        for (int cc = g * kGS; cc < c; ++cc) before += __ldcg(ws.rowhist + (size_t)cc * E + e);
+        hist[e] = before;
+        totsm[e] = total;
+    }
     __syncthreads();
     scan_experts(totsm, E, offs, scratch);
     __syncthreads();
     if (c == 0) write_offsets(offs, totsm, E, T * K, counts, offsets, p2u);
-    count_per_warp(sel, n, E, whist);
-    __syncthreads();
-    scan_over_warps(E, whist, hist);
-    __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const int base = offs[e] + __ldcg(ws.colpre + (size_t)e * grid + c);
+        const int base = offs[e] + hist[e];
         for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += base;
     }
     __syncthreads();
     rank_scatter(sel, n, t0, T, E, K, whist, p2u, u2p);
 
-    // Last CTA out resets the arrival counter for the next call.
+    __shared__ int last;
     __syncthreads();
     if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(ws.bar, 1u);
-        if (prev == 3u * (unsigned)grid - 1u) atomicExch(ws.bar, 0u);
+        __threadfence();
+        last = (atomicAdd(ws.bar, 1u) == 2u * (unsigned)grid - 1u);
+    }
+    __syncthreads();
+    if (last) {
+        for (int i = threadIdx.x; i < ng * E; i += blockDim.x) ws.gsum[i] = 0;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicExch(ws.bar, 0u);
+        }
     }
 }
 
@@ -652,25 +645,19 @@ __global__ void __launch_bounds__(kPW * 32) maps_persistent_kernel(
     const int64_t t0 = (int64_t)c * tpc;
     const int64_t t1 = min(T, t0 + tpc);
     const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
-    __syncthreads();
 
-    // Phase 1: route (or load ids) and histogram this CTA's tokens.
+    // Phase 1: route (or load ids) this CTA's tokens into sel.
     if constexpr (ROUTE) {
         __shared__ int sel_sm[kPW][32];
         float b[VPL];
         load_bias<VPL, VEC>(bias, E, lane, b);
-        const RouteSink<float, true, true> sink{ids_out, w, sel, t0, hist};
+        const RouteSink<float, true, false> sink{ids_out, w, sel, t0, nullptr};
         route_tokens<VPL, VEC, KT>(logits, bias, b, E, K, renorm, t0 + warp, t1, kPW,
                                    VEC ? ring + (size_t)warp * 2 * E : nullptr, sel_sm[warp],
                                    sink);
     } else {
         const int32_t* src = ids_in + t0 * K;
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            const int e = __ldg(src + i);
-            sel[i] = e;
-            if (e >= 0 && e < E) atomicAdd(&hist[e], 1);
-        }
+        for (int i = threadIdx.x; i < n; i += blockDim.x) sel[i] = __ldg(src + i);
     }
     maps_finish(ws, T, E, K, t0, n, sel, hist, totsm, offs, scratch, whist, counts, offsets, p2u,
                 u2p);
@@ -704,7 +691,6 @@ __global__ void __launch_bounds__(256) maps_tpersist_kernel(
     const int64_t t0 = (int64_t)c * tpc;
     const int64_t t1 = min(T, t0 + tpc);
     const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
-    for (int e = threadIdx.x; e < E_; e += blockDim.x) hist[e] = 0;
     troute_setup<E_>(bias, bias_sm);
     float b[E_ / 32];
     load_bias<E_ / 32, true>(bias, E_, lane, b);
@@ -713,9 +699,9 @@ __global__ void __launch_bounds__(256) maps_tpersist_kernel(
     const int64_t tpw = (t1 - t0 + nw - 1) / nw;
     const int64_t tb0 = t0 + warp * tpw;
     const int64_t te = min(t1, tb0 + tpw);
-    troute_range<E_, KT, true, true, float>(logits, b, bias_sm, K, renorm, tb0, te,
-                                            wsm + warp * HW, sel_tmp + warp * 32, ids_out, w, sel,
-                                            t0, hist);
+    troute_range<E_, KT, true, false, float>(logits, b, bias_sm, K, renorm, tb0, te,
+                                             wsm + warp * HW, sel_tmp + warp * 32, ids_out, w,
+                                             sel, t0, nullptr);
     maps_finish(ws, T, E_, K, t0, n, sel, hist, totsm, offs, scratch, whist, counts, offsets, p2u,
                 u2p);
 }
@@ -871,7 +857,7 @@ constexpr int kScatterThreads = 1024;
 constexpr int kTargetSupers = 64;
 constexpr int kMaxSingleSel = 12288;   // single-CTA path: T*K selections held in smem
 constexpr int kMaxPersistSel = 16384;  // persistent path: selections per CTA held in smem
-constexpr int kMaxPersistGrid = 1024;  // column_scan handles up to 4*256 CTAs
+constexpr int kMaxPersistGrid = 1024;  // bounds the workspace (rowhist) and the prefix reads
 constexpr size_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -938,22 +924,32 @@ size_t persist_smem(int tpc, int E, int K, bool route, bool vec) {
     return words * sizeof(int) + std::max(whist, ring);
 }
 
+// Workspace layout shared by every multi-CTA maps path, so that paths, shapes and E can
+// alternate on one buffer.  The zero zone holds zeros between calls (every call restores
+// what it changes in it); the scratch zone behind it is written before it is read.
+//   [0, 256)                     bar, err (persistent kernels)
+//   [kArriveOff, kGsumOff)       arrival counters of the two-kernel super-tiles
+//   [kGsumOff, kScratchOff)      group sums of the persistent kernels ([group][E], E <= E_MAX)
+//   [kScratchOff, ...)           rowhist | tile_counts, super_hist
+constexpr int kMaxSupers = 4096;
+constexpr int kMaxGroups = (kMaxPersistGrid + kGS - 1) / kGS;
+constexpr size_t kArriveOff = 256;
+constexpr size_t kGsumOff = kArriveOff + (size_t)kMaxSupers * sizeof(unsigned);
+constexpr size_t kScratchOff = kGsumOff + (size_t)kMaxGroups * E_MAX * sizeof(int);
+
 size_t persist_ws_bytes(int grid, int E) {
-    return align256(2 * sizeof(int)) + 2 * align256((size_t)E * grid * sizeof(int)) +
-           align256((size_t)E * sizeof(int));
+    return kScratchOff + align256((size_t)E * grid * sizeof(int));
 }
 
 PersistWs carve_persist(void* ws, int grid, int E) {
+    (void)grid;
+    (void)E;
     char* b = static_cast<char*>(ws);
     PersistWs w;
     w.bar = reinterpret_cast<unsigned*>(b);
     w.err = reinterpret_cast<int*>(b + sizeof(int));
-    b += align256(2 * sizeof(int));
-    w.colhist = reinterpret_cast<int*>(b);
-    b += align256((size_t)E * grid * sizeof(int));
-    w.colpre = reinterpret_cast<int*>(b);
-    b += align256((size_t)E * grid * sizeof(int));
-    w.tot = reinterpret_cast<int*>(b);
+    w.gsum = reinterpret_cast<int*>(b + kGsumOff);
+    w.rowhist = reinterpret_cast<int*>(b + kScratchOff);
     return w;
 }
 
@@ -987,15 +983,15 @@ void plan_two_kernel(MapsPlan& p, int64_t T, int E, int K, bool route, bool vec)
 }
 
 size_t two_kernel_ws(const MapsPlan& p, int E) {
-    return align256((size_t)p.S * sizeof(unsigned)) + align256((size_t)p.num_tiles * E * sizeof(int)) +
+    return kScratchOff + align256((size_t)p.num_tiles * E * sizeof(int)) +
            align256((size_t)p.S * E * sizeof(int));
 }
 
 MapsWs carve_two(void* ws, const MapsPlan& p, int E) {
     char* b = static_cast<char*>(ws);
     MapsWs w;
-    w.arrive = reinterpret_cast<unsigned*>(b);
-    b += align256((size_t)p.S * sizeof(unsigned));
+    w.arrive = reinterpret_cast<unsigned*>(b + kArriveOff);
+    b += kScratchOff;
     w.tile_counts = reinterpret_cast<int*>(b);
     b += align256((size_t)p.num_tiles * E * sizeof(int));
     w.super_hist = reinterpret_cast<int*>(b);
@@ -1297,6 +1293,7 @@ struct MapsLaunchT {
             if (p.path == Path::Single) {
                 if (T * K > kMaxSingleSel || p.smem_single > kMaxSmem) return KB_ERR_UNSUPPORTED;
             } else {
+                if (p.path == Path::TwoKernel && p.S > kMaxSupers) return KB_ERR_TOO_LARGE;
                 if (ws == nullptr || ws_bytes < p.ws_bytes) return KB_ERR_WORKSPACE;
                 if (!aligned16(ws)) return KB_ERR_ALIGNMENT;
             }

@@ -94,6 +94,22 @@ def test_maps_repeated_calls_reuse_workspace():
             check_maps(ids, ops.expert_maps(ids.cuda(), 384, mode=mode))
 
 
+def test_maps_workspace_shared_across_paths_and_experts():
+    # One workspace buffer serves every path, T, E and K in turn: what a call leaves in it
+    # must never leak into the next one (zero zone restored, scratch rewritten).
+    g = torch.Generator().manual_seed(3)
+    cases = [(70000, 384, 6, ops.KB_MAPS_MULTI_CTA), (513, 512, 8, ops.KB_MAPS_TWO_KERNEL),
+             (3000, 128, 6, ops.KB_MAPS_MULTI_CTA), (70000, 384, 32, ops.KB_MAPS_TWO_KERNEL),
+             (1, 384, 6, ops.KB_MAPS_MULTI_CTA), (40000, 512, 6, ops.KB_MAPS_MULTI_CTA),
+             (700, 100, 3, ops.KB_MAPS_MULTI_CTA), (70000, 384, 6, ops.KB_MAPS_MULTI_CTA)]
+    for T, E, k, mode in cases:
+        ids = torch.randint(0, E, (T, k), generator=g, dtype=torch.int32)
+        check_maps(ids, ops.expert_maps(ids.cuda(), E, mode=mode), E)
+        logits = torch.randn(min(T, 5000), E, generator=g)
+        ids_r, _, c, off, p2u, u2p = ops.router_maps(logits.cuda(), None, k=min(k, 8), mode=mode)
+        check_maps(ids_r.cpu(), (c, off, p2u, u2p), E)
+
+
 @pytest.mark.parametrize("T", [1, 32, 33, 256, 4096, 65536])
 @pytest.mark.parametrize("mode", MODES)
 def test_router_maps_fused(T, mode):
