@@ -195,6 +195,53 @@ KB_API int kb_residual_norm_pair(const void *a, const void *residual, const void
 KB_API int kb_add_rms_norm(const void *a, const void *b, const void *g, void *out, void *sum_out,
                     int64_t T, int64_t H, float eps, int dtype, kb_stream_t stream);
 
+/* ---------------------------------------------------------------------------------
+ * (a7) The non-GEMM decode chain of n_layers layers in ONE launch, for decode batches
+ * of 1 <= T <= 4 tokens (bf16 activations, head_dim 128, K <= 8, E <= 512, H <= 6144).
+ * Per layer l, in the order of the reference harness's decoder_layer
+ * (benchmarks/11_profile_2block_e2e.py:215-266; layer types of config.json:29-80):
+ *   q_out, k_out  = Q/K RMSNorm + RoPE of q, k (as kb_qk_norm_rope; rnope: no rotation)
+ *   h, moe_in     = sandwich of attn_out and the residual stream (as kb_residual_norm_pair)
+ *   logits        = float(bf16(moe_in @ w_gate_t^T))   (router GEMV, fp32 accumulation)
+ *   ids, weights, counts, offsets, p2u, u2p = router + expert maps of logits (as
+ *                   kb_router_maps with renorm = 0)
+ *   permuted      = expansion of moe_in by p2u (as kb_expand_rows)
+ *   residual, next = post-MoE pair of moe_out and h (as kb_residual_norm_pair)
+ * attn_out, moe_out, q and k are the outputs of the attention / expert GEMMs, which are
+ * outside this library: the same buffers feed every layer.  The residual stream starts as
+ * residual_in and ends in residual_out (which may alias it); h, moe_in, next, q_out, k_out,
+ * logits, ids, weights, maps and permuted hold the last layer's values.  trace_logits
+ * (NULL or fp32 [n_layers, T, E]) receives every layer's logits.  `layers` is a DEVICE
+ * array of n_layers descriptors.  pos == NULL makes every layer RNoPE.
+ * The workspace (kb_decode_chain_workspace_bytes, 16-byte aligned) must be zero-filled
+ * before the first call and is left zero-filled.  The kernel is cooperative (one CTA per
+ * SM): calls must not overlap other work that needs every SM to make progress.
+ * No single counterpart in the reference: it chains the entry points above.
+ */
+typedef struct {
+    const void *g_post_attn;  /* bf16 [H] post-attention RMSNorm weight   */
+    const void *g_pre_moe;    /* bf16 [H] pre-MoE RMSNorm weight           */
+    const void *g_post_ffn;   /* bf16 [H] post-MoE RMSNorm weight          */
+    const void *g_input_ln;   /* bf16 [H] next layer's input RMSNorm weight */
+    const void *g_q;          /* bf16 [128] per-head q norm weight          */
+    const void *g_k;          /* bf16 [128] per-head k norm weight          */
+    const void *w_gate_t;     /* bf16 [E, H] router weight (nn.Linear layout) */
+    const float *gate_bias;   /* fp32 [E] or NULL                           */
+    int32_t rnope;            /* non-zero: full-attention layer, no RoPE    */
+    int32_t reserved;
+} kb_chain_layer_t;
+
+KB_API size_t kb_decode_chain_workspace_bytes(void);
+KB_API int kb_decode_chain(const kb_chain_layer_t *layers, int n_layers, const void *attn_out,
+                           const void *moe_out, const void *q, const void *k,
+                           const int32_t *pos, const float *inv_freq,
+                           const void *residual_in, void *residual_out, void *h, void *moe_in,
+                           void *next, void *q_out, void *k_out, float *logits, int32_t *ids,
+                           float *weights, int32_t *counts, int64_t *offsets, int32_t *p2u,
+                           int32_t *u2p, void *permuted, float *trace_logits, void *workspace,
+                           size_t workspace_bytes, int64_t T, int H, int Hq, int Hkv, int D,
+                           int E, int K, float eps, kb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

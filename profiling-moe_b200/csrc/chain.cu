@@ -1,0 +1,781 @@
+// Decode-chain kernel for sm_100a: every layer of the non-GEMM decode chain of a Kolibri-style
+// MoE decoder in ONE persistent launch, for decode batches of T <= 4 tokens.
+//
+// Per layer, in the order of the reference harness's decoder_layer
+// (benchmarks/11_profile_2block_e2e.py:215-266, with the next layer's input_layernorm
+// :222-227 fused into the post-MoE pair), each stage starting after the previous one ended:
+//   A  Q/K RMSNorm + NeoX RoPE of q, k (RNoPE layers: the norm only)           main CTA
+//   B  sandwich: h = r + RMSNorm(attn_out)*g1 ; moe_in = RMSNorm(h)*g2          main CTA
+//   C  router GEMV: logits[t][e] = float(bf16(moe_in[t] . W[e]))                gate CTAs
+//   D  router (top-K of logits + bias, sigmoid weights) and expert maps         main CTA
+//   E  activation expansion: permuted[r] = moe_in[p2u[r] % T]                    main CTA
+//   F  post-MoE pair: r = h + RMSNorm(moe_out)*g3 ; next = RMSNorm(r)*g4         main CTA
+// The main CTA (block 0) runs every stage but C and keeps r, h and moe_in of its rows in
+// shared memory.  Every other CTA (one per remaining SM) owns up to four experts of the
+// router GEMV: it streams its rows of W for the next layer into shared memory while the main
+// CTA works, waits for the layer's `go` word, computes its logits and counts itself `done`.
+// Those two words are the only cross-CTA synchronisation; every wait is bounded and sets an
+// error word when it gives up.  The arithmetic is that of the stand-alone kernels
+// (norm_math.cuh, route_math.cuh, the Q/K formula of qk_norm_rope.cu), so each stage gives
+// the same bits as its own kernel would on the same inputs.
+#include "kb_common.cuh"
+#include "norm_math.cuh"
+#include "route_math.cuh"
+
+#include <algorithm>
+#include <mutex>
+
+namespace kb {
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int kCT = 512;                     // threads per CTA
+constexpr int kCW = kCT / 32;                // warps per CTA
+constexpr int kPairThreads = 256;            // threads owning row vectors in the norm stages
+constexpr int kMaxGateCtas = 960;            // done words in the workspace
+constexpr int kChainMaxLayers = 256;         // layer descriptors held in shared memory
+constexpr int kChainMaxT = 4;                // tokens per call
+constexpr int kChainMaxK = 8;                // top-K
+constexpr int kGateMaxExperts = 4;           // experts per gate CTA
+constexpr int kHeadChunk = 12;               // heads per warp with loads in flight together
+constexpr int kHalfD = 64;                   // head_dim 128
+constexpr long long kChainSpin = 1LL << 21;  // bounded waits (about a second of polling)
+constexpr int kRedRows = kChainMaxT * kGateMaxExperts;
+
+struct ChainParams {
+    const kb_chain_layer_t* layers;
+    int L, T, H, Hq, Hkv, E, K;
+    float eps;
+    const bf16* attn_out;
+    const bf16* moe_out;
+    const bf16* q;
+    const bf16* k;
+    const int32_t* pos;
+    const float* inv_freq;
+    const bf16* r_in;
+    bf16* r_out;
+    bf16* h;
+    bf16* moe_in;
+    bf16* nxt;
+    bf16* q_out;
+    bf16* k_out;
+    bf16* permuted;
+    float* logits;
+    int32_t* ids;
+    float* w;
+    int32_t* counts;
+    int64_t* offsets;
+    int32_t* p2u;
+    int32_t* u2p;
+    float* trace_logits;
+    unsigned* go;    // layers whose moe_in rows are published; 0 between calls
+    unsigned* done;  // [gate CTAs] layers finished by each gate CTA; 0 between calls
+    int* err;        // non-zero once a wait gave up (the workspace must be re-zeroed)
+};
+
+__device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_rel(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Thread 0 waits until *p >= target.  Gives up (sets err) after kChainSpin polls, or as soon
+// as another CTA has given up.
+__device__ bool wait_geq(const unsigned* p, unsigned target, int* err) {
+    unsigned v = ld_acq(p);
+    long long it = 0;
+    while (v < target) {
+        if (++it > kChainSpin) {
+            atomicExch(err, 1);
+            return false;
+        }
+        if ((it & 1023) == 0 && *(volatile int*)err) return false;
+        __nanosleep(32);
+        v = ld_acq(p);
+    }
+    return true;
+}
+
+// Block-wide sums of n values at once; each value is reduced exactly as block_sum reduces
+// it (warp butterfly, then warp 0 over the warp partials).  red: n*33 floats, which may be
+// reused by the next call without a barrier in between.
+template <int MAXN>
+__device__ __forceinline__ void block_sum_n(float (&v)[MAXN], int n, float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int m = 0; m < MAXN; ++m) {
+        if (m < n) {
+            const float s = warp_sum(v[m]);
+            if (lane == 0) red[m * 33 + warp] = s;
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        for (int m = 0; m < n; ++m) {
+            float s = (lane < nw) ? red[m * 33 + lane] : 0.0f;
+            s = warp_sum(s);
+            if (lane == 0) red[m * 33 + 32] = s;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < MAXN; ++m)
+        if (m < n) v[m] = red[m * 33 + 32];
+    // No trailing barrier: a following reduction on the same buffer writes the partial slots
+    // before its first barrier and the result slot only after it, when every thread has
+    // read this result.
+}
+
+union V8 {
+    uint4 u;
+    bf16 e[8];
+};
+
+template <typename... KArgs, typename... Args>
+int launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+// ------------------------------------------------------------------------------------
+// Main CTA stages.
+// ------------------------------------------------------------------------------------
+struct MainSmem {
+    bf16* r;      // [kChainMaxT][H] residual stream
+    bf16* h;      // [kChainMaxT][H] sandwich sum
+    bf16* x;      // [kChainMaxT][H] moe_in
+    float* cs;    // [kChainMaxT][64]
+    float* sn;    // [kChainMaxT][64]
+    float* red;   // [kRedRows][33]
+    int* hist;    // [E_MAX]
+    int* offs;    // [E_MAX + 4]
+    int* sel;     // [32]
+    int* perm;    // [32]  token of each permuted row
+    int* scratch; // [64]
+    int* flag;    // [4]
+    kb_chain_layer_t* layers;  // [kChainMaxLayers]
+};
+
+__host__ __device__ constexpr size_t main_smem_bytes(int H) {
+    return (size_t)3 * kChainMaxT * H * sizeof(bf16) + 2 * kChainMaxT * kHalfD * sizeof(float) +
+           (size_t)kRedRows * 33 * sizeof(float) + (2 * E_MAX + 4 + 32 + 32 + 64 + 4) * sizeof(int) +
+           (size_t)kChainMaxLayers * sizeof(kb_chain_layer_t);
+}
+__host__ __device__ constexpr size_t gate_smem_bytes(int H) {
+    return (size_t)2 * kGateMaxExperts * H * sizeof(bf16) + (size_t)kRedRows * 33 * sizeof(float) +
+           16;
+}
+
+__device__ MainSmem carve_main(unsigned char* smem, int H) {
+    MainSmem m;
+    m.r = reinterpret_cast<bf16*>(smem);
+    m.h = m.r + (size_t)kChainMaxT * H;
+    m.x = m.h + (size_t)kChainMaxT * H;
+    m.cs = reinterpret_cast<float*>(m.x + (size_t)kChainMaxT * H);
+    m.sn = m.cs + kChainMaxT * kHalfD;
+    m.red = m.sn + kChainMaxT * kHalfD;
+    m.hist = reinterpret_cast<int*>(m.red + kRedRows * 33);
+    m.offs = m.hist + E_MAX;
+    m.sel = m.offs + E_MAX + 4;
+    m.perm = m.sel + 32;
+    m.scratch = m.perm + 32;
+    m.flag = m.scratch + 64;
+    m.layers = reinterpret_cast<kb_chain_layer_t*>(m.flag + 4);
+    return m;
+}
+
+// A: per-head RMSNorm + NeoX RoPE.  Eight lanes per (token, head), 16 elements per lane,
+// four heads per warp.  Lane p of a head holds the elements of lanes 4p..4p+3 of the
+// one-warp-per-head kernel (qk_norm_rope.cu); its butterfly levels 16, 8, 4 become lane
+// exchanges 4, 2, 1 and levels 2, 1 register adds, so the sum of squares, and with it every
+// output, has the same bits.  The NeoX partner of element j (j +- 64) sits in lane p^4.
+constexpr int kQkChunk = 3;  // head groups per warp with loads in flight together
+
+__device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer_t& Ly,
+                                     const MainSmem& s) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = lane >> 3, pl = lane & 7;  // head slot in the warp, lane in the head
+    const int HH = p.Hq + p.Hkv, nh = p.T * HH;
+    const int ngroups = (nh + 3) >> 2;
+    const bool rope = !Ly.rnope && p.pos != nullptr;
+    V8 gq[2], gk[2];
+    gq[0].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_q) + pl * 16));
+    gq[1].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_q) + pl * 16 + 8));
+    gk[0].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_k) + pl * 16));
+    gk[1].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_k) + pl * 16 + 8));
+    for (int g0 = warp; g0 < ngroups; g0 += kCW * kQkChunk) {
+        V8 xv[kQkChunk][2];
+#pragma unroll
+        for (int c = 0; c < kQkChunk; ++c) {  // clamped heads: every load in flight at once
+            const int hd = min((g0 + c * kCW) * 4 + slot, nh - 1);
+            const int t = hd / HH, hh = hd - t * HH;
+            const bf16* src = hh < p.Hq ? p.q + ((size_t)t * p.Hq + hh) * 128
+                                        : p.k + ((size_t)t * p.Hkv + (hh - p.Hq)) * 128;
+            xv[c][0].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 16));
+            xv[c][1].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 16 + 8));
+        }
+#pragma unroll
+        for (int c = 0; c < kQkChunk; ++c) {
+            if (g0 + c * kCW >= ngroups) break;
+            const int hd = (g0 + c * kCW) * 4 + slot;
+            const bool act = hd < nh;
+            const int t = act ? hd / HH : 0, hh = act ? hd - t * HH : 0;
+            const bool is_q = hh < p.Hq;
+            float y[16];
+            float part[4];
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub) {
+                part[sub] = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int k = sub * 4 + i;
+                    y[k] = act ? __bfloat162float(xv[c][k >> 3].e[k & 7]) : 0.0f;
+                    part[sub] = fmaf(y[k], y[k], part[sub]);
+                }
+            }
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+                for (int sub = 0; sub < 4; ++sub)
+                    part[sub] += __shfl_xor_sync(FULL_MASK, part[sub], o);
+            const float l2a = part[0] + part[2], l2b = part[1] + part[3];  // level 2
+            const float ss = l2a + l2b;                                      // level 1
+            const float r = 1.0f / sqrtf(ss / 128.0f + p.eps);
+            const V8* g = is_q ? gq : gk;
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                y[k] = __fmul_rn(__fmul_rn(y[k], r), __bfloat162float(g[k >> 3].e[k & 7]));
+            V8 o[2];
+            if (rope) {
+                const bool first_half = pl < 4;
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const float other = __shfl_xor_sync(FULL_MASK, y[k], 4);
+                    const int j = (pl * 16 + k) & (kHalfD - 1);
+                    const float cc = s.cs[t * kHalfD + j], sv = s.sn[t * kHalfD + j];
+                    const float v = first_half ? __fsub_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv))
+                                               : __fadd_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv));
+                    o[k >> 3].e[k & 7] = __float2bfloat16_rn(v);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 16; ++k) o[k >> 3].e[k & 7] = __float2bfloat16_rn(y[k]);
+            }
+            if (act) {
+                bf16* dst = is_q ? p.q_out + ((size_t)t * p.Hq + hh) * 128
+                                 : p.k_out + ((size_t)t * p.Hkv + (hh - p.Hq)) * 128;
+                reinterpret_cast<uint4*>(dst + pl * 16)[0] = o[0].u;
+                reinterpret_cast<uint4*>(dst + pl * 16)[1] = o[1].u;
+            }
+        }
+    }
+}
+
+// B / F: sum = res + RMSNorm(a)*g1 (rounded) ; norm = RMSNorm(sum)*g2, for the T rows.
+// Threads below kPairThreads own vectors tid + i*kPairThreads, exactly as the stand-alone
+// kernel's 256 threads do; the others add zeros to the reductions, which changes no bit.
+// a comes from global memory (read-only during the launch), res from shared memory.
+// sum goes to sum_sm (and sum_g if non-null), norm to norm_g (and norm_sm if non-null).
+template <int VPT, int TT>
+__device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, const bf16* res_sm,
+                           const bf16* g1, const bf16* g2, bf16* sum_sm, bf16* sum_g,
+                           bf16* norm_g, bf16* norm_sm, float* red) {
+    const int T = p.T, H = p.H, nvec = H / 8;
+    // Threads past kPairThreads own no vector: their index lands past the row.
+    const int tid = threadIdx.x < kPairThreads ? (int)threadIdx.x : nvec;
+    V8 va[TT][VPT];
+    V8 vg1[VPT], vg2[VPT];
+    float ss[TT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {  // weights first: every load of the stage is in flight at once
+        const int v = min(tid + i * kPairThreads, nvec - 1);
+        vg1[i].u = __ldg(reinterpret_cast<const uint4*>(g1) + v);
+        vg2[i].u = __ldg(reinterpret_cast<const uint4*>(g2) + v);
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {  // clamped addresses: every load in flight at once
+        ss[t] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i)
+            va[t][i].u = ld_stream(reinterpret_cast<const uint4*>(a + (size_t)min(t, T - 1) * H) +
+                                   min(tid + i * kPairThreads, nvec - 1));
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t)
+#pragma unroll
+        for (int i = 0; i < VPT; ++i)
+            if (tid + i * kPairThreads >= nvec) va[t][i].u = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        if (t < T) {
+#pragma unroll
+            for (int i = 0; i < VPT; ++i)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float x = __bfloat162float(va[t][i].e[e]);
+                    ss[t] = fmaf(x, x, ss[t]);
+                }
+        }
+    }
+    block_sum_n<TT>(ss, T, red);
+    float ss2[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        ss2[t] = 0.0f;
+        if (t < T) {
+            const float r1 = rms_scale(ss[t], H, p.eps);
+#pragma unroll
+            for (int i = 0; i < VPT; ++i) {
+                const int v = tid + i * kPairThreads;
+                if (v < nvec) {
+                    V8 vr, vh;
+                    const V8& vg = vg1[i];
+                    vr.u = reinterpret_cast<const uint4*>(res_sm + (size_t)t * H)[v];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float post = rnd<bf16>(__fmul_rn(
+                            __fmul_rn(__bfloat162float(va[t][i].e[e]), r1), __bfloat162float(vg.e[e])));
+                        const bf16 hv = __float2bfloat16_rn(__fadd_rn(__bfloat162float(vr.e[e]), post));
+                        vh.e[e] = hv;
+                        const float hf = __bfloat162float(hv);
+                        ss2[t] = fmaf(hf, hf, ss2[t]);
+                    }
+                    va[t][i].u = vh.u;
+                    reinterpret_cast<uint4*>(sum_sm + (size_t)t * H)[v] = vh.u;
+                    if (sum_g) reinterpret_cast<uint4*>(sum_g + (size_t)t * H)[v] = vh.u;
+                }
+            }
+        }
+    }
+    block_sum_n<TT>(ss2, T, red);
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        if (t < T) {
+            const float r2 = rms_scale(ss2[t], H, p.eps);
+#pragma unroll
+            for (int i = 0; i < VPT; ++i) {
+                const int v = tid + i * kPairThreads;
+                if (v < nvec) {
+                    V8 vx;
+                    const V8& vg = vg2[i];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        vx.e[e] = __float2bfloat16_rn(__fmul_rn(
+                            __fmul_rn(__bfloat162float(va[t][i].e[e]), r2), __bfloat162float(vg.e[e])));
+                    reinterpret_cast<uint4*>(norm_g + (size_t)t * H)[v] = vx.u;
+                    if (norm_sm) reinterpret_cast<uint4*>(norm_sm + (size_t)t * H)[v] = vx.u;
+                }
+            }
+        }
+    }
+}
+
+// D: exact top-K per token (warp t routes token t; expert = lane + 32*j), the weights, then
+// the maps of the T*K <= 32 selections.  Same keys and tie rule as the router kernels:
+// score = logit + (bias + 0), ordered by okey (NaN highest), the lower expert index first.
+constexpr int kVPL = E_MAX / 32;  // keys per lane (experts lane + 32*j)
+
+__device__ __noinline__ void stage_route_maps(const ChainParams& p, const float* bias, const MainSmem& s) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int T = p.T, E = p.E, K = p.K, n = T * K;
+    if (warp < T) {
+        const int t = warp;
+        const float* row = p.logits + (size_t)t * E;
+        // All loads first, from clamped addresses, so that they are in flight together.
+        float x[kVPL], b[kVPL];
+#pragma unroll
+        for (int j = 0; j < kVPL; ++j) x[j] = __ldcg(row + min(lane + 32 * j, E - 1));
+        if (bias) {
+#pragma unroll
+            for (int j = 0; j < kVPL; ++j) b[j] = __ldg(bias + min(lane + 32 * j, E - 1)) + 0.0f;
+        } else {
+#pragma unroll
+            for (int j = 0; j < kVPL; ++j) b[j] = 0.0f;
+        }
+        uint32_t key[kVPL];
+#pragma unroll
+        for (int j = 0; j < kVPL; ++j) key[j] = (lane + 32 * j < E) ? okey(x[j] + b[j]) : 0u;
+        for (int r = 0; r < K; ++r) {
+            uint32_t best = 0u;
+            int bj = 0;
+#pragma unroll
+            for (int j = 0; j < kVPL; ++j)
+                if (key[j] > best) {
+                    best = key[j];
+                    bj = j;
+                }
+            const uint32_t wmax = __reduce_max_sync(FULL_MASK, best);
+            const unsigned cand = (best == wmax && best != 0u) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
+            const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
+            if (cand == widx) {
+#pragma unroll
+                for (int j = 0; j < kVPL; ++j)
+                    if (j == bj) key[j] = 0u;
+            }
+            if (lane == 0) s.sel[t * K + r] = (int)widx;
+        }
+        __syncwarp();
+        if (lane < K) {
+            const int id = s.sel[t * K + lane];
+            p.ids[t * K + lane] = id;
+            p.w[t * K + lane] = sigmoid_acc(__ldcg(row + id));
+        }
+    }
+    __syncthreads();
+    // Maps of n <= 32 selections without a scan: offsets[e] = selections below e,
+    // counts[e] = selections equal to e, rank of selection i = selections below its expert
+    // + equal ones before it (selections are in (token, slot) order).
+    for (int e = threadIdx.x; e <= E; e += kCT) {
+        int below = 0, equal = 0;
+        for (int i = 0; i < n; ++i) {
+            const int v = s.sel[i];
+            below += (v < e) ? 1 : 0;
+            equal += (v == e) ? 1 : 0;
+        }
+        p.offsets[e] = (int64_t)below;
+        if (p.counts && e < E) p.counts[e] = equal;
+    }
+    if (warp == 0) {
+        const int e = (lane < n) ? s.sel[lane] : 0x7fffffff;
+        int rank = 0;
+        for (int i = 0; i < n; ++i) {
+            const int v = s.sel[i];
+            rank += (v < e || (v == e && i < lane)) ? 1 : 0;
+        }
+        if (lane < n) {
+            const int tok = lane / K, slot = lane - tok * K;
+            const int u = slot * T + tok;
+            p.p2u[rank] = u;
+            if (p.u2p) p.u2p[u] = rank;
+            s.perm[rank] = tok;
+        }
+    }
+    __syncthreads();
+}
+
+// E: permuted rows straight from the moe_in rows held in shared memory.
+__device__ __noinline__ void stage_expand(const ChainParams& p, const MainSmem& s) {
+    const int nvec = p.H / 8, n = p.T * p.K;
+    for (int r = 0; r < n; ++r) {
+        const uint4* src = reinterpret_cast<const uint4*>(s.x + (size_t)s.perm[r] * p.H);
+        uint4* dst = reinterpret_cast<uint4*>(p.permuted + (size_t)r * p.H);
+        for (int v = threadIdx.x; v < nvec; v += kCT) st_stream(dst + v, src[v]);
+    }
+}
+
+template <int VPT, int TT>
+__device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* smem) {
+    const int T = p.T, H = p.H, nvec = H / 8;
+    const MainSmem s = carve_main(smem, H);
+    const unsigned gate_ctas = gridDim.x - 1;
+    {  // every layer descriptor into shared memory once
+        const int words = p.L * (int)(sizeof(kb_chain_layer_t) / sizeof(int));
+        for (int i = threadIdx.x; i < words; i += kCT)
+            reinterpret_cast<int*>(s.layers)[i] = reinterpret_cast<const int*>(p.layers)[i];
+    }
+    for (int i = threadIdx.x; i < T * nvec; i += kCT) {
+        const int t = i / nvec, v = i - t * nvec;
+        reinterpret_cast<uint4*>(s.r + (size_t)t * H)[v] =
+            reinterpret_cast<const uint4*>(p.r_in + (size_t)t * H)[v];
+    }
+    if (p.pos) {
+        for (int i = threadIdx.x; i < T * kHalfD; i += kCT) {
+            const int t = i / kHalfD, j = i - t * kHalfD;
+            float sv, cv;
+            sincosf(__fmul_rn((float)__ldg(p.pos + t), __ldg(p.inv_freq + j)), &sv, &cv);
+            s.cs[i] = cv;
+            s.sn[i] = sv;
+        }
+    }
+    __syncthreads();
+    for (int l = 0; l < p.L; ++l) {
+        const kb_chain_layer_t& Ly = s.layers[l];
+        if (l + 1 < p.L) {  // the next layer's small weights into L2
+            const kb_chain_layer_t& Ln = s.layers[l + 1];
+            const char* bases[4] = {static_cast<const char*>(Ln.g_post_attn),
+                                    static_cast<const char*>(Ln.g_pre_moe),
+                                    static_cast<const char*>(Ln.g_post_ffn),
+                                    static_cast<const char*>(Ln.g_input_ln)};
+            const int lines = (H * 2 + 127) / 128;
+            for (int i = threadIdx.x; i < 4 * lines; i += kCT)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(bases[i / lines] + (size_t)(i % lines) * 128));
+        }
+        stage_qk(p, Ly, s);
+        __syncthreads();
+        stage_pair<VPT, TT>(p, p.attn_out, s.r, static_cast<const bf16*>(Ly.g_post_attn),
+                        static_cast<const bf16*>(Ly.g_pre_moe), s.h, p.h, p.moe_in, s.x, s.red);
+        __syncthreads();
+        if (threadIdx.x == 0) {  // the barrier above orders every thread's rows before it
+            s.flag[0] = 1;
+            st_rel(p.go, (unsigned)(l + 1));
+        }
+        __syncthreads();
+        // Every gate CTA has its own done word; one thread waits on each, all at once.
+        for (unsigned c = threadIdx.x; c < gate_ctas; c += kCT)
+            if (!wait_geq(p.done + c, (unsigned)(l + 1), p.err)) s.flag[0] = 0;
+        __syncthreads();
+        if (!s.flag[0]) {
+            for (int e = threadIdx.x; e <= p.E; e += kCT) p.offsets[e] = -1;
+            return;
+        }
+        stage_route_maps(p, Ly.gate_bias, s);
+        stage_expand(p, s);
+        stage_pair<VPT, TT>(p, p.moe_out, s.h, static_cast<const bf16*>(Ly.g_post_ffn),
+                        static_cast<const bf16*>(Ly.g_input_ln), s.r, p.r_out, p.nxt, nullptr,
+                        s.red);
+        __syncthreads();
+    }
+    // Every gate CTA has passed its last wait: the words can return to zero.
+    for (unsigned c = threadIdx.x; c < gate_ctas; c += kCT) p.done[c] = 0u;
+    if (threadIdx.x == 0) *p.go = 0u;
+}
+
+// ------------------------------------------------------------------------------------
+// Gate CTAs: router GEMV for experts j, j + G1, ... (G1 = gate CTAs).
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+    const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int VPTG, int TT>
+__device__ __noinline__ void chain_gate(const ChainParams& p, unsigned char* smem) {
+    const int G1 = gridDim.x - 1, j = blockIdx.x - 1;
+    const int H = p.H, E = p.E, T = p.T, nvec = H / 8;
+    bf16* wb = reinterpret_cast<bf16*>(smem);  // [2][kGateMaxExperts][H]
+    float* red = reinterpret_cast<float*>(wb + (size_t)2 * kGateMaxExperts * H);
+    __shared__ int ok;
+    int ex[kGateMaxExperts];
+    int ne = 0;
+#pragma unroll
+    for (int m = 0; m < kGateMaxExperts; ++m) {
+        const int e = j + m * G1;
+        ex[m] = e;
+        if (e < E) ne = m + 1;
+    }
+    auto issue = [&](int l) {
+        const bf16* W = static_cast<const bf16*>(p.layers[l].w_gate_t);
+        bf16* dst = wb + (size_t)(l & 1) * kGateMaxExperts * H;
+        for (int m = 0; m < ne; ++m)
+            for (int v = threadIdx.x; v < nvec; v += kCT)
+                cp16(dst + (size_t)m * H + v * 8, W + (size_t)ex[m] * H + v * 8);
+        cp_commit();
+    };
+    issue(0);
+    for (int l = 0; l < p.L; ++l) {
+        if (l + 1 < p.L) issue(l + 1);
+        else cp_commit();
+        if (threadIdx.x == 0) ok = wait_geq(p.go, (unsigned)(l + 1), p.err) ? 1 : 0;
+        cp_wait<1>();
+        __syncthreads();
+        if (!ok) {
+            cp_wait<0>();
+            return;
+        }
+        const bf16* wl = wb + (size_t)(l & 1) * kGateMaxExperts * H;
+        float acc[TT * kGateMaxExperts];
+#pragma unroll
+        for (int i = 0; i < TT * kGateMaxExperts; ++i) acc[i] = 0.0f;
+        // Every moe_in vector of this thread first (clamped rows and vectors, all in flight
+        // together), then the products; rows t >= T and vectors past H count as zero.
+        V8 xv[TT][VPTG];
+#pragma unroll
+        for (int t = 0; t < TT; ++t)
+#pragma unroll
+            for (int i = 0; i < VPTG; ++i)
+                xv[t][i].u = __ldcg(reinterpret_cast<const uint4*>(p.moe_in + (size_t)min(t, T - 1) * H) +
+                                    min((int)threadIdx.x + i * kCT, nvec - 1));
+#pragma unroll
+        for (int i = 0; i < VPTG; ++i) {
+            const int v = threadIdx.x + i * kCT;
+            const bool vin = v < nvec;
+#pragma unroll
+            for (int m = 0; m < kGateMaxExperts; ++m) {
+                if (m < ne) {
+                    V8 wv;
+                    wv.u = reinterpret_cast<const uint4*>(wl + (size_t)m * H)[vin ? v : 0];
+#pragma unroll
+                    for (int t = 0; t < TT; ++t) {
+                        if (t < T && vin) {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e)
+                                acc[t * kGateMaxExperts + m] =
+                                    fmaf(__bfloat162float(xv[t][i].e[e]), __bfloat162float(wv.e[e]),
+                                         acc[t * kGateMaxExperts + m]);
+                        }
+                    }
+                }
+            }
+        }
+        block_sum_n<TT * kGateMaxExperts>(acc, T * kGateMaxExperts, red);
+#pragma unroll
+        for (int t = 0; t < TT; ++t)
+#pragma unroll
+            for (int m = 0; m < kGateMaxExperts; ++m)
+                if (threadIdx.x == t * kGateMaxExperts + m && t < T && m < ne) {
+                    const float v = __bfloat162float(__float2bfloat16_rn(acc[t * kGateMaxExperts + m]));
+                    p.logits[(size_t)t * E + ex[m]] = v;
+                    if (p.trace_logits) p.trace_logits[((size_t)l * T + t) * E + ex[m]] = v;
+                }
+        __syncthreads();
+        if (threadIdx.x == 0) st_rel(p.done + j, (unsigned)(l + 1));  // after the barrier above
+    }
+}
+
+template <int VPT, int TT>
+__global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_constant__ ChainParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    if (*(volatile int*)p.err) {  // an earlier call gave up: report and do nothing
+        if (blockIdx.x == 0)
+            for (int e = threadIdx.x; e <= p.E; e += kCT) p.offsets[e] = -1;
+        return;
+    }
+    // The stages read the parameters from a shared-memory copy (short, fixed latency).
+    __shared__ ChainParams ps;
+    constexpr int kWords = (int)(sizeof(ChainParams) / sizeof(int));
+    static_assert(sizeof(ChainParams) % sizeof(int) == 0, "ChainParams copy");
+    for (int i = threadIdx.x; i < kWords; i += kCT)
+        reinterpret_cast<int*>(&ps)[i] = reinterpret_cast<const int*>(&p)[i];
+    __syncthreads();
+    if (blockIdx.x == 0) chain_main<VPT, TT>(ps, smem);
+    else chain_gate<(VPT * kPairThreads + kCT - 1) / kCT, TT>(ps, smem);
+}
+
+// ------------------------------------------------------------------------------------
+// Host
+// ------------------------------------------------------------------------------------
+template <int VPT, int TT>
+int run_chain(const ChainParams& prm, size_t smem, int grid, cudaStream_t st) {
+    auto* kern = decode_chain_kernel<VPT, TT>;
+    int err = allow_smem(kern, smem);
+    if (err) return err;
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kCT, smem) != cudaSuccess || nb < 1)
+        return KB_ERR_UNSUPPORTED;
+    return launch_coop(kern, dim3((unsigned)grid), dim3(kCT), smem, st, prm);
+}
+
+template <int VPT>
+int run_tokens(int T, const ChainParams& prm, size_t smem, int grid, cudaStream_t st) {
+    switch (T) {
+        case 1: return run_chain<VPT, 1>(prm, smem, grid, st);
+        case 2: return run_chain<VPT, 2>(prm, smem, grid, st);
+        case 3: return run_chain<VPT, 3>(prm, smem, grid, st);
+        case 4: return run_chain<VPT, 4>(prm, smem, grid, st);
+        default: return KB_ERR_UNSUPPORTED;
+    }
+}
+
+int sm_count() {
+    static std::mutex mu;
+    static int cache[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    int& v = cache[dev & 63];
+    if (v == 0) {
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        if (v <= 0) v = 148;
+    }
+    return v;
+}
+
+}  // namespace
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" size_t kb_decode_chain_workspace_bytes(void) { return 256 + 4 * kMaxGateCtas; }
+
+extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, const void* attn_out,
+                               const void* moe_out, const void* q, const void* k,
+                               const int32_t* pos, const float* inv_freq,
+                               const void* residual_in, void* residual_out, void* h,
+                               void* moe_in, void* next, void* q_out, void* k_out, float* logits,
+                               int32_t* ids, float* weights, int32_t* counts, int64_t* offsets,
+                               int32_t* p2u, int32_t* u2p, void* permuted, float* trace_logits,
+                               void* workspace, size_t workspace_bytes, int64_t T, int H,
+                               int Hq, int Hkv, int D, int E, int K, float eps,
+                               kb_stream_t stream) {
+    if (n_layers > kChainMaxLayers) return KB_ERR_UNSUPPORTED;
+    if (T < 1 || n_layers < 1 || H <= 0 || Hq < 0 || Hkv < 0 || E <= 0 || K <= 0)
+        return KB_ERR_INVALID_ARG;
+    if (T > kChainMaxT || D != 128 || H % 8 != 0 || H / 8 > 3 * kPairThreads || E > E_MAX ||
+        K > kChainMaxK || K > E || Hq + Hkv <= 0)
+        return KB_ERR_UNSUPPORTED;
+    if (!layers || !attn_out || !moe_out || !q || !k || !residual_in || !residual_out || !h ||
+        !moe_in || !next || !q_out || !k_out || !logits || !ids || !weights || !offsets ||
+        !p2u || !permuted || (pos && !inv_freq))
+        return KB_ERR_INVALID_ARG;
+    if (!workspace || workspace_bytes < kb_decode_chain_workspace_bytes()) return KB_ERR_WORKSPACE;
+    const void* vec_ptrs[] = {attn_out, moe_out, q, k, residual_in, residual_out, h, moe_in,
+                              next, q_out, k_out, permuted, workspace};
+    for (const void* v : vec_ptrs)
+        if (!aligned16(v)) return KB_ERR_ALIGNMENT;
+    const int sms = sm_count();
+    const int gate = std::min(std::min(sms - 1, E), kMaxGateCtas);
+    if (gate < 1 || (int64_t)gate * kGateMaxExperts < E) return KB_ERR_UNSUPPORTED;
+    ChainParams prm;
+    prm.layers = layers;
+    prm.L = n_layers;
+    prm.T = (int)T;
+    prm.H = H;
+    prm.Hq = Hq;
+    prm.Hkv = Hkv;
+    prm.E = E;
+    prm.K = K;
+    prm.eps = eps;
+    prm.attn_out = static_cast<const bf16*>(attn_out);
+    prm.moe_out = static_cast<const bf16*>(moe_out);
+    prm.q = static_cast<const bf16*>(q);
+    prm.k = static_cast<const bf16*>(k);
+    prm.pos = pos;
+    prm.inv_freq = inv_freq;
+    prm.r_in = static_cast<const bf16*>(residual_in);
+    prm.r_out = static_cast<bf16*>(residual_out);
+    prm.h = static_cast<bf16*>(h);
+    prm.moe_in = static_cast<bf16*>(moe_in);
+    prm.nxt = static_cast<bf16*>(next);
+    prm.q_out = static_cast<bf16*>(q_out);
+    prm.k_out = static_cast<bf16*>(k_out);
+    prm.permuted = static_cast<bf16*>(permuted);
+    prm.logits = logits;
+    prm.ids = ids;
+    prm.w = weights;
+    prm.counts = counts;
+    prm.offsets = offsets;
+    prm.p2u = p2u;
+    prm.u2p = u2p;
+    prm.trace_logits = trace_logits;
+    unsigned char* wsb = static_cast<unsigned char*>(workspace);
+    prm.go = reinterpret_cast<unsigned*>(wsb);
+    prm.err = reinterpret_cast<int*>(wsb + 128);
+    prm.done = reinterpret_cast<unsigned*>(wsb + 256);
+    const size_t smem = std::max(main_smem_bytes(H), gate_smem_bytes(H));
+    const int vpt = (H / 8 + kPairThreads - 1) / kPairThreads;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (vpt) {
+        case 1: return run_tokens<1>((int)T, prm, smem, 1 + gate, st);
+        case 2: return run_tokens<2>((int)T, prm, smem, 1 + gate, st);
+        case 3: return run_tokens<3>((int)T, prm, smem, 1 + gate, st);
+        default: return KB_ERR_UNSUPPORTED;
+    }
+}

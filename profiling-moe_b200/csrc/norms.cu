@@ -12,35 +12,11 @@
 // rounded to the activation dtype, and the second norm reads the rounded sum.  Products use
 // __fmul_rn so that no FMA contraction changes the rounding.
 #include "kb_common.cuh"
+#include "norm_math.cuh"
 
 #include <algorithm>
 
 namespace kb {
-
-// Block-wide fp32 sum; `red` is a 33-float smem scratch.  All threads get the result.
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nw = (blockDim.x + 31) >> 5;
-    v = warp_sum(v);
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        float s = (lane < nw) ? red[lane] : 0.0f;
-        s = warp_sum(s);
-        if (lane == 0) red[32] = s;
-    }
-    __syncthreads();
-    const float r = red[32];
-    __syncthreads();  // red is reused by the next reduction
-    return r;
-}
-
-__device__ __forceinline__ float rms_scale(float ss, int H, float eps) {
-    return 1.0f / sqrtf(ss / (float)H + eps);
-}
-
-template <typename T>
-__device__ __forceinline__ float rnd(float v) { return Elem<T>::to_f(Elem<T>::from_f(v)); }
 
 // ------------------------------------------------------------------------------------
 // Register kernels: each thread owns VPT 16-byte vectors v = tid + i*blockDim.

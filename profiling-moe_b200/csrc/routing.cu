@@ -27,6 +27,7 @@
 //    histograms, last-arriving CTA folds super-tiles, one CTA per super-tile scatters) remains
 //    as the path for shapes the persistent kernel cannot hold.
 #include "kb_common.cuh"
+#include "route_math.cuh"
 
 #include <algorithm>
 #include <math.h>
@@ -35,22 +36,6 @@
 #include <tuple>
 
 namespace kb {
-
-// ------------------------------------------------------------------------------------
-// Ordering keys.  okey: a larger float gives a larger key, NaN the largest (torch.sort puts
-// NaN first in a descending sort), -0 and +0 share a key; key 0 marks "taken".
-// fkey: the same map for values known to be neither NaN nor -0.
-// ------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t okey(float s) {
-    uint32_t u = __float_as_uint(s);
-    if (u == 0x80000000u) u = 0u;
-    uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return (s != s) ? 0xffffffffu : k;
-}
-__device__ __forceinline__ uint32_t fkey(float s) {
-    const uint32_t u = __float_as_uint(s);
-    return u ^ ((uint32_t)((int32_t)u >> 31) | 0x80000000u);
-}
 
 __device__ __forceinline__ float fmax_nan(float a, float b) {
     float r;
@@ -201,7 +186,6 @@ __device__ __forceinline__ bool route_fast(const float (&s)[VPL], int K_rt, int 
     return true;
 }
 
-__device__ __forceinline__ float sigmoid_acc(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 // Lane r < K holds pick r: weight = sigmoid(raw logit); optional renorm over the K picks.
 __device__ __forceinline__ float pick_weight(float x, int K, int lane, int renorm) {
@@ -512,7 +496,7 @@ struct PersistWs {
 
 constexpr int kPW = 8;                      // warps per persistent CTA
 constexpr int kGS = 16;                     // CTAs per group of the two-level CTA prefix
-constexpr long long kSpinLimit = 20000000;  // bounded barrier wait (~2 s with nanosleep)
+constexpr long long kSpinLimit = 2000000;   // bounded barrier wait (about a second of polling)
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     unsigned v;

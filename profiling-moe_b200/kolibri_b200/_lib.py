@@ -50,7 +50,18 @@ SIGNATURES = {
                                       c_void_p, c_int64, c_int64, c_float, c_int, c_void_p]),
     "kb_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                 c_int64, c_float, c_int, c_void_p]),
+    "kb_decode_chain_workspace_bytes": (c_size_t, []),
+    "kb_decode_chain": (c_int, [c_void_p, c_int] + [c_void_p] * 22 + [c_void_p, c_size_t, c_int64,
+                                c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p]),
 }
+
+
+class ChainLayer(ctypes.Structure):
+    """kb_chain_layer_t: one layer's weights for kb_decode_chain (device pointers)."""
+    _fields_ = [("g_post_attn", c_void_p), ("g_pre_moe", c_void_p), ("g_post_ffn", c_void_p),
+                ("g_input_ln", c_void_p), ("g_q", c_void_p), ("g_k", c_void_p),
+                ("w_gate_t", c_void_p), ("gate_bias", c_void_p), ("rnope", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 class KolibriError(RuntimeError):

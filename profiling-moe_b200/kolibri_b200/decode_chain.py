@@ -44,7 +44,7 @@ class LayerWeights:
     g_input_ln: torch.Tensor    # bf16 [H]  (the next layer's input_layernorm)
     g_q: torch.Tensor           # bf16 [D]
     g_k: torch.Tensor           # bf16 [D]
-    w_gate: torch.Tensor        # bf16 [H, E]
+    w_gate_t: torch.Tensor      # bf16 [E, H] (nn.Linear layout: logits = x @ w_gate_t.T)
     gate_bias: torch.Tensor     # fp32 [E]
     rnope: bool
 
@@ -52,7 +52,7 @@ class LayerWeights:
 def make_layers(n_layers: int, device: torch.device, seed: int = 4, H: int = wl.HIDDEN,
                 E: int = wl.NUM_EXPERTS, D: int = wl.HEAD_DIM) -> List[LayerWeights]:
     """Random-init layer weights with the benchmark distributions (gammas 1+N(0,0.02),
-    W_g N(0,0.02), gate bias N(0,0.1)), drawn from one generator on `device`."""
+    W_g N(0,0.02) stored [E, H], gate bias N(0,0.1)), drawn from one generator on `device`."""
     g = torch.Generator(device=device).manual_seed(seed)
     bf = torch.bfloat16
 
@@ -64,7 +64,7 @@ def make_layers(n_layers: int, device: torch.device, seed: int = 4, H: int = wl.
         layers.append(LayerWeights(
             g_post_attn=gamma(H), g_pre_moe=gamma(H), g_post_ffn=gamma(H), g_input_ln=gamma(H),
             g_q=gamma(D), g_k=gamma(D),
-            w_gate=(0.02 * torch.randn(H, E, generator=g, device=device)).to(bf).contiguous(),
+            w_gate_t=(0.02 * torch.randn(E, H, generator=g, device=device)).to(bf).contiguous(),
             gate_bias=(0.1 * torch.randn(E, generator=g, device=device)).contiguous(),
             rnope=wl.is_rnope_layer(i)))
     return layers
@@ -163,10 +163,10 @@ class DecodeChain:
                     record(i, "qk", dict(q=self.q, k=self.k, gq=L.g_q, gk=L.g_k, pos=pos,
                                          q_out=self.q_out, k_out=self.k_out))
                 if self.gate_gemm:
-                    torch.matmul(self.moe_in, L.w_gate, out=self.logits_bf)
+                    torch.matmul(self.moe_in, L.w_gate_t.t(), out=self.logits_bf)
                     self.logits.copy_(self.logits_bf)
                     if record:
-                        record(i, "gate", dict(x=self.moe_in, w=L.w_gate, logits=self.logits))
+                        record(i, "gate", dict(x=self.moe_in, w=L.w_gate_t.t(), logits=self.logits))
                 _lib.check(lib.kb_router_maps(
                     self.logits.data_ptr(), L.gate_bias.data_ptr(), self.ids.data_ptr(),
                     self.w.data_ptr(), self.counts.data_ptr(), self.offsets.data_ptr(),
@@ -193,6 +193,46 @@ class DecodeChain:
                 if record:
                     record(i, "post_moe", dict(a=self.moe_out, residual=h_in, g1=L.g_post_ffn,
                                                g2=L.g_input_ln, sum=self.r, norm=self.nxt))
+
+    # ------------------------------------------------------------------------------------
+    # The whole chain in one launch (kb_decode_chain), for T <= 4.
+    # ------------------------------------------------------------------------------------
+    MEGA_MAX_T = 4
+
+    def _mega_setup(self):
+        if getattr(self, "_mega", None) is not None:
+            return self._mega
+        import ctypes
+        descs = (_lib.ChainLayer * len(self.layers))()
+        for i, L in enumerate(self.layers):
+            descs[i] = _lib.ChainLayer(
+                L.g_post_attn.data_ptr(), L.g_pre_moe.data_ptr(), L.g_post_ffn.data_ptr(),
+                L.g_input_ln.data_ptr(), L.g_q.data_ptr(), L.g_k.data_ptr(),
+                L.w_gate_t.data_ptr(), L.gate_bias.data_ptr(), int(L.rnope), 0)
+        raw = torch.frombuffer(bytearray(ctypes.string_at(descs, ctypes.sizeof(descs))),
+                               dtype=torch.uint8)
+        dev_descs = raw.to(self.device)
+        ws = torch.zeros(int(self.lib.kb_decode_chain_workspace_bytes()), dtype=torch.uint8,
+                         device=self.device)
+        self._mega = (dev_descs, ws)
+        return self._mega
+
+    def run_mega(self, stream: torch.cuda.Stream, trace: Optional[torch.Tensor] = None) -> None:
+        """Enqueue the whole chain as one kb_decode_chain launch on `stream` (T <= 4).
+        trace: optional fp32 [layers, T, E] receiving every layer's logits."""
+        if self.T > self.MEGA_MAX_T:
+            raise ValueError(f"kb_decode_chain takes at most {self.MEGA_MAX_T} tokens")
+        descs, ws = self._mega_setup()
+        P = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        with torch.cuda.stream(stream):
+            _lib.check(self.lib.kb_decode_chain(
+                descs.data_ptr(), len(self.layers), P(self.attn_out), P(self.moe_out), P(self.q),
+                P(self.k), P(self.pos), P(self.inv_freq), P(self.r0), P(self.r), P(self.h),
+                P(self.moe_in), P(self.nxt), P(self.q_out), P(self.k_out), P(self.logits),
+                P(self.ids), P(self.w), P(self.counts), P(self.offsets), P(self.p2u), P(self.u2p),
+                P(self.permuted), P(trace), ws.data_ptr(), ws.numel(), self.T, self.H, self.Hq,
+                self.Hkv, self.D, self.E, self.K, self.eps, stream.cuda_stream),
+                "kb_decode_chain")
 
     def capture(self, stream: torch.cuda.Stream) -> torch.cuda.CUDAGraph:
         """Run the chain once eagerly (library set-up, cuBLAS handles), then record it in one

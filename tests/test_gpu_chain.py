@@ -93,3 +93,55 @@ def test_chain_without_gate_gemm():
     torch.cuda.synchronize()
     assert len(seen) == 5 * 4
     assert chain.launches_per_layer() == 4
+
+
+@pytest.mark.parametrize("T", [1, 2, 4])
+def test_decode_chain_kernel_matches_stages(T):
+    """kb_decode_chain (one launch for all layers) against the stage-by-stage path: the
+    routing-independent state is bit-identical, every layer's logits agree with cuBLAS to
+    bf16 rounding and with the CPU oracle, and the last layer's router, maps and expansion
+    match the oracle on the kernel's own logits."""
+    dev = torch.device("cuda")
+    layers = dc.make_layers(5, dev)
+    chain = dc.DecodeChain(T, layers, dev)
+    s = torch.cuda.Stream()
+    ref_logits = []
+
+    def keep(i, stage, t):
+        if stage == "gate":
+            ref_logits.append((t["x"].detach().cpu(), t["logits"].detach().cpu()))
+    chain.run_layers(s, record=keep)
+    torch.cuda.synchronize()
+    ref = {n: getattr(chain, n).clone() for n in ("r", "nxt", "h", "moe_in", "q_out", "k_out")}
+    for n in ("r", "nxt", "h", "moe_in", "q_out", "k_out", "ids", "logits", "p2u"):
+        getattr(chain, n).zero_()
+    trace = torch.full((5, T, wl.NUM_EXPERTS), float("nan"), device=dev)
+    chain.run_mega(s, trace=trace)
+    chain.run_mega(s)            # a second call on the same workspace
+    torch.cuda.synchronize()
+    for n, v in ref.items():
+        assert torch.equal(getattr(chain, n), v), n
+    tr = trace.cpu()
+    for i, (x, lg) in enumerate(ref_logits):
+        assert torch.equal(tr[i], tr[i].to(torch.bfloat16).float())
+        torch.testing.assert_close(tr[i], lg, rtol=2.0 ** -7, atol=2e-3)
+        ref_cpu = orc.router_logits_ref(x.float(), layers[i].w_gate_t.t().float().cpu())
+        torch.testing.assert_close(tr[i], ref_cpu, rtol=2.0 ** -7, atol=2e-3)
+    last = tr[-1]
+    assert torch.equal(chain.logits.cpu(), last)
+    rid, rw = orc.router_ref(last, layers[-1].gate_bias.cpu())
+    assert torch.equal(chain.ids.cpu(), rid)
+    torch.testing.assert_close(chain.w.cpu(), rw, rtol=1e-6, atol=0)
+    rc, roff, rp2u, ru2p = orc.expert_maps_ref(rid, wl.NUM_EXPERTS)
+    np.testing.assert_array_equal(np_of(chain.counts), rc)
+    np.testing.assert_array_equal(np_of(chain.offsets), roff)
+    np.testing.assert_array_equal(np_of(chain.p2u), rp2u)
+    np.testing.assert_array_equal(np_of(chain.u2p), ru2p)
+    assert torch.equal(chain.permuted.cpu(), orc.expansion_ref(chain.moe_in.cpu(), rp2u))
+
+
+def test_decode_chain_kernel_rejects_large_batches():
+    dev = torch.device("cuda")
+    chain = dc.DecodeChain(5, dc.make_layers(1, dev), dev)
+    with pytest.raises(ValueError):
+        chain.run_mega(torch.cuda.current_stream())
