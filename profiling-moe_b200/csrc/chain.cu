@@ -32,13 +32,12 @@ using bf16 = __nv_bfloat16;
 
 constexpr int kCT = 512;                     // threads per CTA
 constexpr int kCW = kCT / 32;                // warps per CTA
-constexpr int kPairThreads = 256;            // threads owning row vectors in the norm stages
 constexpr int kMaxGateCtas = 960;            // done words in the workspace
 constexpr int kChainMaxLayers = 256;         // layer descriptors held in shared memory
+constexpr int kMaxChunks = E_MAX / 32;       // 32-expert chunks of the router
 constexpr int kChainMaxT = 4;                // tokens per call
 constexpr int kChainMaxK = 8;                // top-K
 constexpr int kGateMaxExperts = 4;           // experts per gate CTA
-constexpr int kHeadChunk = 12;               // heads per warp with loads in flight together
 constexpr int kHalfD = 64;                   // head_dim 128
 constexpr long long kChainSpin = 1LL << 21;  // bounded waits (about a second of polling)
 constexpr int kRedRows = kChainMaxT * kGateMaxExperts;
@@ -46,6 +45,7 @@ constexpr int kRedRows = kChainMaxT * kGateMaxExperts;
 struct ChainParams {
     const kb_chain_layer_t* layers;
     int L, T, H, Hq, Hkv, E, K;
+    int pair_threads;  // threads owning row vectors in the norm stages (row_shape)
     float eps;
     const bf16* attn_out;
     const bf16* moe_out;
@@ -82,6 +82,18 @@ __device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
 __device__ __forceinline__ void st_rel(unsigned* p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+    const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp4(void* dst, const void* src) {
+    const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Thread 0 waits until *p >= target.  Gives up (sets err) after kChainSpin polls, or as soon
 // as another CTA has given up.
@@ -169,12 +181,16 @@ struct MainSmem {
     int* scratch; // [64]
     int* flag;    // [4]
     kb_chain_layer_t* layers;  // [kChainMaxLayers]
+    float* xrow;  // [kChainMaxT][E_MAX] logits of the layer
+    int* cand;    // [kChainMaxT][kMaxChunks][kChainMaxK] chunk winners
+    float* bias;  // [E_MAX] gate bias of the layer (+0 for -0), 0 without one
 };
 
 __host__ __device__ constexpr size_t main_smem_bytes(int H) {
     return (size_t)3 * kChainMaxT * H * sizeof(bf16) + 2 * kChainMaxT * kHalfD * sizeof(float) +
            (size_t)kRedRows * 33 * sizeof(float) + (2 * E_MAX + 4 + 32 + 32 + 64 + 4) * sizeof(int) +
-           (size_t)kChainMaxLayers * sizeof(kb_chain_layer_t);
+           (size_t)kChainMaxLayers * sizeof(kb_chain_layer_t) +
+           (size_t)(kChainMaxT * E_MAX + kChainMaxT * kMaxChunks * kChainMaxK + E_MAX) * 4;
 }
 __host__ __device__ constexpr size_t gate_smem_bytes(int H) {
     return (size_t)2 * kGateMaxExperts * H * sizeof(bf16) + (size_t)kRedRows * 33 * sizeof(float) +
@@ -196,50 +212,48 @@ __device__ MainSmem carve_main(unsigned char* smem, int H) {
     m.scratch = m.perm + 32;
     m.flag = m.scratch + 64;
     m.layers = reinterpret_cast<kb_chain_layer_t*>(m.flag + 4);
+    m.xrow = reinterpret_cast<float*>(m.layers + kChainMaxLayers);
+    m.cand = reinterpret_cast<int*>(m.xrow + kChainMaxT * E_MAX);
+    m.bias = reinterpret_cast<float*>(m.cand + kChainMaxT * kMaxChunks * kChainMaxK);
     return m;
 }
 
-// A: per-head RMSNorm + NeoX RoPE.  Eight lanes per (token, head), 16 elements per lane,
-// four heads per warp.  Lane p of a head holds the elements of lanes 4p..4p+3 of the
-// one-warp-per-head kernel (qk_norm_rope.cu); its butterfly levels 16, 8, 4 become lane
-// exchanges 4, 2, 1 and levels 2, 1 register adds, so the sum of squares, and with it every
-// output, has the same bits.  The NeoX partner of element j (j +- 64) sits in lane p^4.
-constexpr int kQkChunk = 3;  // head groups per warp with loads in flight together
+// A: per-head RMSNorm + NeoX RoPE.  Four lanes per (token, head), 32 elements per lane,
+// eight heads per warp.  Lane p of a head holds the elements of lanes 8p..8p+7 of the
+// one-warp-per-head kernel (qk_norm_rope.cu); its butterfly levels 16, 8 become lane
+// exchanges 2, 1 and levels 4, 2, 1 register adds, so the sum of squares, and with it every
+// output, has the same bits.  The NeoX partner of element j (j +- 64) sits in lane p^2.
+constexpr int kQkChunk = 1;  // head groups per warp with loads in flight together
 
 __device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer_t& Ly,
                                      const MainSmem& s) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int slot = lane >> 3, pl = lane & 7;  // head slot in the warp, lane in the head
+    const int slot = lane >> 2, pl = lane & 3;  // head slot in the warp, lane in the head
     const int HH = p.Hq + p.Hkv, nh = p.T * HH;
-    const int ngroups = (nh + 3) >> 2;
+    const int ngroups = (nh + 7) >> 3;
     const bool rope = !Ly.rnope && p.pos != nullptr;
-    V8 gq[2], gk[2];
-    gq[0].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_q) + pl * 16));
-    gq[1].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_q) + pl * 16 + 8));
-    gk[0].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_k) + pl * 16));
-    gk[1].u = __ldg(reinterpret_cast<const uint4*>(static_cast<const bf16*>(Ly.g_k) + pl * 16 + 8));
     for (int g0 = warp; g0 < ngroups; g0 += kCW * kQkChunk) {
-        V8 xv[kQkChunk][2];
+        V8 xv[kQkChunk][4];
 #pragma unroll
         for (int c = 0; c < kQkChunk; ++c) {  // clamped heads: every load in flight at once
-            const int hd = min((g0 + c * kCW) * 4 + slot, nh - 1);
+            const int hd = min((g0 + c * kCW) * 8 + slot, nh - 1);
             const int t = hd / HH, hh = hd - t * HH;
             const bf16* src = hh < p.Hq ? p.q + ((size_t)t * p.Hq + hh) * 128
                                         : p.k + ((size_t)t * p.Hkv + (hh - p.Hq)) * 128;
-            xv[c][0].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 16));
-            xv[c][1].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 16 + 8));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) xv[c][u].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 32) + u);
         }
 #pragma unroll
         for (int c = 0; c < kQkChunk; ++c) {
             if (g0 + c * kCW >= ngroups) break;
-            const int hd = (g0 + c * kCW) * 4 + slot;
+            const int hd = (g0 + c * kCW) * 8 + slot;
             const bool act = hd < nh;
             const int t = act ? hd / HH : 0, hh = act ? hd - t * HH : 0;
             const bool is_q = hh < p.Hq;
-            float y[16];
-            float part[4];
+            float y[32];
+            float part[8];
 #pragma unroll
-            for (int sub = 0; sub < 4; ++sub) {
+            for (int sub = 0; sub < 8; ++sub) {
                 part[sub] = 0.0f;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -249,24 +263,31 @@ __device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer
                 }
             }
 #pragma unroll
-            for (int o = 4; o > 0; o >>= 1)
+            for (int o = 2; o > 0; o >>= 1)  // levels 16, 8
 #pragma unroll
-                for (int sub = 0; sub < 4; ++sub)
+                for (int sub = 0; sub < 8; ++sub)
                     part[sub] += __shfl_xor_sync(FULL_MASK, part[sub], o);
-            const float l2a = part[0] + part[2], l2b = part[1] + part[3];  // level 2
-            const float ss = l2a + l2b;                                      // level 1
+            float a4[4];
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub) a4[sub] = part[sub] + part[sub + 4];  // level 4
+            const float a20 = a4[0] + a4[2], a21 = a4[1] + a4[3];                  // level 2
+            const float ss = a20 + a21;                                             // level 1
             const float r = 1.0f / sqrtf(ss / 128.0f + p.eps);
-            const V8* g = is_q ? gq : gk;
+            V8 g[4];  // this lane's gamma slice (L1 after the first head)
 #pragma unroll
-            for (int k = 0; k < 16; ++k)
+            for (int u = 0; u < 4; ++u)
+                g[u].u = __ldg(reinterpret_cast<const uint4*>(
+                    static_cast<const bf16*>(is_q ? Ly.g_q : Ly.g_k) + pl * 32) + u);
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
                 y[k] = __fmul_rn(__fmul_rn(y[k], r), __bfloat162float(g[k >> 3].e[k & 7]));
-            V8 o[2];
+            V8 o[4];
             if (rope) {
-                const bool first_half = pl < 4;
+                const bool first_half = pl < 2;
 #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    const float other = __shfl_xor_sync(FULL_MASK, y[k], 4);
-                    const int j = (pl * 16 + k) & (kHalfD - 1);
+                for (int k = 0; k < 32; ++k) {
+                    const float other = __shfl_xor_sync(FULL_MASK, y[k], 2);
+                    const int j = (pl * 32 + k) & (kHalfD - 1);
                     const float cc = s.cs[t * kHalfD + j], sv = s.sn[t * kHalfD + j];
                     const float v = first_half ? __fsub_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv))
                                                : __fadd_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv));
@@ -274,21 +295,22 @@ __device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer
                 }
             } else {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) o[k >> 3].e[k & 7] = __float2bfloat16_rn(y[k]);
+                for (int k = 0; k < 32; ++k) o[k >> 3].e[k & 7] = __float2bfloat16_rn(y[k]);
             }
             if (act) {
                 bf16* dst = is_q ? p.q_out + ((size_t)t * p.Hq + hh) * 128
                                  : p.k_out + ((size_t)t * p.Hkv + (hh - p.Hq)) * 128;
-                reinterpret_cast<uint4*>(dst + pl * 16)[0] = o[0].u;
-                reinterpret_cast<uint4*>(dst + pl * 16)[1] = o[1].u;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) reinterpret_cast<uint4*>(dst + pl * 32)[u] = o[u].u;
             }
         }
     }
 }
 
 // B / F: sum = res + RMSNorm(a)*g1 (rounded) ; norm = RMSNorm(sum)*g2, for the T rows.
-// Threads below kPairThreads own vectors tid + i*kPairThreads, exactly as the stand-alone
-// kernel's 256 threads do; the others add zeros to the reductions, which changes no bit.
+// Threads below pair_threads own vectors tid + i*pair_threads, exactly as the stand-alone
+// kernel's threads do (row_shape); the others add zeros to the reductions, which changes no
+// bit.
 // a comes from global memory (read-only during the launch), res from shared memory.
 // sum goes to sum_sm (and sum_g if non-null), norm to norm_g (and norm_sm if non-null).
 template <int VPT, int TT>
@@ -296,14 +318,15 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
                            const bf16* g1, const bf16* g2, bf16* sum_sm, bf16* sum_g,
                            bf16* norm_g, bf16* norm_sm, float* red) {
     const int T = p.T, H = p.H, nvec = H / 8;
-    // Threads past kPairThreads own no vector: their index lands past the row.
-    const int tid = threadIdx.x < kPairThreads ? (int)threadIdx.x : nvec;
+    // Threads past pair_threads own no vector: their index lands past the row.
+    const int PT = p.pair_threads;
+    const int tid = (int)threadIdx.x < PT ? (int)threadIdx.x : nvec;
     V8 va[TT][VPT];
     V8 vg1[VPT], vg2[VPT];
     float ss[TT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {  // weights first: every load of the stage is in flight at once
-        const int v = min(tid + i * kPairThreads, nvec - 1);
+        const int v = min(tid + i * PT, nvec - 1);
         vg1[i].u = __ldg(reinterpret_cast<const uint4*>(g1) + v);
         vg2[i].u = __ldg(reinterpret_cast<const uint4*>(g2) + v);
     }
@@ -313,13 +336,13 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
 #pragma unroll
         for (int i = 0; i < VPT; ++i)
             va[t][i].u = ld_stream(reinterpret_cast<const uint4*>(a + (size_t)min(t, T - 1) * H) +
-                                   min(tid + i * kPairThreads, nvec - 1));
+                                   min(tid + i * PT, nvec - 1));
     }
 #pragma unroll
     for (int t = 0; t < TT; ++t)
 #pragma unroll
         for (int i = 0; i < VPT; ++i)
-            if (tid + i * kPairThreads >= nvec) va[t][i].u = make_uint4(0, 0, 0, 0);
+            if (tid + i * PT >= nvec) va[t][i].u = make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
         if (t < T) {
@@ -341,7 +364,7 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
             const float r1 = rms_scale(ss[t], H, p.eps);
 #pragma unroll
             for (int i = 0; i < VPT; ++i) {
-                const int v = tid + i * kPairThreads;
+                const int v = tid + i * PT;
                 if (v < nvec) {
                     V8 vr, vh;
                     const V8& vg = vg1[i];
@@ -369,7 +392,7 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
             const float r2 = rms_scale(ss2[t], H, p.eps);
 #pragma unroll
             for (int i = 0; i < VPT; ++i) {
-                const int v = tid + i * kPairThreads;
+                const int v = tid + i * PT;
                 if (v < nvec) {
                     V8 vx;
                     const V8& vg = vg2[i];
@@ -385,55 +408,78 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
     }
 }
 
-// D: exact top-K per token (warp t routes token t; expert = lane + 32*j), the weights, then
-// the maps of the T*K <= 32 selections.  Same keys and tie rule as the router kernels:
-// score = logit + (bias + 0), ordered by okey (NaN highest), the lower expert index first.
-constexpr int kVPL = E_MAX / 32;  // keys per lane (experts lane + 32*j)
+// D: exact top-K per token, then the weights and the maps of the T*K <= 32 selections.
+// Same keys and tie rule as the router kernels: score = logit + (bias + 0), ordered by okey
+// (NaN highest), the lower expert index first.  Two steps: every warp takes the top-K of one
+// 32-expert chunk of one token (one expert per lane), then warp t merges the chunk winners
+// of token t (at most 16 chunks * K candidates).  The bias row sits in shared memory
+// (bias_sm, filled at the start of the layer) and the logits are copied there for the
+// weights.
+__device__ __forceinline__ void warp_topk_round(uint32_t& key, int idx, int K, int lane,
+                                                int* out_idx) {
+    for (int r = 0; r < K; ++r) {
+        const uint32_t wmax = __reduce_max_sync(FULL_MASK, key);
+        const unsigned cand = (key == wmax && key != 0u) ? (unsigned)idx : 0xffffffffu;
+        const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
+        if (cand == widx) key = 0u;
+        if (lane == 0) out_idx[r] = (int)widx;  // 0xffffffff (-1): fewer than K candidates
+    }
+}
 
-__device__ __noinline__ void stage_route_maps(const ChainParams& p, const float* bias, const MainSmem& s) {
+__device__ __noinline__ void stage_route_maps(const ChainParams& p, const float* bias_sm,
+                                             const MainSmem& s) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int T = p.T, E = p.E, K = p.K, n = T * K;
+    const int nch = (E + 31) >> 5;  // 32-expert chunks per token
+    cp_wait<0>();  // the bias row of this layer
+    __syncthreads();
+    // Step 1: (token, chunk) pairs over the warps.
+    for (int pc = warp; pc < T * nch; pc += kCW) {
+        const int t = pc / nch, c = pc - t * nch;
+        const int e = c * 32 + lane;
+        const float x = __ldcg(p.logits + (size_t)t * E + min(e, E - 1));
+        uint32_t key = (e < E) ? okey(x + (bias_sm[min(e, E - 1)] + 0.0f)) : 0u;
+        if (e < E) s.xrow[t * E_MAX + e] = x;
+        warp_topk_round(key, e, K, lane, s.cand + (t * kMaxChunks + c) * kChainMaxK);
+    }
+    __syncthreads();
+    // Step 2: warp t merges token t's chunk winners (lane l holds candidates l, l+32, ...).
     if (warp < T) {
         const int t = warp;
-        const float* row = p.logits + (size_t)t * E;
-        // All loads first, from clamped addresses, so that they are in flight together.
-        float x[kVPL], b[kVPL];
+        const int* cd = s.cand + t * kMaxChunks * kChainMaxK;
+        const int nc = nch * K;
+        uint32_t key[(kMaxChunks * kChainMaxK + 31) / 32];
+        int idx[(kMaxChunks * kChainMaxK + 31) / 32];
 #pragma unroll
-        for (int j = 0; j < kVPL; ++j) x[j] = __ldcg(row + min(lane + 32 * j, E - 1));
-        if (bias) {
-#pragma unroll
-            for (int j = 0; j < kVPL; ++j) b[j] = __ldg(bias + min(lane + 32 * j, E - 1)) + 0.0f;
-        } else {
-#pragma unroll
-            for (int j = 0; j < kVPL; ++j) b[j] = 0.0f;
+        for (int j = 0; j < (kMaxChunks * kChainMaxK + 31) / 32; ++j) {
+            const int i = lane + 32 * j;
+            const int cc = i / K, r = i - cc * K;
+            const int e = (i < nc) ? cd[cc * kChainMaxK + r] : -1;
+            idx[j] = e;
+            key[j] = (e >= 0) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
         }
-        uint32_t key[kVPL];
-#pragma unroll
-        for (int j = 0; j < kVPL; ++j) key[j] = (lane + 32 * j < E) ? okey(x[j] + b[j]) : 0u;
         for (int r = 0; r < K; ++r) {
             uint32_t best = 0u;
-            int bj = 0;
+            int bi = 0x7fffffff;
 #pragma unroll
-            for (int j = 0; j < kVPL; ++j)
-                if (key[j] > best) {
+            for (int j = 0; j < (kMaxChunks * kChainMaxK + 31) / 32; ++j)
+                if (key[j] > best || (key[j] == best && key[j] != 0u && idx[j] < bi)) {
                     best = key[j];
-                    bj = j;
+                    bi = idx[j];
                 }
             const uint32_t wmax = __reduce_max_sync(FULL_MASK, best);
-            const unsigned cand = (best == wmax && best != 0u) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
+            const unsigned cand = (best == wmax && best != 0u) ? (unsigned)bi : 0xffffffffu;
             const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
-            if (cand == widx) {
 #pragma unroll
-                for (int j = 0; j < kVPL; ++j)
-                    if (j == bj) key[j] = 0u;
-            }
+            for (int j = 0; j < (kMaxChunks * kChainMaxK + 31) / 32; ++j)
+                if (idx[j] == (int)widx) key[j] = 0u;
             if (lane == 0) s.sel[t * K + r] = (int)widx;
         }
         __syncwarp();
         if (lane < K) {
             const int id = s.sel[t * K + lane];
             p.ids[t * K + lane] = id;
-            p.w[t * K + lane] = sigmoid_acc(__ldcg(row + id));
+            p.w[t * K + lane] = sigmoid_acc(s.xrow[t * E_MAX + id]);
         }
     }
     __syncthreads();
@@ -505,12 +551,22 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
     __syncthreads();
     for (int l = 0; l < p.L; ++l) {
         const kb_chain_layer_t& Ly = s.layers[l];
+        // This layer's gate bias into shared memory, in the background until the router.
+        if (Ly.gate_bias) {
+            for (int e = threadIdx.x; e < p.E; e += kCT) cp4(s.bias + e, Ly.gate_bias + e);
+        } else {
+            for (int e = threadIdx.x; e < p.E; e += kCT) s.bias[e] = 0.0f;
+        }
+        cp_commit();
         if (l + 1 < p.L) {  // the next layer's small weights into L2
             const kb_chain_layer_t& Ln = s.layers[l + 1];
             const char* bases[4] = {static_cast<const char*>(Ln.g_post_attn),
                                     static_cast<const char*>(Ln.g_pre_moe),
                                     static_cast<const char*>(Ln.g_post_ffn),
                                     static_cast<const char*>(Ln.g_input_ln)};
+            if (Ln.gate_bias && threadIdx.x < (p.E * 4 + 127) / 128)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(
+                    reinterpret_cast<const char*>(Ln.gate_bias) + threadIdx.x * 128));
             const int lines = (H * 2 + 127) / 128;
             for (int i = threadIdx.x; i < 4 * lines; i += kCT)
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(bases[i / lines] + (size_t)(i % lines) * 128));
@@ -533,7 +589,7 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
             for (int e = threadIdx.x; e <= p.E; e += kCT) p.offsets[e] = -1;
             return;
         }
-        stage_route_maps(p, Ly.gate_bias, s);
+        stage_route_maps(p, s.bias, s);
         stage_expand(p, s);
         stage_pair<VPT, TT>(p, p.moe_out, s.h, static_cast<const bf16*>(Ly.g_post_ffn),
                         static_cast<const bf16*>(Ly.g_input_ln), s.r, p.r_out, p.nxt, nullptr,
@@ -548,15 +604,9 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
 // ------------------------------------------------------------------------------------
 // Gate CTAs: router GEMV for experts j, j + G1, ... (G1 = gate CTAs).
 // ------------------------------------------------------------------------------------
-__device__ __forceinline__ void cp16(void* dst, const void* src) {
-    const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+constexpr int kQuarters = kCW / kGateMaxExperts;  // warps sharing one expert's dot product
 
-template <int VPTG, int TT>
+template <int VQ, int TT>
 __device__ __noinline__ void chain_gate(const ChainParams& p, unsigned char* smem) {
     const int G1 = gridDim.x - 1, j = blockIdx.x - 1;
     const int H = p.H, E = p.E, T = p.T, nvec = H / 8;
@@ -591,50 +641,56 @@ __device__ __noinline__ void chain_gate(const ChainParams& p, unsigned char* sme
             return;
         }
         const bf16* wl = wb + (size_t)(l & 1) * kGateMaxExperts * H;
-        float acc[TT * kGateMaxExperts];
+        // Warp w computes expert m = w / kQuarters over quarter q = w % kQuarters of H for
+        // every token: its W vectors once from shared memory, each token's moe_in vectors
+        // from L2, two accumulator chains per token, a warp sum; the quarters are then added
+        // in order by one thread per (token, expert).
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const int m = warp / kQuarters, q = warp - m * kQuarters;
+        const int Q = (nvec + kQuarters - 1) / kQuarters;
+        if (m < ne) {
+            V8 wv[VQ];
 #pragma unroll
-        for (int i = 0; i < TT * kGateMaxExperts; ++i) acc[i] = 0.0f;
-        // Every moe_in vector of this thread first (clamped rows and vectors, all in flight
-        // together), then the products; rows t >= T and vectors past H count as zero.
-        V8 xv[TT][VPTG];
+            for (int i = 0; i < VQ; ++i) {
+                const int v = q * Q + lane + 32 * i;
+                wv[i].u = reinterpret_cast<const uint4*>(wl + (size_t)m * H)[min(v, nvec - 1)];
+            }
 #pragma unroll
-        for (int t = 0; t < TT; ++t)
+            for (int t = 0; t < TT; ++t) {
+                V8 xv[VQ];
 #pragma unroll
-            for (int i = 0; i < VPTG; ++i)
-                xv[t][i].u = __ldcg(reinterpret_cast<const uint4*>(p.moe_in + (size_t)min(t, T - 1) * H) +
-                                    min((int)threadIdx.x + i * kCT, nvec - 1));
+                for (int i = 0; i < VQ; ++i) {
+                    const int v = q * Q + lane + 32 * i;
+                    xv[i].u = __ldcg(reinterpret_cast<const uint4*>(p.moe_in + (size_t)t * H) +
+                                     min(v, nvec - 1));
+                }
+                float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-        for (int i = 0; i < VPTG; ++i) {
-            const int v = threadIdx.x + i * kCT;
-            const bool vin = v < nvec;
+                for (int i = 0; i < VQ; ++i) {
+                    const int v = q * Q + lane + 32 * i;
+                    if (v < min((q + 1) * Q, nvec)) {
 #pragma unroll
-            for (int m = 0; m < kGateMaxExperts; ++m) {
-                if (m < ne) {
-                    V8 wv;
-                    wv.u = reinterpret_cast<const uint4*>(wl + (size_t)m * H)[vin ? v : 0];
-#pragma unroll
-                    for (int t = 0; t < TT; ++t) {
-                        if (t < T && vin) {
-#pragma unroll
-                            for (int e = 0; e < 8; ++e)
-                                acc[t * kGateMaxExperts + m] =
-                                    fmaf(__bfloat162float(xv[t][i].e[e]), __bfloat162float(wv.e[e]),
-                                         acc[t * kGateMaxExperts + m]);
+                        for (int e = 0; e < 8; e += 2) {
+                            a0 = fmaf(__bfloat162float(xv[i].e[e]), __bfloat162float(wv[i].e[e]), a0);
+                            a1 = fmaf(__bfloat162float(xv[i].e[e + 1]), __bfloat162float(wv[i].e[e + 1]), a1);
                         }
                     }
                 }
+                const float sum = warp_sum(a0 + a1);
+                if (lane == 0) red[(m * kQuarters + q) * TT + t] = sum;
             }
         }
-        block_sum_n<TT * kGateMaxExperts>(acc, T * kGateMaxExperts, red);
+        __syncthreads();
+        if (threadIdx.x < ne * TT) {
+            const int mm = threadIdx.x / TT, t = threadIdx.x - mm * TT;
+            float sum = 0.0f;
 #pragma unroll
-        for (int t = 0; t < TT; ++t)
-#pragma unroll
-            for (int m = 0; m < kGateMaxExperts; ++m)
-                if (threadIdx.x == t * kGateMaxExperts + m && t < T && m < ne) {
-                    const float v = __bfloat162float(__float2bfloat16_rn(acc[t * kGateMaxExperts + m]));
-                    p.logits[(size_t)t * E + ex[m]] = v;
-                    if (p.trace_logits) p.trace_logits[((size_t)l * T + t) * E + ex[m]] = v;
-                }
+            for (int qq = 0; qq < kQuarters; ++qq) sum += red[(mm * kQuarters + qq) * TT + t];
+            const float v = __bfloat162float(__float2bfloat16_rn(sum));
+            const int e = j + mm * G1;
+            p.logits[(size_t)t * E + e] = v;
+            if (p.trace_logits) p.trace_logits[((size_t)l * T + t) * E + e] = v;
+        }
         __syncthreads();
         if (threadIdx.x == 0) st_rel(p.done + j, (unsigned)(l + 1));  // after the barrier above
     }
@@ -656,7 +712,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
         reinterpret_cast<int*>(&ps)[i] = reinterpret_cast<const int*>(&p)[i];
     __syncthreads();
     if (blockIdx.x == 0) chain_main<VPT, TT>(ps, smem);
-    else chain_gate<(VPT * kPairThreads + kCT - 1) / kCT, TT>(ps, smem);
+    else chain_gate<VPT * kCT / (kQuarters * 32), TT>(ps, smem);
 }
 
 // ------------------------------------------------------------------------------------
@@ -718,7 +774,7 @@ extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, con
     if (n_layers > kChainMaxLayers) return KB_ERR_UNSUPPORTED;
     if (T < 1 || n_layers < 1 || H <= 0 || Hq < 0 || Hkv < 0 || E <= 0 || K <= 0)
         return KB_ERR_INVALID_ARG;
-    if (T > kChainMaxT || D != 128 || H % 8 != 0 || H / 8 > 3 * kPairThreads || E > E_MAX ||
+    if (T > kChainMaxT || D != 128 || H % 8 != 0 || row_shape(H / 8).vpt == 0 || row_shape(H / 8).vpt > 3 || E > E_MAX ||
         K > kChainMaxK || K > E || Hq + Hkv <= 0)
         return KB_ERR_UNSUPPORTED;
     if (!layers || !attn_out || !moe_out || !q || !k || !residual_in || !residual_out || !h ||
@@ -770,7 +826,9 @@ extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, con
     prm.err = reinterpret_cast<int*>(wsb + 128);
     prm.done = reinterpret_cast<unsigned*>(wsb + 256);
     const size_t smem = std::max(main_smem_bytes(H), gate_smem_bytes(H));
-    const int vpt = (H / 8 + kPairThreads - 1) / kPairThreads;
+    const RowShape rs = row_shape(H / 8);
+    const int vpt = rs.vpt;
+    prm.pair_threads = rs.threads;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (vpt) {
         case 1: return run_tokens<1>((int)T, prm, smem, 1 + gate, st);

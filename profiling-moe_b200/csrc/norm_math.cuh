@@ -31,4 +31,21 @@ __device__ __forceinline__ float rms_scale(float ss, int H, float eps) {
 template <typename T>
 __device__ __forceinline__ float rnd(float v) { return Elem<T>::to_f(Elem<T>::from_f(v)); }
 
+// Launch shape of a row of nvec 16-byte vectors: vpt vectors per thread, threads a multiple
+// of 32 (at most 512).  Thread i owns vectors i + k*threads, k < vpt.  The stand-alone norm
+// kernels and the decode-chain kernel both use it, so their reductions add in one order.
+// vpt == 0: the row is too long for the register kernels.
+struct RowShape {
+    int vpt, threads;
+};
+inline RowShape row_shape(int nvec) {
+    int vpt = (nvec + 511) / 512;
+    if (vpt > 8) return {0, 0};
+    if (vpt == 5) vpt = 6;
+    if (vpt == 7) vpt = 8;
+    int threads = (nvec + vpt - 1) / vpt;
+    threads = (threads + 31) & ~31;
+    return {vpt, threads};
+}
+
 }  // namespace kb

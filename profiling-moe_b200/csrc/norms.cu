@@ -209,22 +209,6 @@ namespace {
 
 constexpr int kMaxGenericH = 48 * 1024;  // fp32 row in <= 192 KB of shared memory
 
-struct RowShape {
-    int vpt;
-    int threads;
-};
-
-// 16-byte vectors per thread and threads per CTA for a row of nvec vectors.
-inline RowShape row_shape(int nvec) {
-    int vpt = (nvec + 255) / 256;
-    if (vpt > 8) return {0, 0};
-    if (vpt == 5) vpt = 6;
-    if (vpt == 7) vpt = 8;
-    int threads = (nvec + vpt - 1) / vpt;
-    threads = (threads + 31) & ~31;
-    return {vpt, threads};
-}
-
 inline unsigned row_grid(int64_t rows) {
     return (unsigned)std::min<int64_t>(rows, (int64_t)INT32_MAX);
 }
