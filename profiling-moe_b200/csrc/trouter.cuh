@@ -226,3 +226,161 @@ __device__ __forceinline__ void troute_setup(const float* __restrict__ bias, flo
         bias_sm[e] = bias ? __ldg(bias + e) + 0.0f : 0.0f;
     __syncthreads();
 }
+
+// Stage 1 of a batch of nb <= 32 rows that already sit in shared memory (rows_sm, row stride
+// RS floats): rows r0, r0 + rstep, ... of this warp, warp-cooperative group maxima
+// (conflict-free float4 reads), two rows at a time.  gm: nb x (G+1) floats.
+template <int E_, int RS>
+__device__ __forceinline__ void troute_stage1_sm(const float* rows_sm, int nb, int r0, int rstep,
+                                                 const float (&b)[E_ / 32], float* gm) {
+    constexpr int Q = E_ / 128;
+    constexpr int GP = E_ / 16 + 1;
+    const int lane = threadIdx.x & 31;
+    for (int i = r0; i < nb; i += 2 * rstep) {
+        const int i2 = i + rstep;
+        const bool two = i2 < nb;
+        const float* ra = rows_sm + (size_t)i * RS + 4 * lane;
+        const float* rb = rows_sm + (size_t)(two ? i2 : i) * RS + 4 * lane;
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const float4 x = *reinterpret_cast<const float4*>(ra + 128 * q);
+            const float4 y = *reinterpret_cast<const float4*>(rb + 128 * q);
+            float m = fmax_nan(fmax_nan(x.x + b[4 * q + 0], x.y + b[4 * q + 1]),
+                               fmax_nan(x.z + b[4 * q + 2], x.w + b[4 * q + 3]));
+            float n = fmax_nan(fmax_nan(y.x + b[4 * q + 0], y.y + b[4 * q + 1]),
+                               fmax_nan(y.z + b[4 * q + 2], y.w + b[4 * q + 3]));
+            m = fmax_nan(m, __shfl_xor_sync(FULL_MASK, m, 1));
+            n = fmax_nan(n, __shfl_xor_sync(FULL_MASK, n, 1));
+            m = fmax_nan(m, __shfl_xor_sync(FULL_MASK, m, 2));
+            n = fmax_nan(n, __shfl_xor_sync(FULL_MASK, n, 2));
+            if ((lane & 3) == 0) {
+                gm[i * GP + (lane >> 2) + 8 * q] = m;
+                if (two) gm[i2 * GP + (lane >> 2) + 8 * q] = n;
+            }
+        }
+    }
+}
+
+// Stage 2 of a batch whose rows sit in shared memory (stride RS floats; RS = E_ + 4 spreads
+// the rows of a warp's lanes over the banks) and whose group maxima are in gm: lane l ranks
+// token tb + l (l < nb), re-reading its qualifying groups and its weights from shared memory.
+// GLOBAL: rows_sm is the batch's first row in global memory instead (stride RS = E_), read
+// through the read-only path.  Rows holding a NaN take the exact path on the global row.
+template <int E_, int RS, int KT, typename WT, bool GLOBAL = false>
+__device__ void troute_stage2_sm(const float* rows_sm, int nb, int64_t tb,
+                                 const float* __restrict__ logits, const float* bias_sm,
+                                 int K_rt, int renorm, const float* gm, int* sel_tmp,
+                                 int32_t* ids, WT* w, int* sel, int64_t sel_t0) {
+    using C = TCfg<E_, KT>;
+    constexpr int GP = C::G + 1;
+    const int K = KT ? KT : K_rt;
+    const int lane = threadIdx.x & 31;
+    const float4* bias4 = reinterpret_cast<const float4*>(bias_sm);
+    // ---------------- stage 2 ----------------
+    const int64_t t = tb + lane;
+    const bool valid = lane < nb;
+    const float* row = rows_sm + (size_t)(valid ? lane : 0) * RS;
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    float gmax[C::G];
+#pragma unroll
+    for (int g = 0; g < C::G; ++g) gmax[g] = gm[(valid ? lane : 0) * GP + g];
+    bool nan_row = false;
+    float tk[C::KM];
+#pragma unroll
+    for (int i = 0; i < C::KM; ++i) tk[i] = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < C::G; ++g) {
+        float v = gmax[g];
+        nan_row |= (v != v);
+#pragma unroll
+        for (int i = 0; i < C::KM; ++i) {
+            const float hi = fmaxf(tk[i], v);
+            v = fminf(tk[i], v);
+            tk[i] = hi;
+        }
+    }
+    float tau = tk[0];
+#pragma unroll
+    for (int i = 1; i < C::KM; ++i)
+        if (i == K - 1) tau = tk[i];
+    const bool bad = valid && nan_row;
+    if (valid && !nan_row) {
+        uint32_t key[C::KM];
+        int idx[C::KM];
+#pragma unroll
+        for (int i = 0; i < C::KM; ++i) { key[i] = 0u; idx[i] = 0; }
+        unsigned gq = 0u;
+#pragma unroll
+        for (int g = 0; g < C::G; ++g) gq |= (gmax[g] >= tau) ? (1u << g) : 0u;
+        while (gq) {
+            const int g = __ffs(gq) - 1;
+            gq &= gq - 1u;
+            unsigned m = 0u;
+            float xs[16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 x4 = GLOBAL ? __ldg(row4 + g * 4 + q) : row4[g * 4 + q];
+                const float4 bb = bias4[g * 4 + q];
+                xs[4 * q + 0] = x4.x + bb.x;
+                xs[4 * q + 1] = x4.y + bb.y;
+                xs[4 * q + 2] = x4.z + bb.z;
+                xs[4 * q + 3] = x4.w + bb.w;
+            }
+#pragma unroll
+            for (int k = 0; k < 16; ++k) m |= (xs[k] >= tau ? 1u : 0u) << k;
+            // Candidates of this group in index order, each bubbled into the list ordered by
+            // (key desc, index asc); a displaced element keeps precedence over equal keys
+            // with a higher index.
+            while (m) {
+                const int k = __ffs(m) - 1;
+                m &= m - 1u;
+                int jj = g * C::GS + k;
+                uint32_t kk = fkey((GLOBAL ? __ldg(row + jj) : row[jj]) + bias_sm[jj]);
+#pragma unroll
+                for (int i = 0; i < C::KM; ++i) {
+                    const bool gt = kk > key[i] || (kk == key[i] && jj < idx[i]);
+                    const uint32_t ok = key[i];
+                    const int oi = idx[i];
+                    key[i] = gt ? kk : ok;
+                    idx[i] = gt ? jj : oi;
+                    kk = gt ? ok : kk;
+                    jj = gt ? oi : jj;
+                }
+            }
+        }
+        float wv[C::KM];
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < C::KM; ++i) {
+            wv[i] = 0.0f;
+            if (i < K) {
+                wv[i] = sigmoid_acc(GLOBAL ? __ldg(row + idx[i]) : row[idx[i]]);
+                sum += wv[i];
+            }
+        }
+        if (renorm) {
+            const float inv = 1.0f / (sum + 1e-20f);
+#pragma unroll
+            for (int i = 0; i < C::KM; ++i) wv[i] = wv[i] * inv;
+        }
+        put_row<true, false, C::KM, WT>(ids, w, sel, sel_t0, nullptr, t, K, idx, wv);
+    }
+    // ---------------- exact path for rows holding a NaN ----------------
+    unsigned badm = __ballot_sync(FULL_MASK, bad);
+    while (badm) {
+        const int l = __ffs(badm) - 1;
+        badm &= badm - 1u;
+        const float* brow = logits + (tb + l) * E_;
+        route_exact<E_ / 32, true>(brow, bias_sm, E_, K, lane, sel_tmp);
+        const int id = (lane < K) ? sel_tmp[lane] : 0;
+        const float wl = pick_weight((lane < K) ? __ldg(brow + id) : 0.0f, K, lane, renorm);
+        if (lane < K) {
+            const int64_t tt = tb + l;
+            ids[tt * K + lane] = id;
+            w[tt * K + lane] = Elem<WT>::from_f(wl);
+            sel[(int)(tt - sel_t0) * K + lane] = id;
+        }
+        __syncwarp();
+    }
+    __syncwarp();
+}
