@@ -152,6 +152,17 @@ KB_API int kb_expert_maps_noalloc(const int32_t *ids, int32_t *counts, int64_t *
 KB_API int kb_expand_rows(const void *x, void *out, const int32_t *p2u, int64_t T, int64_t rows,
                    int64_t row_bytes, kb_stream_t stream);
 
+/* MoE finalize (combine), the consumer of the maps and weights:
+ *   out[t, :] = dtype( sum_{k < K} float(expert_out[u2p[k*T + t], :]) * weights[t, k] )
+ * fp32 products, summed in slot order k = 0..K-1, one rounding to dtype; a slot whose u2p is
+ * negative or >= T*K contributes nothing.  expert_out [T*K, H] in permuted (expert) order,
+ * u2p int32 [K*T] (kb_expert_maps), weights fp32 [T, K], out [T, H]; dtype KB_BF16, KB_F16
+ * or KB_F32; rows 16-byte aligned.  1 <= K <= 32.
+ * Replaces the eager finalize of the reference harness
+ * (benchmarks/11_profile_2block_e2e.py:259-262). */
+KB_API int kb_moe_finalize(const void *expert_out, const int32_t *u2p, const float *weights,
+                           void *out, int64_t T, int K, int64_t H, int dtype, kb_stream_t stream);
+
 /* ---------------------------------------------------------------------------------
  * (a4) Per-head Q/K RMSNorm fused with NeoX RoPE, bf16 in and out:
  *   y = x * (1/sqrt(mean(x^2) + eps)) * gamma     (fp32, per head of D elements)

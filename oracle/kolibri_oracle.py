@@ -27,6 +27,7 @@ file:line, relative to the reference repository root) and runs it on the CPU:
   post_moe_pre_attn_ref    benchmarks/11_profile_2block_e2e.py:269-270 then :229-231
                            (out = h + RMSNorm(moe_out); next = RMSNorm(out))
   router_logits_ref        benchmarks/11_profile_2block_e2e.py:242-243 ((x @ W_g).float())
+  finalize_ref             benchmarks/11_profile_2block_e2e.py:259-262 (weighted combine by u2p)
 
 Pinning: tests/golden/ holds outputs of the reference's own eager functions (extracted from
 the reference sources by tests/golden/make_golden.py) at the benchmark seeds; the oracle is
@@ -177,3 +178,13 @@ def post_moe_pre_attn_ref(moe_out, h, gamma_post_moe, gamma_pre_attn, eps: float
 
 def router_logits_ref(x: torch.Tensor, w_gate: torch.Tensor) -> torch.Tensor:
     return (x @ w_gate).float()
+
+
+def finalize_ref(expert_out: torch.Tensor, u2p, weights: torch.Tensor) -> torch.Tensor:
+    """(expert_out[u2p.view(K, T)].float() * weights.float().t().unsqueeze(-1)).sum(0).to(dtype);
+    slots whose u2p is negative contribute zero."""
+    T, K = weights.shape
+    perm = torch.as_tensor(u2p).view(K, T).long()
+    valid = (perm >= 0).unsqueeze(-1)
+    rows = expert_out[perm.clamp(min=0)].float() * valid
+    return (rows * weights.float().t().unsqueeze(-1)).sum(0).to(expert_out.dtype)

@@ -41,6 +41,8 @@ SIGNATURES = {
                                  c_void_p]),
     "kb_expert_maps_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                        c_int64, c_int, c_int, c_int, c_void_p]),
+    "kb_moe_finalize": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64,
+                                c_int, c_void_p]),
     "kb_expand_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                c_void_p]),
     "kb_qk_norm_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -17,6 +17,7 @@ from ._lib import (KB_BF16, KB_F16, KB_F32, KB_MAPS_AUTO, KB_MAPS_MULTI_CTA, KB_
 __all__ = [
     "router", "expert_maps", "router_maps", "expand_rows", "qk_norm_rope", "rope_inv_freq",
     "residual_norm_pair", "add_rms_norm", "reserve_workspace", "set_pdl", "expert_maps_noalloc",
+    "moe_finalize",
     "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA", "KB_MAPS_TWO_KERNEL",
 ]
 
@@ -205,6 +206,32 @@ def expand_rows(x: torch.Tensor, p2u: torch.Tensor) -> torch.Tensor:
     out = torch.empty((rows,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
     check(load().kb_expand_rows(_p(x), _p(out), _p(p2u), T, rows, row_bytes,
                                 _stream(x.device)), "kb_expand_rows")
+    return out
+
+
+def moe_finalize(expert_out: torch.Tensor, u2p: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    """Weighted combine of the K expert-output rows of every token.
+
+    expert_out [T*K, H] (permuted order), u2p int32 [K*T] (slot*T + token -> permuted row),
+    weights fp32 [T, K]  ->  out [T, H] = sum_k expert_out[u2p[k*T+t]] * w[t, k] (fp32, in
+    slot order, one rounding)."""
+    _cuda(expert_out, "expert_out")
+    _cuda(u2p, "u2p")
+    _cuda(weights, "weights")
+    for t, n in ((expert_out, "expert_out"), (u2p, "u2p"), (weights, "weights")):
+        _contig(t, n)
+    if u2p.dtype != torch.int32 or weights.dtype != torch.float32 or weights.dim() != 2:
+        raise ValueError("u2p must be int32 and weights float32 [T, K]")
+    if expert_out.dtype not in _DTYPE_CODE:
+        raise ValueError("expert_out must be bfloat16, float16 or float32")
+    T, K = weights.shape
+    H = expert_out.shape[-1]
+    if expert_out.numel() != T * K * H or u2p.numel() != T * K:
+        raise ValueError("expert_out must hold T*K rows and u2p T*K entries")
+    out = torch.empty((T, H), dtype=expert_out.dtype, device=expert_out.device)
+    check(load().kb_moe_finalize(_p(expert_out), _p(u2p), _p(weights), _p(out), T, K, H,
+                                 _DTYPE_CODE[expert_out.dtype], _stream(expert_out.device)),
+          "kb_moe_finalize")
     return out
 
 
