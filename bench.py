@@ -245,6 +245,43 @@ def decode_chain_times(dev, tokens, n_layers, stream, steps=20, warmup=3):
 
 
 # ------------------------------------------------------------------------------------
+# Expert-parallel dispatch + combine (N > 1): count all-gather and token all-to-all
+# ------------------------------------------------------------------------------------
+def ep_round_trip(dev, world, rank, T=4096, H=6144, steps=10, warmup=3):
+    import torch.distributed as dist
+    from kolibri_b200 import workloads as wl
+    from kolibri_b200.ep import ExpertParallel
+    g = torch.Generator().manual_seed(31 + rank)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
+    logits, bias = wl.router_inputs(T, seed=41 + rank)
+    logits, bias = logits.to(dev), bias.to(dev)
+    ep = ExpertParallel(E, K)
+    sent = 0
+    for i in range(warmup + steps):
+        if i == warmup:
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+        d = ep.dispatch(x, logits, bias)
+        ep.combine(d, d.rows)  # identity experts
+        sent = sum(d.send_splits) - d.send_splits[rank]
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = torch.tensor([a.elapsed_time(b) / steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    nvlink_bytes = 2 * sent * (H * 2 + 12)  # rows and metadata out, rows back
+    return {"tokens_per_gpu": T, "hidden": H, "experts_per_gpu": E // world,
+            "us_per_step": round(ms * 1e3, 2),
+            "stages": "router+maps, expansion, count all-gather, row+meta all-to-all, "
+                      "grouping by local expert, reverse all-to-all, finalize",
+            "remote_bytes_per_gpu": nvlink_bytes,
+            "remote_GBps_per_gpu": round(nvlink_bytes / (ms * 1e-3) / 1e9, 1)}
+
+
+# ------------------------------------------------------------------------------------
 # B200 arm
 # ------------------------------------------------------------------------------------
 def main():
@@ -391,6 +428,8 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(ems, 4), "steps": e_steps}
 
+    ep = ep_round_trip(dev, world, rank) if world > 1 else None
+
     chain = None
     if args.chain_tokens:
         chain = decode_chain_times(dev, [int(t) for t in args.chain_tokens.split(",") if t],
@@ -424,6 +463,7 @@ def main():
         "cpu_baseline": cpu,
         "e2e": e2e,
         "decode_chain": chain,
+        "ep_dispatch": ep,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
