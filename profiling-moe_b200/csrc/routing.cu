@@ -739,7 +739,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* e
     atomicExch(err, 1);
     return false;
 }
-// One bulk copy global -> this CTA's shared memory, completing on `bar` (no multicast).
+// One bulk copy global -> this CTA's own shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
