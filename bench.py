@@ -337,12 +337,11 @@ def main():
             step(i)
     torch.cuda.synchronize(dev)
     graphs = []
-    if world == 1:
-        for i in range(nsets):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                step(i)
-            graphs.append(g)
+    for i in range(nsets):  # the count all-gather (N > 1) is captured with the kernel
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(i)
+        graphs.append(g)
     run = (lambda i: graphs[i % nsets].replay()) if graphs else step
     import ctypes
     path_c, launch_c, grid_c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
@@ -350,7 +349,7 @@ def main():
                                     ctypes.byref(launch_c), ctypes.byref(grid_c)),
                "kb_maps_describe")
     launches_per_step = launch_c.value
-    path_name = {1: "single-CTA", 2: "persistent cooperative", 3: "two-kernel"}[path_c.value]
+    path_name = {1: "single-CTA", 2: "persistent multi-CTA", 3: "two-kernel"}[path_c.value]
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -454,7 +453,7 @@ def main():
         "config": {"workload": f"fused router+expert-maps, T={T} tokens per GPU, E=384, k=6",
                    "tokens_per_gpu": T, "experts": E, "top_k": K,
                    "l2": "4 rotating input sets of 100 MB (> 126 MB L2 together)",
-                   "graph": bool(graphs) or world == 1,
+                   "graph": bool(graphs),
                    "parallelism": f"token-sharded x{world}" + (" + count all-gather" if world > 1 else "")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
