@@ -337,11 +337,12 @@ def main():
             step(i)
     torch.cuda.synchronize(dev)
     graphs = []
-    for i in range(nsets):  # the count all-gather (N > 1) is captured with the kernel
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            step(i)
-        graphs.append(g)
+    if world == 1:  # N > 1: the step (kernel + NCCL all-gather) runs eagerly
+        for i in range(nsets):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(i)
+            graphs.append(g)
     run = (lambda i: graphs[i % nsets].replay()) if graphs else step
     import ctypes
     path_c, launch_c, grid_c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()

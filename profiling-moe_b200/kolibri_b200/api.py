@@ -37,6 +37,7 @@ def load_api() -> types.SimpleNamespace:
         sys.path.insert(0, str(ROOT))
     import kernels
     from kernels.cuda import kolibri_build_expert_maps as kbem
+    from kernels.cuda import kolibri_router_dispatch as krd
     from kernels.kolibri_cuda_router import kolibri_cuda_ops
 
     mods = {k: load_module_from_path(k, v) for k, v in _MODULES.items()}
@@ -56,6 +57,7 @@ def load_api() -> types.SimpleNamespace:
         kolibri_activation_expansion=mods["fused_moe_prologue"].kolibri_activation_expansion,
         fused_moe_prologue=mods["fused_moe_prologue"].fused_moe_prologue,
         fused_qk_norm_rope=mods["fused_qk_norm_rope"].fused_qk_norm_rope,
+        fused_kolibri_router_dispatch=krd.fused_kolibri_router_dispatch,
         apply_qk_norm_rope_qkv=mods["fused_qk_norm_rope"].apply_qk_norm_rope_qkv,
     )
     return ns

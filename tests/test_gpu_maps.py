@@ -172,3 +172,23 @@ def test_reference_map_entry_points(api):
     small = ids[:40].contiguous()
     p2u, u2p, off = api.kolibri_dispatch_map(small.cuda(), 384, force_single_block=True)
     np.testing.assert_array_equal(np_of(p2u), orc.expert_maps_ref(small, 384)[2])
+
+
+@pytest.mark.parametrize("T", [1, 40, 4096])
+def test_router_dispatch_entry_point(T, api):
+    # kernels/cuda/kolibri_router_dispatch.py:49-64: (permuted rows, permuted scales, p2u, offsets)
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, 2048, generator=g).to(torch.bfloat16)
+    logits, bias = wl.router_inputs(T, seed=5)
+    out, scales, p2u, off = api.fused_kolibri_router_dispatch(x.cuda(), logits.cuda(), bias.cuda())
+    rid, rw = orc.router_ref(logits, bias)
+    rc, roff, rp2u, ru2p = orc.expert_maps_ref(rid, 384)
+    np.testing.assert_array_equal(np_of(off), roff)
+    np.testing.assert_array_equal(np_of(p2u), rp2u)
+    assert torch.equal(out.cpu(), orc.expansion_ref(x, rp2u))
+    src = torch.from_numpy(rp2u).long()
+    ref_scales = rw.reshape(-1)[(src % T) * 6 + src // T]
+    torch.testing.assert_close(scales.cpu(), ref_scales, rtol=1e-6, atol=0)
+    with pytest.raises(RuntimeError, match="384 experts"):
+        api.fused_kolibri_router_dispatch(x.cuda(), logits[:, :256].contiguous().cuda(),
+                                          bias[:256].contiguous().cuda())
