@@ -20,7 +20,8 @@
 //    more than three picks is re-ranked by an exact key-based path.  Both give the same answer.
 //  * Maps at large T: one persistent cooperative kernel.  Phase 1 routes (or loads ids) and
 //    builds a per-CTA histogram; phase 2 scans each expert's column of CTA histograms; phase 3
-//    ranks the CTA's selections stably with __match_any_sync in input order and scatters.
+//    ranks the CTA's selections stably in input order (expert lanes of a chunk found by
+//    ballots over the expert bits) and scatters.
 //    Phases are separated by a grid barrier whose wait is bounded (on timeout the kernel sets
 //    an error flag in the workspace and returns; later calls then poison the offsets).
 //  * Small T: one CTA does everything in shared memory.  A two-kernel variant (tile
@@ -28,6 +29,9 @@
 //    as the path for shapes the persistent kernel cannot hold.
 #include "kb_common.cuh"
 #include "route_math.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <math.h>
@@ -330,23 +334,38 @@ __device__ __forceinline__ void warp_ranges(int n, int& c0, int& c1) {
     c1 = min(chunks, c0 + per);
 }
 
+// Lanes of the warp holding the same expert as this lane (meaningful for valid lanes; e in
+// [0, E_MAX)): one ballot per bit of e.  Nine ballots issue back to back; match.any on
+// sm_100 has a dependent latency of about 380 cycles against about 25 for a ballot, and
+// shared-memory atomics on random experts serialise (about 2 us for 2.6k selections a CTA).
+__device__ __forceinline__ unsigned same_expert_lanes(int e, bool valid) {
+    static_assert(E_MAX <= 512, "nine expert bits");
+    unsigned m = __ballot_sync(FULL_MASK, valid);
+#pragma unroll
+    for (int b = 0; b < 9; ++b) {
+        const bool bit = (e >> b) & 1;
+        const unsigned vb = __ballot_sync(FULL_MASK, bit);
+        m &= bit ? vb : ~vb;
+    }
+    return m;
+}
+
 // Per-warp histograms of sel[0..n) over each warp's chunk range.  whist: [nwarps][E].
-__device__ void count_per_warp(const int* sel, int n, int E, int* whist) {
+// One shared-memory atomic per selection (cheaper on sm_100 than finding equal lanes).
+template <typename SelT>
+__device__ void count_per_warp(const SelT* sel, int n, int E, int* whist) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* h = whist + warp * E;
     for (int e = lane; e < E; e += 32) h[e] = 0;
     __syncwarp();
     int c0, c1;
     warp_ranges(n, c0, c1);
-    for (int c = c0; c < c1; ++c) {
-        const int i = c * 32 + lane;
-        const int e = (i < n) ? sel[i] : -1;
-        const bool valid = (e >= 0 && e < E);
-        const unsigned peers = __match_any_sync(FULL_MASK, valid ? e : -1);
-        const int leader = 31 - __clz(peers);
-        if (valid && lane == leader) h[e] += __popc(peers);
-        __syncwarp();
+    const int end = min(n, c1 * 32);
+    for (int i = c0 * 32 + lane; i < end; i += 32) {
+        const int e = (int)sel[i];
+        if (e >= 0 && e < E) atomicAdd(h + e, 1);
     }
+    __syncwarp();
 }
 
 // whist[w][e] <- sum_{w'<w} whist[w'][e] (exclusive over warps); tot[e] <- column total.
@@ -391,19 +410,29 @@ __device__ void scan_experts(const int* tot, int E, int* offs, int* scratch) {
 }
 
 // Stable ranks and scatter.  whist[w][e] holds the first permuted row of warp w's
-// selections of expert e (base already added).  sel0 = global index of sel[0] = t0*K.
-__device__ void rank_scatter(const int* sel, int n, int64_t t0, int64_t T, int E, int K,
+// selections of expert e (base already added).  Selection i of the block is token t0 + i/K,
+// slot i%K.  A warp walks its chunks in order; inside a chunk, lanes of one expert rank by
+// lane (same_expert_lanes), and the chunk's last lane of the expert advances the running row.
+// The next chunk's expert lanes are computed before this chunk's shared-memory update, so
+// the ballots overlap the update chain.
+template <typename SelT>
+__device__ void rank_scatter(const SelT* sel, int n, int64_t t0, int64_t T, int E, int K,
                              int* whist, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* h = whist + warp * E;
     const unsigned lt = (1u << lane) - 1u;
     int c0, c1;
     warp_ranges(n, c0, c1);
+    if (c0 >= c1) return;
+    int i = c0 * 32 + lane;
+    int e = (i < n) ? (int)sel[i] : -1;
+    bool valid = (e >= 0 && e < E);
+    unsigned peers = same_expert_lanes(e, valid);
     for (int c = c0; c < c1; ++c) {
-        const int i = c * 32 + lane;
-        const int e = (i < n) ? sel[i] : -1;
-        const bool valid = (e >= 0 && e < E);
-        const unsigned peers = __match_any_sync(FULL_MASK, valid ? e : -1);
+        const int i_n = i + 32;
+        const int e_n = (c + 1 < c1 && i_n < n) ? (int)sel[i_n] : -1;
+        const bool valid_n = (e_n >= 0 && e_n < E);
+        const unsigned peers_n = same_expert_lanes(e_n, valid_n);
         const int leader = 31 - __clz(peers);
         const int base = valid ? h[e] : 0;
         __syncwarp();
@@ -421,6 +450,10 @@ __device__ void rank_scatter(const int* sel, int n, int64_t t0, int64_t T, int E
                 u2p[u] = -1;
             }
         }
+        i = i_n;
+        e = e_n;
+        valid = valid_n;
+        peers = peers_n;
     }
 }
 
@@ -487,6 +520,8 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
 // ------------------------------------------------------------------------------------
 // Persistent cooperative maps kernel (large T).
 // ------------------------------------------------------------------------------------
+__host__ __device__ constexpr size_t tile_align_c(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
 struct PersistWs {
     unsigned* bar;   // arrival counter; 0 between calls (the last CTA out resets it)
     int* err;        // non-zero after a barrier wait gave up; the workspace must be re-zeroed
@@ -538,8 +573,9 @@ __device__ bool grid_barrier(const PersistWs& ws, unsigned target) {
 //                       ceil(grid/kGS) + kGS - 1 independent L2 reads per expert); expert
 //                       totals = sum of all groups; global offsets; scatter
 // The last CTA out zeroes the group sums and resets the arrival counter.
+template <typename SelT>
 __device__ void maps_finish(const PersistWs& ws, int64_t T, int E, int K, int64_t t0, int n,
-                            int* sel, int* hist, int* totsm, int* offs, int* scratch, int* whist,
+                            const SelT* sel, int* hist, int* totsm, int* offs, int* scratch, int* whist,
                             int32_t* counts, int64_t* offsets, int32_t* p2u, int32_t* u2p) {
     const int grid = gridDim.x, c = blockIdx.x;
     const int nwarps = blockDim.x >> 5;
@@ -589,6 +625,229 @@ __device__ void maps_finish(const PersistWs& ws, int64_t T, int E, int K, int64_
         for (int i = threadIdx.x; i < ng * E; i += blockDim.x) ws.gsum[i] = 0;
         __syncthreads();
         if (threadIdx.x == 0) {
+            __threadfence();
+            atomicExch(ws.bar, 0u);
+        }
+    }
+}
+
+// Split grid barrier: arrive once this CTA's stores are issued, do local work, then wait.
+__device__ __forceinline__ void grid_arrive(const PersistWs& ws) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(ws.bar, 1u);
+    }
+}
+__device__ bool grid_wait(const PersistWs& ws, unsigned target) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        unsigned v = ld_acquire_gpu(ws.bar);
+        long long it = 0;
+        while (v < target && it < kSpinLimit) {
+            __nanosleep(32);
+            v = ld_acquire_gpu(ws.bar);
+            ++it;
+        }
+        if (v < target) atomicExch(ws.err, 1);
+        ok = (v >= target) && (*(volatile int*)ws.err == 0);
+        __threadfence();
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+// CTA-sorted positions of the tile kernel's selections.  whist[w][e]: position of warp w's
+// first selection of expert e.  A shared-memory atomic hands out the positions, so each
+// expert's run is ordered by warp and by chunk, but the lanes of one chunk that share an
+// expert may come out in any order; fix_order restores selection order inside runs.
+// stage_sel[pos] = selection index.
+__device__ void rank_atomic(const uint16_t* sel, int n, int E, int* whist, int* stage_sel) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int* h = whist + warp * E;
+    int c0, c1;
+    warp_ranges(n, c0, c1);
+    for (int c = c0; c < c1; ++c) {  // every lane runs every chunk: the warp stays converged
+        const int i = c * 32 + lane;
+        if (i < n) {
+            const int e = (int)sel[i];
+            if (e < E) stage_sel[atomicAdd(h + e, 1)] = i;
+        }
+        __syncwarp();  // chunk c's positions are taken before chunk c + 1's
+    }
+}
+
+// Odd-even transposition over stage_sel[0..nvalid) (sorted by expert): swaps neighbours of
+// one expert whose selection indices are out of order.  Out-of-order entries only span the
+// lanes of one 32-wide chunk, so 16 double rounds sort them; the loop stops at the first
+// round without a swap.  Block-wide (barriers inside).
+__device__ void fix_order(const uint16_t* sel, int nvalid, int* stage_sel) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    for (int round = 0; round < 17; ++round) {
+        int swapped = 0;
+#pragma unroll 1
+        for (int ph = 0; ph < 2; ++ph) {
+            for (int j = 2 * tid + ph; j + 1 < nvalid; j += 2 * nthr) {
+                const int a = stage_sel[j], b = stage_sel[j + 1];
+                if (a > b && sel[a] == sel[b]) {
+                    stage_sel[j] = b;
+                    stage_sel[j + 1] = a;
+                    swapped = 1;
+                }
+            }
+            __syncthreads();
+        }
+        if (!__syncthreads_or(swapped)) break;
+    }
+}
+
+// Shared-memory ints the tile kernel's map phases need beyond the selections: whist, local
+// offsets, prefix partial sums, and (staged writes) the three rank arrays.
+__host__ __device__ constexpr size_t tile_maps_ints(int nthreads, int E, int n, bool staged) {
+    return (size_t)(nthreads / 32) * E + tile_align_c(E + 1, 4) +
+           (size_t)2 * (nthreads / (E / 4)) * E + (staged ? (size_t)2 * n : 0);
+}
+
+// Maps phases of the tile kernel (E % 4 == 0, blockDim >= E/4), after the CTA's selections
+// sel[0..n) (16-bit experts, tokens t0..) are in shared memory.  free_sm: the ring, free now.
+// As maps_finish, with:
+//   arrive early   the grid barrier is entered right after the CTA histogram is published;
+//                  the CTA-local expert offsets and (staged) the CTA-sorted positions of all
+//                  selections (rank_atomic + fix_order) are computed while others arrive
+//   prefix         every thread issues its 128-bit loads of group sums and earlier rows of
+//                  its group before summing; partial sums meet in shared memory
+//   staged writes  p2u in CTA-sorted order (one run of consecutive rows per expert) and u2p
+//                  slot-major (consecutive tokens): coalesced, instead of one 32-byte sector
+//                  per selection.  Without room for the staging arrays: rank_scatter.
+template <int E>
+__device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t t0, int n,
+                                 const uint16_t* sel, int* hist, int* totsm, int* offs,
+                                 int* scratch, int* free_sm, bool staged, int32_t* counts,
+                                 int64_t* offsets, int32_t* p2u, int32_t* u2p) {
+    static_assert(E % 4 == 0, "int4 rows");
+    constexpr int Q4 = E / 4;
+    const int grid = gridDim.x, c = blockIdx.x, nthr = blockDim.x, tid = threadIdx.x;
+    const int nwarps = nthr >> 5;
+    const int g = c / kGS, ng = (grid + kGS - 1) / kGS;
+    const int R = nthr / Q4;
+    int* whist = free_sm;
+    int* loc = whist + nwarps * E;
+    int* part_b = loc + tile_align_c(E + 1, 4);
+    int* part_t = part_b + R * E;
+    int* stage_sel = part_t + R * E;
+    int* stage_r = stage_sel + n;
+
+    __syncthreads();  // selections complete; the ring is free
+    count_per_warp(sel, n, E, whist);
+    __syncthreads();
+    scan_over_warps(E, whist, hist);  // hist = CTA histogram, whist exclusive over warps
+    for (int e = tid; e < E; e += nthr) {
+        const int v = hist[e];
+        __stcg(ws.rowhist + (size_t)c * E + e, v);
+        if (v) atomicAdd(ws.gsum + (size_t)g * E + e, v);
+    }
+    grid_arrive(ws);
+    // While the other CTAs arrive: CTA-local expert offsets and CTA-sorted positions.
+    scan_experts(hist, E, loc, scratch);  // barriers inside
+    __syncthreads();
+    for (int e = tid; e < E; e += nthr) {
+        const int l = loc[e];
+        for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += l;
+    }
+    __syncthreads();
+    const int nvalid = loc[E];
+    if (staged) {
+        rank_atomic(sel, n, E, whist, stage_sel);
+        __syncthreads();
+        fix_order(sel, nvalid, stage_sel);
+    }
+    if (!grid_wait(ws, (unsigned)grid)) return;
+    pdl_launch();
+
+    // Rows before this CTA: group sums 0..g-1 and rows g*kGS..c-1; totals: all group sums.
+    const int nrows = ng + (c - g * kGS);
+    if (tid < R * Q4) {
+        const int qd = tid % Q4, r0 = tid / Q4;
+        const int4* gs4 = reinterpret_cast<const int4*>(ws.gsum);
+        const int4* rh4 = reinterpret_cast<const int4*>(ws.rowhist + (size_t)g * kGS * E);
+        int4 bs = make_int4(0, 0, 0, 0), ts = make_int4(0, 0, 0, 0);
+        for (int rb = r0; rb < nrows; rb += 8 * R) {
+            int4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int r = rb + u * R;
+                v[u] = make_int4(0, 0, 0, 0);
+                if (r < nrows)
+                    v[u] = __ldcg(r < ng ? gs4 + (size_t)r * Q4 + qd : rh4 + (size_t)(r - ng) * Q4 + qd);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int r = rb + u * R;
+                const bool tot = r < ng, bef = (r < g) || (r >= ng);
+                if (tot) { ts.x += v[u].x; ts.y += v[u].y; ts.z += v[u].z; ts.w += v[u].w; }
+                if (bef) { bs.x += v[u].x; bs.y += v[u].y; bs.z += v[u].z; bs.w += v[u].w; }
+            }
+        }
+        reinterpret_cast<int4*>(part_b)[r0 * Q4 + qd] = bs;
+        reinterpret_cast<int4*>(part_t)[r0 * Q4 + qd] = ts;
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nthr) {
+        int b = 0, t = 0;
+        for (int r = 0; r < R; ++r) {
+            b += part_b[r * E + e];
+            t += part_t[r * E + e];
+        }
+        hist[e] = b;
+        totsm[e] = t;
+    }
+    __syncthreads();
+    scan_experts(totsm, E, offs, scratch);
+    __syncthreads();
+    if (c == 0) write_offsets(offs, totsm, E, T * K, counts, offsets, p2u);
+    // Global row of CTA-sorted position lpos of expert e = offs[e] + hist[e] + lpos - loc[e].
+    for (int e = tid; e < E; e += nthr) hist[e] = offs[e] + hist[e] - loc[e];
+    __syncthreads();
+    if (staged) {
+        // p2u in CTA-sorted order: each expert's rows are consecutive.
+        for (int i = tid; i < n; i += nthr) stage_r[i] = -1;  // ids outside [0, E)
+        __syncthreads();
+        for (int j = tid; j < nvalid; j += nthr) {
+            const int i = stage_sel[j];
+            const int r = hist[sel[i]] + j;
+            const unsigned tl = (unsigned)i / (unsigned)K;
+            const int sl = i - (int)tl * K;
+            p2u[r] = (int32_t)((int64_t)sl * T + t0 + tl);
+            stage_r[i] = r;
+        }
+        __syncthreads();
+        if (u2p) {  // slot-major: consecutive tokens
+            const int ntok = n / K;
+            for (int j = tid; j < n; j += nthr) {
+                const int sl = j / ntok, tl = j - sl * ntok;
+                u2p[(int64_t)sl * T + t0 + tl] = stage_r[tl * K + sl];
+            }
+        }
+    } else {
+        for (int e = tid; e < E; e += nthr) {
+            const int d = hist[e];
+            for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += d;
+        }
+        __syncthreads();
+        rank_scatter(sel, n, t0, T, E, K, whist, p2u, u2p);
+    }
+
+    __shared__ int last;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        last = (atomicAdd(ws.bar, 1u) == 2u * (unsigned)grid - 1u);
+    }
+    __syncthreads();
+    if (last) {
+        for (int i = tid; i < ng * E; i += nthr) ws.gsum[i] = 0;
+        __syncthreads();
+        if (tid == 0) {
             __threadfence();
             atomicExch(ws.bar, 0u);
         }
@@ -876,6 +1135,379 @@ __global__ void __launch_bounds__(kTmaThreads, 1) maps_tma_kernel(
                 u2p);
 }
 
+// ------------------------------------------------------------------------------------
+// Tile maps kernel (routing, E = 32*VPL in {128, 256, 384}, K <= 8): one CTA per SM.
+//
+// Warp 0 streams the CTA's tokens in tiles of kTileRows = 32 rows through an nslot-deep
+// ring: one 2-D tensor copy per 32-column box (E/32 boxes per tile), with the 128-byte
+// swizzle, so that 32 lanes each reading their own row hit 8 distinct 16-byte bank groups
+// per quarter-warp (conflict-free lane-per-row float4 reads).  Consumer pair p (warps 1+2p
+// and 2+2p) owns slot p and routes tiles p, p + nslot, ...; lane l ranks token l of the tile:
+//   stage 1     warp h of the pair takes the 16-expert groups [h*G/2, (h+1)*G/2) of its
+//               row: group maxima of s = x + b (NaN-propagating), into gm
+//   tau         both warps read all G maxima: tau = K-th largest, a lower bound of the K-th
+//               largest score (the top-K groups each hold an element >= tau)
+//   candidates  warp h rescans its qualifying groups (maximum >= tau); elements >= tau enter
+//               a register top-K in ascending index order, so a strict key comparison keeps
+//               the lower index first among equal scores
+//   merge       warp 1 hands its list to warp 0 through shared memory; warp 0 inserts it
+//               (its indices are all higher), weighs sigmoid(raw logit) and writes
+// Rows holding a NaN take the exact warp-cooperative path on the global row.  Then the maps
+// phases (maps_finish) with the CTA's selections as 16-bit expert ids.
+// smem (base rounded up to 1024 bytes):
+//   ring[nslot][E/32 boxes][32 rows][32] | gm[nslot][32][G+1] | xk[nslot][KM][32]
+//   | xi[nslot][KM][32] | bias[E] | sel_tmp[nslot][32] | sel (u16)[tpc*K, padded to 8]
+//   | hist[E] | totsm[E] | offs[E+1, padded to 4] | scratch[64] | full[nslot], empty[nslot]
+// whist (maps phases) aliases the ring.
+// ------------------------------------------------------------------------------------
+constexpr int kTileRows = 32;
+constexpr int kTileMaxSlots = 6;
+constexpr int kTileMaxThreads = 32 * (1 + 2 * kTileMaxSlots);
+
+template <int E_, int KT>
+struct TileCfg {
+    static constexpr int G = E_ / 16;                 // 16-expert groups
+    static constexpr int H = G / 2;                   // groups per warp of a pair
+    static constexpr int GP = G + 1;                  // gm row stride (odd)
+    static constexpr int BOXES = E_ / 32;             // 32-column boxes per tile
+    static constexpr int BOX_FLOATS = kTileRows * 32;
+    static constexpr int SLOT_FLOATS = kTileRows * E_;
+    static constexpr int KM = TCfg<E_, KT>::KM;       // register top-K capacity
+    static_assert(E_ % 32 == 0 && G % 2 == 0, "tile shape");
+};
+
+__host__ __device__ constexpr size_t tile_align(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Byte sizes of the tile kernel's shared-memory regions (before the 1024-byte alignment slack).
+template <int E_, int KT>
+__host__ __device__ constexpr size_t tile_smem_bytes(int nslot, int tpc, int K) {
+    using C = TileCfg<E_, KT>;
+    return (size_t)nslot * C::SLOT_FLOATS * 4 + (size_t)nslot * 32 * C::GP * 4 +
+           (size_t)2 * nslot * C::KM * 32 * 4 + (size_t)E_ * 4 + (size_t)nslot * 32 * 4 +
+           tile_align((size_t)tpc * K, 8) * 2 +
+           ((size_t)2 * E_ + tile_align(E_ + 1, 4) + 64) * 4 + (size_t)2 * nslot * 8;
+}
+
+// Float offset of (row r, column col) in a tile slot: box col/32, 128-byte swizzle (the
+// 16-byte chunk index within a 128-byte row is XORed with r mod 8).
+__device__ __forceinline__ int tile_off(int r, int col) {
+    return (col >> 5) * (kTileRows * 32) + r * 32 + ((((col >> 2) & 7) ^ (r & 7)) << 2) + (col & 3);
+}
+
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// One 2-D tensor copy (box at column x, row y) into this CTA's shared memory, completing on bar.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+          "r"(smem_u32(bar)) : "memory");
+}
+
+// Barrier over the two warps of consumer pair p (named barrier 1 + p).
+__device__ __forceinline__ void pair_sync(int p) {
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + p) : "memory");
+}
+static_assert(kTileMaxSlots < 16, "named barriers 1..kTileMaxSlots must exist");
+
+// Insert (kk, jj) into a top-KM list sorted by key descending; candidates arrive in ascending
+// index order, so a strict comparison keeps the earlier (lower) index first among equal keys.
+// The comparisons are independent: positions at and after the first smaller key shift down.
+template <int KM>
+__device__ __forceinline__ void topk_insert(uint32_t (&key)[KM], int (&idx)[KM], uint32_t kk,
+                                            int jj) {
+    bool gt[KM];
+#pragma unroll
+    for (int i = 0; i < KM; ++i) gt[i] = kk > key[i];
+#pragma unroll
+    for (int i = KM - 1; i > 0; --i) {
+        key[i] = gt[i] ? (gt[i - 1] ? key[i - 1] : kk) : key[i];
+        idx[i] = gt[i] ? (gt[i - 1] ? idx[i - 1] : jj) : idx[i];
+    }
+    key[0] = gt[0] ? kk : key[0];
+    idx[0] = gt[0] ? jj : idx[0];
+}
+
+template <int E_, int KT>
+__global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
+    const __grid_constant__ CUtensorMap tmap, const float* __restrict__ logits,
+    const float* __restrict__ bias, int32_t* __restrict__ ids_out, float* __restrict__ w,
+    int64_t T, int K_rt, int renorm, int tpc, int nslot, int32_t* __restrict__ counts,
+    int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p,
+    PersistWs ws) {
+    using C = TileCfg<E_, KT>;
+    constexpr int G = C::G, H = C::H, GP = C::GP, KM = C::KM;
+    const int K = KT ? KT : K_rt;
+    pdl_wait();
+    extern __shared__ __align__(16) unsigned char tile_raw[];
+    unsigned char* base = tile_raw + ((1024u - (smem_u32(tile_raw) & 1023u)) & 1023u);
+    float* ring = reinterpret_cast<float*>(base);
+    float* gm = ring + (size_t)nslot * C::SLOT_FLOATS;
+    uint32_t* xk = reinterpret_cast<uint32_t*>(gm + (size_t)nslot * 32 * GP);
+    int* xi = reinterpret_cast<int*>(xk + (size_t)nslot * KM * 32);
+    float* bias_sm = reinterpret_cast<float*>(xi + (size_t)nslot * KM * 32);
+    int* sel_tmp = reinterpret_cast<int*>(bias_sm + E_);
+    uint16_t* sel = reinterpret_cast<uint16_t*>(sel_tmp + nslot * 32);
+    int* hist = reinterpret_cast<int*>(sel + tile_align((size_t)tpc * K, 8));
+    int* totsm = hist + E_;
+    int* offs = totsm + E_;
+    int* scratch = offs + tile_align(E_ + 1, 4);
+    uint64_t* full = reinterpret_cast<uint64_t*>(scratch + 64);
+    uint64_t* empty = full + nslot;
+    int* whist = reinterpret_cast<int*>(ring);
+    if (ws_poisoned(ws, E_, offsets)) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x;
+    const int64_t t0 = (int64_t)c * tpc;
+    const int64_t t1 = min(T, t0 + tpc);
+    const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
+    const int nbat = (t1 > t0) ? (int)((t1 - t0 + kTileRows - 1) / kTileRows) : 0;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < nslot; ++st) {
+            mbar_init(full + st, 1);
+            mbar_init(empty + st, 2);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    troute_setup<E_>(bias, bias_sm);  // includes the barrier that publishes the mbarriers
+
+    if (warp == 0) {
+        // Producer: every tile of this CTA in order; lane 0 waits for the slot, posts the
+        // byte count of the whole tile (rows past T are zero-filled and still counted) and
+        // issues one tensor copy per box.
+        bool ok = true;
+        int issued = 0;
+        for (int bi = 0; bi < nbat && ok; ++bi) {
+            const int st = bi % nslot, k = bi / nslot;
+            if (lane == 0 && k > 0) ok = mbar_wait(empty + st, (unsigned)((k - 1) & 1), ws.err);
+            ok = __shfl_sync(FULL_MASK, ok, 0);
+            if (!ok) break;
+            const int y = (int)(t0 + (int64_t)bi * kTileRows);
+            if (lane == 0) {
+                mbar_expect_tx(full + st, (unsigned)(C::SLOT_FLOATS * sizeof(float)));
+                float* dst = ring + (size_t)st * C::SLOT_FLOATS;
+#pragma unroll 1
+                for (int bx = 0; bx < C::BOXES; ++bx)
+                    tma_load_2d(dst + bx * C::BOX_FLOATS, &tmap, 32 * bx, y, full + st);
+            }
+            issued = bi + 1;
+        }
+        if (!ok && lane == 0) {  // drain: no copy may still be writing when the CTA moves on
+            for (int bi = max(0, issued - nslot); bi < issued; ++bi)
+                mbar_wait(full + bi % nslot, (unsigned)((bi / nslot) & 1), ws.err);
+        }
+        __syncwarp();
+    } else if (warp <= 2 * nslot) {
+        const int p = (warp - 1) >> 1, h = (warp - 1) & 1;
+        const float* slot = ring + (size_t)p * C::SLOT_FLOATS;
+        float* gms = gm + (size_t)p * 32 * GP;
+        uint32_t* xks = xk + (size_t)p * KM * 32;
+        int* xis = xi + (size_t)p * KM * 32;
+        const float4* bias4 = reinterpret_cast<const float4*>(bias_sm);
+        const int sw = lane & 7;
+        const float* myrow = slot + lane * 32;  // this lane's row inside box 0
+        __shared__ int pair_ok[kTileMaxSlots];
+        for (int bi = p; bi < nbat; bi += nslot) {
+            const unsigned par = (unsigned)((bi / nslot) & 1);
+            // The pair's first warp decides whether the tile arrived (bounded wait); the
+            // decision reaches the second through the pair barrier, so both take one branch.
+            if (h == 0) {
+                const bool ok = mbar_wait(full + p, par, ws.err);
+                if (lane == 0) pair_ok[p] = ok ? 1 : 0;
+            }
+            pair_sync(p);
+            if (!pair_ok[p]) break;
+            if (h == 1) mbar_wait(full + p, par, ws.err);  // completed: returns at once
+            const int64_t tb = t0 + (int64_t)bi * kTileRows;
+            const int rows = (int)min((int64_t)kTileRows, t1 - tb);
+            const bool valid = lane < rows;
+
+            // ---- stage 1: maxima of this warp's groups of the lane's row ----
+#pragma unroll
+            for (int gg = 0; gg < H; ++gg) {
+                const int g = h * H + gg;
+                const float* rp = myrow + (g >> 1) * C::BOX_FLOATS;
+                const int j0 = (g & 1) * 4;
+                float m[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 x = *reinterpret_cast<const float4*>(rp + (((j0 + q) ^ sw) << 2));
+                    const float4 b = bias4[4 * g + q];
+                    m[q] = fmax3_nan(x.x + b.x, x.y + b.y, fmax_nan(x.z + b.z, x.w + b.w));
+                }
+                gms[lane * GP + g] = fmax3_nan(m[0], m[1], fmax_nan(m[2], m[3]));
+            }
+            pair_sync(p);
+
+            // ---- tau: K-th largest group maximum (both warps, all groups) ----
+            float gmax[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) gmax[g] = gms[lane * GP + g];
+            bool nan_row = false;
+            float tk[KM];
+#pragma unroll
+            for (int i = 0; i < KM; ++i) tk[i] = -INFINITY;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float v = gmax[g];
+                nan_row |= (v != v);
+#pragma unroll
+                for (int i = 0; i < KM; ++i) {
+                    const float hi = fmaxf(tk[i], v);
+                    v = fminf(tk[i], v);
+                    tk[i] = hi;
+                }
+            }
+            float tau = tk[0];
+#pragma unroll
+            for (int i = 1; i < KM; ++i)
+                if (i == K - 1) tau = tk[i];
+            unsigned gq = 0u;
+#pragma unroll
+            for (int g = 0; g < G; ++g) gq |= (gmax[g] >= tau) ? (1u << g) : 0u;
+            gq = (gq >> (h * H)) & ((1u << H) - 1u);
+
+            // ---- candidates of this warp's qualifying groups ----
+            uint32_t key[KM];
+            int idx[KM];
+#pragma unroll
+            for (int i = 0; i < KM; ++i) { key[i] = 0u; idx[i] = 0; }
+            if (valid && !nan_row) {
+                while (gq) {
+                    const int g = h * H + __ffs(gq) - 1;
+                    gq &= gq - 1u;
+                    const float* rp = myrow + (g >> 1) * C::BOX_FLOATS;
+                    const int j0 = (g & 1) * 4;
+                    float sv[16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 x = *reinterpret_cast<const float4*>(rp + (((j0 + q) ^ sw) << 2));
+                        const float4 b = bias4[4 * g + q];
+                        sv[4 * q + 0] = x.x + b.x;
+                        sv[4 * q + 1] = x.y + b.y;
+                        sv[4 * q + 2] = x.z + b.z;
+                        sv[4 * q + 3] = x.w + b.w;
+                    }
+                    // Mask of the elements >= tau, built as a tree (no 16-deep OR chain).
+                    unsigned mq[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        mq[q] = ((sv[4 * q] >= tau) ? 1u : 0u) | ((sv[4 * q + 1] >= tau) ? 2u : 0u) |
+                                ((sv[4 * q + 2] >= tau) ? 4u : 0u) | ((sv[4 * q + 3] >= tau) ? 8u : 0u);
+                    unsigned msk = (mq[0] | (mq[1] << 4)) | ((mq[2] << 8) | (mq[3] << 12));
+                    while (msk) {
+                        const int k = __ffs(msk) - 1;
+                        msk &= msk - 1u;
+                        // sv[k] by a 4-level select on the bits of k (registers, no reload)
+                        float a8[8], a4[4], a2[2];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) a8[u] = (k & 1) ? sv[2 * u + 1] : sv[2 * u];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) a4[u] = (k & 2) ? a8[2 * u + 1] : a8[2 * u];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) a2[u] = (k & 4) ? a4[2 * u + 1] : a4[2 * u];
+                        const float v = (k & 8) ? a2[1] : a2[0];
+                        topk_insert<KM>(key, idx, fkey(v), g * 16 + k);
+                    }
+                }
+            }
+
+            // ---- merge, weights, outputs ----
+            if (h == 1) {
+#pragma unroll
+                for (int i = 0; i < KM; ++i) {
+                    xks[i * 32 + lane] = key[i];
+                    xis[i * 32 + lane] = idx[i];
+                }
+            }
+            pair_sync(p);
+            if (h == 1) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty + p);
+                continue;
+            }
+            const bool bad = valid && nan_row;
+            // The tile's ids and weights are staged in the pair's exchange buffers (32 x KM
+            // entries each, row-major [token][K]) and leave as whole 128-byte lines.
+            int32_t* oi = reinterpret_cast<int32_t*>(xks);
+            float* ow = reinterpret_cast<float*>(xis);
+            float xr[KM];  // raw logits of the picks: the last reads of the slot
+            if (valid && !nan_row) {
+#pragma unroll
+                for (int i = 0; i < KM; ++i)
+                    if (i < K) topk_insert<KM>(key, idx, xks[i * 32 + lane], xis[i * 32 + lane]);
+#pragma unroll
+                for (int i = 0; i < KM; ++i) xr[i] = (i < K) ? slot[tile_off(lane, idx[i])] : 0.0f;
+            }
+            __syncwarp();  // slot and exchange buffers read: release the slot, reuse the buffers
+            if (lane == 0) mbar_arrive(empty + p);
+            if (valid && !nan_row) {
+                float wv[KM];
+                float sum = 0.0f;
+#pragma unroll
+                for (int i = 0; i < KM; ++i) {
+                    wv[i] = 0.0f;
+                    if (i < K) {
+                        wv[i] = sigmoid_acc(xr[i]);
+                        sum += wv[i];
+                    }
+                }
+                if (renorm) {
+                    const float inv = 1.0f / (sum + 1e-20f);
+#pragma unroll
+                    for (int i = 0; i < KM; ++i) wv[i] = wv[i] * inv;
+                }
+                uint16_t* sp = sel + (int)(tb + lane - t0) * K;
+#pragma unroll
+                for (int i = 0; i < KM; ++i) {
+                    if (i < K) {
+                        oi[lane * K + i] = idx[i];
+                        ow[lane * K + i] = wv[i];
+                        sp[i] = (uint16_t)idx[i];
+                    }
+                }
+            }
+            // Rows holding a NaN: the exact warp-cooperative ranking on the global row.
+            unsigned badm = __ballot_sync(FULL_MASK, bad);
+            while (badm) {
+                const int l = __ffs(badm) - 1;
+                badm &= badm - 1u;
+                const float* brow = logits + (tb + l) * E_;
+                route_exact<E_ / 32, true>(brow, bias_sm, E_, K, lane, sel_tmp + p * 32);
+                const int id = (lane < K) ? sel_tmp[p * 32 + lane] : 0;
+                const float wl = pick_weight((lane < K) ? __ldg(brow + id) : 0.0f, K, lane, renorm);
+                if (lane < K) {
+                    oi[l * K + lane] = id;
+                    ow[l * K + lane] = wl;
+                    sel[(int)(tb + l - t0) * K + lane] = (uint16_t)id;
+                }
+                __syncwarp();
+            }
+            __syncwarp();
+            {
+                const int cnt = rows * K;
+                int32_t* gi = ids_out + tb * K;
+                float* gw = w + tb * K;
+                for (int j = lane; j < cnt; j += 32) {
+                    gi[j] = oi[j];
+                    gw[j] = ow[j];
+                }
+            }
+            __syncwarp();
+        }
+    }
+    const bool staged =
+        tile_maps_ints(blockDim.x, E_, n, true) <= (size_t)nslot * C::SLOT_FLOATS;
+    maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, whist, staged, counts,
+                         offsets, p2u, u2p);
+}
+
 // Hybrid router for kb_router: each warp takes a contiguous range of tokens.
 // smem: bias[E] | wsm[nw][hwarp] | sel_tmp[nw][32]
 template <int E_, int KT, typename WT>
@@ -1050,7 +1682,7 @@ DevInfo dev_info() {
     return d;
 }
 
-enum class Path { Single, Persistent, TPersistent, Tma, TwoKernel };
+enum class Path { Single, Persistent, TPersistent, Tma, Tile, TwoKernel };
 
 struct MapsPlan {
     Path path;
@@ -1063,6 +1695,7 @@ struct MapsPlan {
     int TT, num_tiles, tiles_per_super, S, super_tokens;
     size_t smem_scatter, smem_count;
     size_t ws_bytes;   // workspace for the chosen multi-CTA path
+    CUtensorMap tmap;  // tile path: the logits tensor map
 };
 
 size_t single_smem(int64_t T, int E, int K, bool route, bool vec) {
@@ -1131,6 +1764,31 @@ int coop_blocks_per_sm(KernelT kern, size_t smem) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kPW * 32, smem) != cudaSuccess)
         return 0;
     return nb;
+}
+
+// 2-D tensor map of a [T][E] fp32 logits matrix for the tile kernel: 32 x 32 boxes, 128-byte
+// swizzle, rows past T zero-filled.  The encoder comes from the driver at first use.
+bool make_tile_map(CUtensorMap* map, const float* logits, int64_t T, int E) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)E, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)E * sizeof(float)};
+    const cuuint32_t box[2] = {32, (cuuint32_t)kTileRows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(logits),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
 }
 
 // Two-kernel plan (also the workspace bound).
@@ -1446,7 +2104,63 @@ struct MapsLaunchT {
             }
         }
 
-        static MapsPlan plan(int64_t T, int E, int K, int mode) {
+        // Tile kernel (routing, E = 32*VPL in {128, 256, 384}, K <= 8, T >= 32): one CTA per
+        // SM with as many 32-row ring slots (and consumer pairs) as shared memory holds.
+        static size_t tile_smem(int nslot, int tpc, int K) {
+            constexpr int E_ = 32 * VPL;
+            return 1024 + (K == 6 ? tile_smem_bytes<E_, 6>(nslot, tpc, K)
+                                  : tile_smem_bytes<E_, 0>(nslot, tpc, K));
+        }
+        static int tile_blocks_per_sm(int K, int nslot, size_t smem) {
+            if constexpr (!(ROUTE && VEC && 32 * VPL <= 384)) {
+                return 0;
+            } else {
+                constexpr int E_ = 32 * VPL;
+                static std::mutex mu;
+                static std::map<std::tuple<int, int, int, size_t>, int> cache;
+                int dev = 0;
+                cudaGetDevice(&dev);
+                std::lock_guard<std::mutex> lk(mu);
+                int& v = cache[std::make_tuple(dev, K == 6 ? 6 : 0, nslot, smem)];
+                if (v == 0) {
+                    int occ = 0;
+                    auto* kern = (K == 6) ? maps_tile_kernel<E_, 6> : maps_tile_kernel<E_, 0>;
+                    allow_smem(kern, smem);
+                    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 32 * (1 + 2 * nslot),
+                                                                      smem) != cudaSuccess)
+                        occ = 0;
+                    v = occ > 0 ? occ : -1;
+                }
+                return v;
+            }
+        }
+        static bool plan_tile(MapsPlan& p, int64_t T, int E, int K) {
+            if constexpr (!(ROUTE && VEC && 32 * VPL <= 384)) {
+                return false;
+            } else {
+                constexpr int E_ = 32 * VPL;
+                if (E != E_ || K > 8 || T < kTileRows || T > (int64_t)INT32_MAX) return false;
+                const int sms = dev_info().sms;
+                int grid = (int)std::min<int64_t>(std::min(kMaxPersistGrid, sms),
+                                                  (T + kTileRows - 1) / kTileRows);
+                grid = std::max(grid, 1);
+                const int64_t tpc = (T + grid - 1) / grid;
+                if (tpc * K > kMaxPersistSel) return false;
+                for (int ns = kTileMaxSlots; ns >= 2; --ns) {
+                    const size_t smem = tile_smem(ns, (int)tpc, K);
+                    if (smem > kMaxSmem) continue;
+                    if (tile_blocks_per_sm(K, ns, smem) < 1) return false;
+                    p.grid = (int)((T + tpc - 1) / tpc);
+                    p.tpc = (int)tpc;
+                    p.tnw = ns;
+                    p.smem_persist = smem;
+                    return true;
+                }
+                return false;
+            }
+        }
+
+        static MapsPlan plan(int64_t T, int E, int K, int mode, bool allow_tile = true) {
             MapsPlan p{};
             const bool fits_single = T * K <= kMaxSingleSel;
             const int64_t auto_single_T = ROUTE ? 32 : 768;
@@ -1456,7 +2170,10 @@ struct MapsLaunchT {
                 return p;
             }
             plan_two_kernel(p, T, E, K, ROUTE, VEC);
-            if (mode != KB_MAPS_TWO_KERNEL && plan_tma(p, T, E, K)) {
+            if (mode != KB_MAPS_TWO_KERNEL && allow_tile && plan_tile(p, T, E, K)) {
+                p.path = Path::Tile;
+                p.ws_bytes = persist_ws_bytes(p.grid, E);
+            } else if (mode != KB_MAPS_TWO_KERNEL && plan_tma(p, T, E, K)) {
                 p.path = Path::Tma;
                 p.ws_bytes = persist_ws_bytes(p.grid, E);
             } else if (mode != KB_MAPS_TWO_KERNEL && plan_tpersist(p, T, E, K)) {
@@ -1485,6 +2202,16 @@ struct MapsLaunchT {
                               ids_in, ids_out, w, T, E, K, renorm, counts, offsets, p2u, u2p);
             }
             if constexpr (ROUTE && VEC && 32 * VPL <= 384) {
+                if (p.path == Path::Tile) {
+                    constexpr int E_ = 32 * VPL;
+                    auto* kern = maps_tile_kernel<E_, (KT == 6 ? 6 : 0)>;
+                    int err = allow_smem(kern, p.smem_persist);
+                    if (err) return err;
+                    return launch_coop(kern, dim3(p.grid), dim3(32 * (1 + 2 * p.tnw)),
+                                       p.smem_persist, st, p.tmap, logits, bias, ids_out, w, T, K,
+                                       renorm, p.tpc, p.tnw, counts, offsets, p2u, u2p,
+                                       carve_persist(ws, p.grid, E));
+                }
                 if (p.path == Path::Tma) {
                     constexpr int E_ = 32 * VPL;
                     auto* kern = maps_tma_kernel<E_, (KT == 6 ? 6 : 0)>;
@@ -1533,7 +2260,11 @@ struct MapsLaunchT {
                        int32_t* ids_out, float* w, int32_t* counts, int64_t* offsets,
                        int32_t* p2u, int32_t* u2p, void* ws, size_t ws_bytes, int64_t T,
                        int E, int K, int renorm, int mode, cudaStream_t st) {
-            const MapsPlan p = plan(T, E, K, mode);
+            // The tile path's tensor copies need a 16-byte aligned logits base and the
+            // driver's tensor-map encoder; without either the next path is taken.
+            MapsPlan p = plan(T, E, K, mode, !ROUTE || aligned16(logits));
+            if (p.path == Path::Tile && !make_tile_map(&p.tmap, logits, T, E))
+                p = plan(T, E, K, mode, false);
             if (p.path == Path::Single) {
                 if (T * K > kMaxSingleSel || p.smem_single > kMaxSmem) return KB_ERR_UNSUPPORTED;
             } else {
@@ -1544,7 +2275,8 @@ struct MapsLaunchT {
             if (VEC && ROUTE && K == 6)
                 return run_kt<6>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
                                  ws, T, E, K, renorm, st);
-            if (p.path == Path::TPersistent || p.path == Path::Tma)  // runtime-K (K <= 8)
+            if (p.path == Path::TPersistent || p.path == Path::Tma ||
+                p.path == Path::Tile)  // runtime-K (K <= 8)
                 return run_kt<0>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
                                  ws, T, E, K, renorm, st);
             return run_kt<0>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p, ws,
@@ -1562,6 +2294,8 @@ struct MapsLaunchT {
             if (plan_tpersist(r, T, E, K)) b = std::max(b, persist_ws_bytes(r.grid, E));
             MapsPlan u{};
             if (plan_tma(u, T, E, K)) b = std::max(b, persist_ws_bytes(u.grid, E));
+            MapsPlan v{};
+            if (plan_tile(v, T, E, K)) b = std::max(b, persist_ws_bytes(v.grid, E));
             return b;
         }
 
@@ -1570,7 +2304,7 @@ struct MapsLaunchT {
                              int* grid) {
             const MapsPlan p = plan(T, E, K, mode);
             const bool pers = p.path == Path::Persistent || p.path == Path::TPersistent ||
-                              p.path == Path::Tma;
+                              p.path == Path::Tma || p.path == Path::Tile;
             const int pk = p.path == Path::Single ? KB_MAPS_SINGLE_CTA
                          : pers ? KB_MAPS_MULTI_CTA : KB_MAPS_TWO_KERNEL;
             if (path) *path = pk;

@@ -192,3 +192,60 @@ def test_router_dispatch_entry_point(T, api):
     with pytest.raises(RuntimeError, match="384 experts"):
         api.fused_kolibri_router_dispatch(x.cuda(), logits[:, :256].contiguous().cuda(),
                                           bias[:256].contiguous().cuda())
+
+
+def _adversarial_logits(E, T=320, seed=0):
+    """Rows that stress the candidate pass: NaN / inf / -0 rows, displaced ties, the top
+    picks packed into one 16-expert group, and coarse integer logits (ties everywhere)."""
+    g = torch.Generator().manual_seed(seed + E)
+    x = torch.randn(T, E, generator=g)
+    x[0, E // 3] = float("nan")
+    x[0, 7] = float("inf")
+    x[1, :] = -float("inf")
+    x[2, ::3] = float("nan")
+    x[3, :] = 0.0
+    x[3, ::2] = -0.0
+    x[4, E // 2:] = float("inf")
+    for r in range(16, 80):                      # equal low-index scores displaced later
+        x[r] = 0.0
+        x[r, :40] = 3.0
+        x[r, 60 + r % (E - 70)] = 5.0 + (r % 3)
+        x[r, E - 1 - r % 8] = 4.0
+    for r in range(80, 144):                     # up to 12 winners inside one group
+        grp = r % (E // 16)
+        x[r] = torch.randn(E, generator=g) - 10.0
+        n = 1 + r % 12
+        x[r, grp * 16: grp * 16 + n] = 10.0 + torch.arange(n).float()
+    x[144:] = torch.randint(-3, 4, (T - 144, E), generator=g).float()
+    return x
+
+
+@pytest.mark.parametrize("E", [128, 256, 384])
+@pytest.mark.parametrize("k", [6, 8])
+def test_router_maps_adversarial_rows(E, k):
+    x = _adversarial_logits(E)
+    g = torch.Generator().manual_seed(E + k)
+    biases = [None, torch.randint(-1, 2, (E,), generator=g).float()]
+    biases[1][::5] = -0.0
+    for bias in biases:
+        rid, rw = orc.router_ref(x, bias, k=k)
+        rc, roff, rp2u, ru2p = orc.expert_maps_ref(rid, E)
+        for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA):
+            ids, w, c, off, p2u, u2p = ops.router_maps(
+                x.cuda(), None if bias is None else bias.cuda(), k=k, mode=mode)
+            assert torch.equal(ids.cpu(), rid), \
+                f"rows {torch.nonzero((ids.cpu() != rid).any(1))[:8].flatten().tolist()}"
+            torch.testing.assert_close(w.cpu(), rw, rtol=1e-6, atol=0, equal_nan=True)
+            check_maps(rid, (c, off, p2u, u2p), E)
+
+
+def test_router_maps_tile_path_tails():
+    # Token counts around the 32-row tile and CTA boundaries of the multi-CTA path.
+    for T in (32, 33, 63, 65, 4736, 4767, 148 * 32 * 3 + 5):
+        logits, bias = wl.router_inputs(T, seed=T)
+        ids, w, c, off, p2u, u2p = ops.router_maps(logits.cuda(), bias.cuda(),
+                                                   mode=ops.KB_MAPS_MULTI_CTA)
+        rid, rw = orc.router_ref(logits, bias)
+        assert torch.equal(ids.cpu(), rid), T
+        torch.testing.assert_close(w.cpu(), rw, rtol=1e-6, atol=0)
+        check_maps(rid, (c, off, p2u, u2p))
