@@ -1147,11 +1147,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) maps_tma_kernel(
 //               row: group maxima of s = x + b (NaN-propagating), into gm
 //   tau         both warps read all G maxima: tau = K-th largest, a lower bound of the K-th
 //               largest score (the top-K groups each hold an element >= tau)
-//   candidates  warp h rescans its qualifying groups (maximum >= tau); elements >= tau enter
-//               a register top-K in ascending index order, so a strict key comparison keeps
-//               the lower index first among equal scores
-//   merge       warp 1 hands its list to warp 0 through shared memory; warp 0 inserts it
-//               (its indices are all higher), weighs sigmoid(raw logit) and writes
+//   candidates  the qualifying groups (maximum >= tau) alternate between the two warps in
+//               index order; elements >= tau enter a register top-K in ascending index
+//               order, so a strict key comparison keeps the lower index first
+//   merge       warp 1 hands its list to warp 0 through shared memory; warp 0 merges it
+//               (key, then lower index), releases the slot, weighs sigmoid(raw logit) and
+//               writes the tile's ids and weights as whole lines
 // Rows holding a NaN take the exact warp-cooperative path on the global row.  Then the maps
 // phases (maps_finish) with the CTA's selections as 16-bit expert ids.
 // smem (base rounded up to 1024 bytes):
@@ -1225,6 +1226,22 @@ __device__ __forceinline__ void topk_insert(uint32_t (&key)[KM], int (&idx)[KM],
     bool gt[KM];
 #pragma unroll
     for (int i = 0; i < KM; ++i) gt[i] = kk > key[i];
+#pragma unroll
+    for (int i = KM - 1; i > 0; --i) {
+        key[i] = gt[i] ? (gt[i - 1] ? key[i - 1] : kk) : key[i];
+        idx[i] = gt[i] ? (gt[i - 1] ? idx[i - 1] : jj) : idx[i];
+    }
+    key[0] = gt[0] ? kk : key[0];
+    idx[0] = gt[0] ? jj : idx[0];
+}
+
+// As topk_insert for an entry of any index: ties go to the lower index.
+template <int KM>
+__device__ __forceinline__ void topk_merge(uint32_t (&key)[KM], int (&idx)[KM], uint32_t kk,
+                                           int jj) {
+    bool gt[KM];
+#pragma unroll
+    for (int i = 0; i < KM; ++i) gt[i] = kk > key[i] || (kk == key[i] && jj < idx[i]);
 #pragma unroll
     for (int i = KM - 1; i > 0; --i) {
         key[i] = gt[i] ? (gt[i - 1] ? key[i - 1] : kk) : key[i];
@@ -1368,10 +1385,13 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
 #pragma unroll
             for (int i = 1; i < KM; ++i)
                 if (i == K - 1) tau = tk[i];
+            // Qualifying groups in index order alternate between the pair's warps (warp h
+            // takes the (h+1)-th, (h+3)-th, ...), which splits them evenly; each warp's
+            // candidates still arrive in ascending index order.
             unsigned gq = 0u;
 #pragma unroll
             for (int g = 0; g < G; ++g) gq |= (gmax[g] >= tau) ? (1u << g) : 0u;
-            gq = (gq >> (h * H)) & ((1u << H) - 1u);
+            if (h == 1) gq &= gq - 1u;
 
             // ---- candidates of this warp's qualifying groups ----
             uint32_t key[KM];
@@ -1380,8 +1400,9 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
             for (int i = 0; i < KM; ++i) { key[i] = 0u; idx[i] = 0; }
             if (valid && !nan_row) {
                 while (gq) {
-                    const int g = h * H + __ffs(gq) - 1;
+                    const int g = __ffs(gq) - 1;
                     gq &= gq - 1u;
+                    gq &= gq - 1u;  // the next qualifying group belongs to the other warp
                     const float* rp = myrow + (g >> 1) * C::BOX_FLOATS;
                     const int j0 = (g & 1) * 4;
                     float sv[16];
@@ -1441,7 +1462,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
             if (valid && !nan_row) {
 #pragma unroll
                 for (int i = 0; i < KM; ++i)
-                    if (i < K) topk_insert<KM>(key, idx, xks[i * 32 + lane], xis[i * 32 + lane]);
+                    if (i < K) topk_merge<KM>(key, idx, xks[i * 32 + lane], xis[i * 32 + lane]);
 #pragma unroll
                 for (int i = 0; i < KM; ++i) xr[i] = (i < K) ? slot[tile_off(lane, idx[i])] : 0.0f;
             }
