@@ -657,23 +657,39 @@ __device__ bool grid_wait(const PersistWs& ws, unsigned target) {
     return ok != 0;
 }
 
-// CTA-sorted positions of the tile kernel's selections.  whist[w][e]: position of warp w's
-// first selection of expert e.  A shared-memory atomic hands out the positions, so each
-// expert's run is ordered by warp and by chunk, but the lanes of one chunk that share an
-// expert may come out in any order; fix_order restores selection order inside runs.
-// stage_sel[pos] = selection index.
-__device__ void rank_atomic(const uint16_t* sel, int n, int E, int* whist, int* stage_sel) {
+// Per-warp counts and ranks in one pass over each warp's chunk range: whist[w][e] (zeroed
+// here) ends as warp w's count of expert e, and lrk[i] is the count of sel[i]'s expert in
+// the warp's earlier chunks plus a position among the chunk's lanes of that expert.  A
+// shared-memory atomic hands these out, so the lanes of one chunk sharing an expert may come
+// out in any order; fix_order restores selection order.
+__device__ void count_rank_warp(const uint16_t* sel, int n, int E, int* whist, uint16_t* lrk) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* h = whist + warp * E;
+    for (int e = lane; e < E; e += 32) h[e] = 0;
+    __syncwarp();
     int c0, c1;
     warp_ranges(n, c0, c1);
     for (int c = c0; c < c1; ++c) {  // every lane runs every chunk: the warp stays converged
         const int i = c * 32 + lane;
         if (i < n) {
             const int e = (int)sel[i];
-            if (e < E) stage_sel[atomicAdd(h + e, 1)] = i;
+            if (e < E) lrk[i] = (uint16_t)atomicAdd(h + e, 1);
         }
-        __syncwarp();  // chunk c's positions are taken before chunk c + 1's
+        __syncwarp();  // chunk c's ranks are taken before chunk c + 1's
+    }
+}
+
+// CTA-sorted position of every selection of this warp's chunk range: loc[e] (the CTA's
+// offset of expert e) + whist[w][e] (warp w's offset inside it) + lrk[i].
+__device__ void place_sorted(const uint16_t* sel, int n, int E, const int* loc, const int* whist,
+                             const uint16_t* lrk, int* stage_sel) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int* h = whist + warp * E;
+    int c0, c1;
+    warp_ranges(n, c0, c1);
+    for (int i = c0 * 32 + lane; i < min(n, c1 * 32); i += 32) {
+        const int e = (int)sel[i];
+        if (e < E) stage_sel[loc[e] + h[e] + lrk[i]] = i;
     }
 }
 
@@ -705,15 +721,17 @@ __device__ void fix_order(const uint16_t* sel, int nvalid, int* stage_sel) {
 // offsets, prefix partial sums, and (staged writes) the three rank arrays.
 __host__ __device__ constexpr size_t tile_maps_ints(int nthreads, int E, int n, bool staged) {
     return (size_t)(nthreads / 32) * E + tile_align_c(E + 1, 4) +
-           (size_t)2 * (nthreads / (E / 4)) * E + (staged ? (size_t)2 * n : 0);
+           (size_t)2 * (nthreads / (E / 4)) * E + (staged ? (size_t)2 * n + (n + 1) / 2 : 0);
 }
 
 // Maps phases of the tile kernel (E % 4 == 0, blockDim >= E/4), after the CTA's selections
 // sel[0..n) (16-bit experts, tokens t0..) are in shared memory.  free_sm: the ring, free now.
 // As maps_finish, with:
+//   count + rank   one pass of shared-memory atomics gives the per-warp counts and each
+//                  selection's rank inside its warp (count_rank_warp)
 //   arrive early   the grid barrier is entered right after the CTA histogram is published;
 //                  the CTA-local expert offsets and (staged) the CTA-sorted positions of all
-//                  selections (rank_atomic + fix_order) are computed while others arrive
+//                  selections (place_sorted + fix_order) are computed while others arrive
 //   prefix         every thread issues its 128-bit loads of group sums and earlier rows of
 //                  its group before summing; partial sums meet in shared memory
 //   staged writes  p2u in CTA-sorted order (one run of consecutive rows per expert) and u2p
@@ -736,9 +754,13 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     int* part_t = part_b + R * E;
     int* stage_sel = part_t + R * E;
     int* stage_r = stage_sel + n;
+    uint16_t* lrk = reinterpret_cast<uint16_t*>(stage_r + n);
 
     __syncthreads();  // selections complete; the ring is free
-    count_per_warp(sel, n, E, whist);
+    if (staged)
+        count_rank_warp(sel, n, E, whist, lrk);
+    else
+        count_per_warp(sel, n, E, whist);
     __syncthreads();
     scan_over_warps(E, whist, hist);  // hist = CTA histogram, whist exclusive over warps
     for (int e = tid; e < E; e += nthr) {
@@ -750,16 +772,16 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     // While the other CTAs arrive: CTA-local expert offsets and CTA-sorted positions.
     scan_experts(hist, E, loc, scratch);  // barriers inside
     __syncthreads();
-    for (int e = tid; e < E; e += nthr) {
-        const int l = loc[e];
-        for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += l;
-    }
-    __syncthreads();
     const int nvalid = loc[E];
     if (staged) {
-        rank_atomic(sel, n, E, whist, stage_sel);
+        place_sorted(sel, n, E, loc, whist, lrk, stage_sel);
         __syncthreads();
         fix_order(sel, nvalid, stage_sel);
+    } else {
+        for (int e = tid; e < E; e += nthr) {
+            const int l = loc[e];
+            for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += l;
+        }
     }
     if (!grid_wait(ws, (unsigned)grid)) return;
     pdl_launch();
@@ -837,20 +859,15 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
         rank_scatter(sel, n, t0, T, E, K, whist, p2u, u2p);
     }
 
+    // Every CTA has used the group sums it loaded before it counts itself out here; kernel
+    // completion makes the last CTA's reset visible to the next call.
     __shared__ int last;
     __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        last = (atomicAdd(ws.bar, 1u) == 2u * (unsigned)grid - 1u);
-    }
+    if (tid == 0) last = (atomicAdd(ws.bar, 1u) == 2u * (unsigned)grid - 1u);
     __syncthreads();
     if (last) {
         for (int i = tid; i < ng * E; i += nthr) ws.gsum[i] = 0;
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            atomicExch(ws.bar, 0u);
-        }
+        if (tid == 0) atomicExch(ws.bar, 0u);
     }
 }
 
