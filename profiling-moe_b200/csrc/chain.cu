@@ -8,14 +8,15 @@
 //   B  sandwich: h = r + RMSNorm(attn_out)*g1 ; moe_in = RMSNorm(h)*g2          main CTA
 //   C  router GEMV: logits[t][e] = float(bf16(moe_in[t] . W[e]))                gate CTAs
 //   D  router (top-K of logits + bias, sigmoid weights) and expert maps         main CTA
-//   E  activation expansion: permuted[r] = moe_in[p2u[r] % T]                    main CTA
+//   E  activation expansion: permuted[r] = moe_in[p2u[r] % T]     main CTA (gate CTAs at T=1)
 //   F  post-MoE pair: r = h + RMSNorm(moe_out)*g3 ; next = RMSNorm(r)*g4         main CTA
 // The main CTA (block 0) runs every stage but C and keeps r, h and moe_in of its rows in
 // shared memory.  Every other CTA (one per remaining SM) owns up to four experts of the
 // router GEMV: it streams its rows of W for the next layer into shared memory while the main
-// CTA works, waits for the layer's `go` word, computes its logits and counts itself `done`.
-// Those two words are the only cross-CTA synchronisation; every wait is bounded and sets an
-// error word when it gives up.  The arithmetic is that of the stand-alone kernels
+// CTA works, waits for the layer's `go` word, computes its logits and publishes each one with
+// the layer's tag in a 64-bit record, which the main CTA polls (the logits arrive with the
+// tag).  `go` and the records are the only cross-CTA synchronisation; every wait is bounded
+// and sets an error word when it gives up.  The arithmetic is that of the stand-alone kernels
 // (norm_math.cuh, route_math.cuh, the Q/K formula of qk_norm_rope.cu), so each stage gives
 // the same bits as its own kernel would on the same inputs.
 #include "kb_common.cuh"
@@ -32,7 +33,7 @@ using bf16 = __nv_bfloat16;
 
 constexpr int kCT = 512;                     // threads per CTA
 constexpr int kCW = kCT / 32;                // warps per CTA
-constexpr int kMaxGateCtas = 960;            // done words in the workspace
+constexpr int kMaxGateCtas = 960;            // gate CTAs with logit records in the workspace
 constexpr int kChainMaxLayers = 256;         // layer descriptors held in shared memory
 constexpr int kMaxChunks = E_MAX / 32;       // 32-expert chunks of the router
 constexpr int kChainMaxT = 4;                // tokens per call
@@ -70,7 +71,9 @@ struct ChainParams {
     int32_t* u2p;
     float* trace_logits;
     unsigned* go;    // layers whose moe_in rows are published; 0 between calls
-    unsigned* done;  // [gate CTAs] layers finished by each gate CTA; 0 between calls
+    // [gate CTAs][kGateMaxExperts][kChainMaxT] logit records: (layer + 1) << 32 | float bits,
+    // written by the gate CTAs with one 64-bit store each; 0 between calls
+    unsigned long long* rec;
     int* err;        // non-zero once a wait gave up (the workspace must be re-zeroed)
 };
 
@@ -81,6 +84,15 @@ __device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
 }
 __device__ __forceinline__ void st_rel(unsigned* p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// 64-bit accesses are single-copy atomic: a record's tag and value are seen together.
+__device__ __forceinline__ void st_rec(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_rec(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ void cp16(void* dst, const void* src) {
@@ -182,7 +194,6 @@ struct MainSmem {
     int* flag;    // [4]
     kb_chain_layer_t* layers;  // [kChainMaxLayers]
     float* xrow;  // [kChainMaxT][E_MAX] logits of the layer
-    int* cand;    // [kChainMaxT][kMaxChunks][kChainMaxK] chunk winners
     float* bias;  // [E_MAX] gate bias of the layer (+0 for -0), 0 without one
 };
 
@@ -190,7 +201,7 @@ __host__ __device__ constexpr size_t main_smem_bytes(int H) {
     return (size_t)3 * kChainMaxT * H * sizeof(bf16) + 2 * kChainMaxT * kHalfD * sizeof(float) +
            (size_t)kRedRows * 33 * sizeof(float) + (2 * E_MAX + 4 + 32 + 32 + 64 + 4) * sizeof(int) +
            (size_t)kChainMaxLayers * sizeof(kb_chain_layer_t) +
-           (size_t)(kChainMaxT * E_MAX + kChainMaxT * kMaxChunks * kChainMaxK + E_MAX) * 4;
+           (size_t)(kChainMaxT * E_MAX + E_MAX) * 4;
 }
 __host__ __device__ constexpr size_t gate_smem_bytes(int H) {
     return (size_t)2 * kGateMaxExperts * H * sizeof(bf16) + (size_t)kRedRows * 33 * sizeof(float) +
@@ -213,8 +224,7 @@ __device__ MainSmem carve_main(unsigned char* smem, int H) {
     m.flag = m.scratch + 64;
     m.layers = reinterpret_cast<kb_chain_layer_t*>(m.flag + 4);
     m.xrow = reinterpret_cast<float*>(m.layers + kChainMaxLayers);
-    m.cand = reinterpret_cast<int*>(m.xrow + kChainMaxT * E_MAX);
-    m.bias = reinterpret_cast<float*>(m.cand + kChainMaxT * kMaxChunks * kChainMaxK);
+    m.bias = m.xrow + kChainMaxT * E_MAX;
     return m;
 }
 
@@ -410,69 +420,60 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
 
 // D: exact top-K per token, then the weights and the maps of the T*K <= 32 selections.
 // Same keys and tie rule as the router kernels: score = logit + (bias + 0), ordered by okey
-// (NaN highest), the lower expert index first.  Two steps: every warp takes the top-K of one
-// 32-expert chunk of one token (one expert per lane), then warp t merges the chunk winners
-// of token t (at most 16 chunks * K candidates).  The bias row sits in shared memory
-// (bias_sm, filled at the start of the layer) and the logits are copied there for the
-// weights.
-__device__ __forceinline__ void warp_topk_round(uint32_t& key, int idx, int K, int lane,
-                                                int* out_idx) {
-    for (int r = 0; r < K; ++r) {
-        const uint32_t wmax = __reduce_max_sync(FULL_MASK, key);
-        const unsigned cand = (key == wmax && key != 0u) ? (unsigned)idx : 0xffffffffu;
-        const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
-        if (cand == widx) key = 0u;
-        if (lane == 0) out_idx[r] = (int)widx;  // 0xffffffff (-1): fewer than K candidates
-    }
-}
-
+// (NaN highest), the lower expert index first.  Warp t ranks token t on its own: lane l
+// holds experts l, l + 32, ... (kMaxChunks keys), and each of K rounds takes the warp's
+// largest key, the lowest expert among equal keys (redux max, then redux min), and clears
+// it.  The bias row (bias_sm, filled at the start of the layer) and the layer's logits
+// (xrow, filled from the gate records) sit in shared memory.
 __device__ __noinline__ void stage_route_maps(const ChainParams& p, const float* bias_sm,
                                              const MainSmem& s) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int T = p.T, E = p.E, K = p.K, n = T * K;
-    const int nch = (E + 31) >> 5;  // 32-expert chunks per token
     cp_wait<0>();  // the bias row of this layer
     __syncthreads();
-    // Step 1: (token, chunk) pairs over the warps.
-    for (int pc = warp; pc < T * nch; pc += kCW) {
-        const int t = pc / nch, c = pc - t * nch;
-        const int e = c * 32 + lane;
-        const float x = __ldcg(p.logits + (size_t)t * E + min(e, E - 1));
-        uint32_t key = (e < E) ? okey(x + (bias_sm[min(e, E - 1)] + 0.0f)) : 0u;
-        if (e < E) s.xrow[t * E_MAX + e] = x;
-        warp_topk_round(key, e, K, lane, s.cand + (t * kMaxChunks + c) * kChainMaxK);
-    }
-    __syncthreads();
-    // Step 2: warp t merges token t's chunk winners (lane l holds candidates l, l+32, ...).
     if (warp < T) {
         const int t = warp;
-        const int* cd = s.cand + t * kMaxChunks * kChainMaxK;
-        const int nc = nch * K;
-        uint32_t key[(kMaxChunks * kChainMaxK + 31) / 32];
-        int idx[(kMaxChunks * kChainMaxK + 31) / 32];
+        uint32_t key[kMaxChunks];
 #pragma unroll
-        for (int j = 0; j < (kMaxChunks * kChainMaxK + 31) / 32; ++j) {
-            const int i = lane + 32 * j;
-            const int cc = i / K, r = i - cc * K;
-            const int e = (i < nc) ? cd[cc * kChainMaxK + r] : -1;
-            idx[j] = e;
-            key[j] = (e >= 0) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
+        for (int j = 0; j < kMaxChunks; ++j) {  // logits arrived with the gate records
+            const int e = lane + 32 * j;
+            key[j] = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
         }
+        static_assert(kMaxChunks == 16, "four-level tournament");
         for (int r = 0; r < K; ++r) {
-            uint32_t best = 0u;
-            int bi = 0x7fffffff;
+            // Lane maximum by a 4-level tournament of (key, j); the right side wins only on a
+            // strictly larger key, so the lowest j (expert) of the lane wins ties.
+            uint32_t k8[8], k4[4], k2[2];
+            int j8[8], j4[4], j2[2];
 #pragma unroll
-            for (int j = 0; j < (kMaxChunks * kChainMaxK + 31) / 32; ++j)
-                if (key[j] > best || (key[j] == best && key[j] != 0u && idx[j] < bi)) {
-                    best = key[j];
-                    bi = idx[j];
-                }
+            for (int u = 0; u < 8; ++u) {
+                const bool rt = key[2 * u + 1] > key[2 * u];
+                k8[u] = rt ? key[2 * u + 1] : key[2 * u];
+                j8[u] = rt ? 2 * u + 1 : 2 * u;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const bool rt = k8[2 * u + 1] > k8[2 * u];
+                k4[u] = rt ? k8[2 * u + 1] : k8[2 * u];
+                j4[u] = rt ? j8[2 * u + 1] : j8[2 * u];
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const bool rt = k4[2 * u + 1] > k4[2 * u];
+                k2[u] = rt ? k4[2 * u + 1] : k4[2 * u];
+                j2[u] = rt ? j4[2 * u + 1] : j4[2 * u];
+            }
+            const bool rt = k2[1] > k2[0];
+            const uint32_t best = rt ? k2[1] : k2[0];
+            const int bj = rt ? j2[1] : j2[0];
             const uint32_t wmax = __reduce_max_sync(FULL_MASK, best);
-            const unsigned cand = (best == wmax && best != 0u) ? (unsigned)bi : 0xffffffffu;
+            const unsigned cand = (best == wmax && best != 0u) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
             const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
+            if (cand == widx) {
 #pragma unroll
-            for (int j = 0; j < (kMaxChunks * kChainMaxK + 31) / 32; ++j)
-                if (idx[j] == (int)widx) key[j] = 0u;
+                for (int j = 0; j < kMaxChunks; ++j)
+                    if (j == bj) key[j] = 0u;
+            }
             if (lane == 0) s.sel[t * K + r] = (int)widx;
         }
         __syncwarp();
@@ -514,13 +515,51 @@ __device__ __noinline__ void stage_route_maps(const ChainParams& p, const float*
     __syncthreads();
 }
 
-// E: permuted rows straight from the moe_in rows held in shared memory.
+// E: permuted rows straight from the moe_in rows held in shared memory (T > 1).  At T == 1
+// every selection is token 0, so the K permuted rows are copies of moe_in whatever the
+// routing: the gate CTAs write them while they compute the router GEMV (chain_gate).
 __device__ __noinline__ void stage_expand(const ChainParams& p, const MainSmem& s) {
     const int nvec = p.H / 8, n = p.T * p.K;
     for (int r = 0; r < n; ++r) {
         const uint4* src = reinterpret_cast<const uint4*>(s.x + (size_t)s.perm[r] * p.H);
         uint4* dst = reinterpret_cast<uint4*>(p.permuted + (size_t)r * p.H);
         for (int v = threadIdx.x; v < nvec; v += kCT) st_stream(dst + v, src[v]);
+    }
+}
+
+// Waits (bounded) until every logit record of gate CTA c carries `tag`, then stores the
+// logits in xrow[t][e].  A failed wait sets the error word.
+__device__ bool take_records(const ChainParams& p, unsigned c, unsigned gate_ctas, unsigned tag,
+                             float* xrow) {
+    const unsigned long long* rc = p.rec + (size_t)c * kGateMaxExperts * kChainMaxT;
+    const int T = p.T, E = p.E;
+    long long it = 0;
+    while (true) {
+        unsigned long long r[kGateMaxExperts][kChainMaxT];
+        bool all = true;
+#pragma unroll
+        for (int m = 0; m < kGateMaxExperts; ++m)
+#pragma unroll
+            for (int t = 0; t < kChainMaxT; ++t) {
+                const bool used = (int)(c + m * gate_ctas) < E && t < T;
+                r[m][t] = used ? ld_rec(rc + m * kChainMaxT + t) : ((unsigned long long)tag << 32);
+                all = all && (unsigned)(r[m][t] >> 32) == tag;
+            }
+        if (all) {
+#pragma unroll
+            for (int m = 0; m < kGateMaxExperts; ++m)
+#pragma unroll
+                for (int t = 0; t < kChainMaxT; ++t) {
+                    const int e = (int)(c + m * gate_ctas);
+                    if (e < E && t < T) xrow[t * E_MAX + e] = __uint_as_float((unsigned)r[m][t]);
+                }
+            return true;
+        }
+        if (++it > kChainSpin || ((it & 1023) == 0 && *(volatile int*)p.err)) {
+            atomicExch(p.err, 1);
+            return false;
+        }
+        __nanosleep(32);
     }
 }
 
@@ -581,23 +620,25 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
             st_rel(p.go, (unsigned)(l + 1));
         }
         __syncthreads();
-        // Every gate CTA has its own done word; one thread waits on each, all at once.
+        // One thread per gate CTA polls that CTA's logit records (all loads of a poll in
+        // flight at once) until each carries this layer's tag; the logits arrive with it.
         for (unsigned c = threadIdx.x; c < gate_ctas; c += kCT)
-            if (!wait_geq(p.done + c, (unsigned)(l + 1), p.err)) s.flag[0] = 0;
+            if (!take_records(p, c, gate_ctas, (unsigned)(l + 1), s.xrow)) s.flag[0] = 0;
         __syncthreads();
         if (!s.flag[0]) {
             for (int e = threadIdx.x; e <= p.E; e += kCT) p.offsets[e] = -1;
             return;
         }
         stage_route_maps(p, s.bias, s);
-        stage_expand(p, s);
+        if (p.T > 1) stage_expand(p, s);  // T == 1: the gate CTAs wrote it
         stage_pair<VPT, TT>(p, p.moe_out, s.h, static_cast<const bf16*>(Ly.g_post_ffn),
                         static_cast<const bf16*>(Ly.g_input_ln), s.r, p.r_out, p.nxt, nullptr,
                         s.red);
         __syncthreads();
     }
-    // Every gate CTA has passed its last wait: the words can return to zero.
-    for (unsigned c = threadIdx.x; c < gate_ctas; c += kCT) p.done[c] = 0u;
+    // Every gate CTA has written its last records: they and go can return to zero.
+    for (unsigned i = threadIdx.x; i < gate_ctas * kGateMaxExperts * kChainMaxT; i += kCT)
+        p.rec[i] = 0ull;
     if (threadIdx.x == 0) *p.go = 0u;
 }
 
@@ -639,6 +680,14 @@ __device__ __noinline__ void chain_gate(const ChainParams& p, unsigned char* sme
         if (!ok) {
             cp_wait<0>();
             return;
+        }
+        if (T == 1 && p.permuted) {  // this CTA's share of the K copies of moe_in (expansion)
+            const int total = p.K * nvec, per = (total + G1 - 1) / G1;
+            for (int i = j * per + threadIdx.x; i < min(total, (j + 1) * per); i += kCT) {
+                const int v = i % nvec;
+                st_stream(reinterpret_cast<uint4*>(p.permuted) + i,
+                          __ldcg(reinterpret_cast<const uint4*>(p.moe_in) + v));
+            }
         }
         const bf16* wl = wb + (size_t)(l & 1) * kGateMaxExperts * H;
         // Warp w computes expert m = w / kQuarters over quarter q = w % kQuarters of H for
@@ -690,9 +739,10 @@ __device__ __noinline__ void chain_gate(const ChainParams& p, unsigned char* sme
             const int e = j + mm * G1;
             p.logits[(size_t)t * E + e] = v;
             if (p.trace_logits) p.trace_logits[((size_t)l * T + t) * E + e] = v;
+            st_rec(p.rec + ((size_t)j * kGateMaxExperts + mm) * kChainMaxT + t,
+                   ((unsigned long long)(l + 1) << 32) | __float_as_uint(v));
         }
-        __syncthreads();
-        if (threadIdx.x == 0) st_rel(p.done + j, (unsigned)(l + 1));  // after the barrier above
+        __syncthreads();  // this layer's reads of moe_in and of the W buffer are over
     }
 }
 
@@ -759,7 +809,9 @@ int sm_count() {
 
 using namespace kb;
 
-extern "C" size_t kb_decode_chain_workspace_bytes(void) { return 256 + 4 * kMaxGateCtas; }
+extern "C" size_t kb_decode_chain_workspace_bytes(void) {
+    return 256 + (size_t)8 * kMaxGateCtas * kGateMaxExperts * kChainMaxT;
+}
 
 extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, const void* attn_out,
                                const void* moe_out, const void* q, const void* k,
@@ -824,7 +876,7 @@ extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, con
     unsigned char* wsb = static_cast<unsigned char*>(workspace);
     prm.go = reinterpret_cast<unsigned*>(wsb);
     prm.err = reinterpret_cast<int*>(wsb + 128);
-    prm.done = reinterpret_cast<unsigned*>(wsb + 256);
+    prm.rec = reinterpret_cast<unsigned long long*>(wsb + 256);
     const size_t smem = std::max(main_smem_bytes(H), gate_smem_bytes(H));
     const RowShape rs = row_shape(H / 8);
     const int vpt = rs.vpt;
