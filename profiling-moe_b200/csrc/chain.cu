@@ -243,15 +243,19 @@ __device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer
     const int ngroups = (nh + 7) >> 3;
     const bool rope = !Ly.rnope && p.pos != nullptr;
     for (int g0 = warp; g0 < ngroups; g0 += kCW * kQkChunk) {
-        V8 xv[kQkChunk][4];
+        V8 xv[kQkChunk][4], gv[kQkChunk][4];
 #pragma unroll
         for (int c = 0; c < kQkChunk; ++c) {  // clamped heads: every load in flight at once
             const int hd = min((g0 + c * kCW) * 8 + slot, nh - 1);
             const int t = hd / HH, hh = hd - t * HH;
             const bf16* src = hh < p.Hq ? p.q + ((size_t)t * p.Hq + hh) * 128
                                         : p.k + ((size_t)t * p.Hkv + (hh - p.Hq)) * 128;
+            const bf16* gsrc = static_cast<const bf16*>(hh < p.Hq ? Ly.g_q : Ly.g_k) + pl * 32;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) xv[c][u].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 32) + u);
+            for (int u = 0; u < 4; ++u) {
+                xv[c][u].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 32) + u);
+                gv[c][u].u = __ldg(reinterpret_cast<const uint4*>(gsrc) + u);
+            }
         }
 #pragma unroll
         for (int c = 0; c < kQkChunk; ++c) {
@@ -283,22 +287,27 @@ __device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer
             const float a20 = a4[0] + a4[2], a21 = a4[1] + a4[3];                  // level 2
             const float ss = a20 + a21;                                             // level 1
             const float r = 1.0f / sqrtf(ss / 128.0f + p.eps);
-            V8 g[4];  // this lane's gamma slice (L1 after the first head)
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-                g[u].u = __ldg(reinterpret_cast<const uint4*>(
-                    static_cast<const bf16*>(is_q ? Ly.g_q : Ly.g_k) + pl * 32) + u);
+            const V8* g = gv[c];  // this lane's gamma slice, loaded with the head
 #pragma unroll
             for (int k = 0; k < 32; ++k)
                 y[k] = __fmul_rn(__fmul_rn(y[k], r), __bfloat162float(g[k >> 3].e[k & 7]));
             V8 o[4];
             if (rope) {
                 const bool first_half = pl < 2;
+                // cos/sin of this lane's elements k: angles j = (pl*32 + k) mod 64, 4 at a time
+                const float4* cs4 = reinterpret_cast<const float4*>(s.cs + t * kHalfD + ((pl * 32) & (kHalfD - 1)));
+                const float4* sn4 = reinterpret_cast<const float4*>(s.sn + t * kHalfD + ((pl * 32) & (kHalfD - 1)));
+                float cv[32], svv[32];
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const float4 a = cs4[m], b = sn4[m];
+                    cv[4 * m] = a.x; cv[4 * m + 1] = a.y; cv[4 * m + 2] = a.z; cv[4 * m + 3] = a.w;
+                    svv[4 * m] = b.x; svv[4 * m + 1] = b.y; svv[4 * m + 2] = b.z; svv[4 * m + 3] = b.w;
+                }
 #pragma unroll
                 for (int k = 0; k < 32; ++k) {
                     const float other = __shfl_xor_sync(FULL_MASK, y[k], 2);
-                    const int j = (pl * 32 + k) & (kHalfD - 1);
-                    const float cc = s.cs[t * kHalfD + j], sv = s.sn[t * kHalfD + j];
+                    const float cc = cv[k], sv = svv[k];
                     const float v = first_half ? __fsub_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv))
                                                : __fadd_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv));
                     o[k >> 3].e[k & 7] = __float2bfloat16_rn(v);
