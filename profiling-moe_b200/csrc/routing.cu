@@ -832,8 +832,10 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     __syncthreads();
     if (staged) {
         // p2u in CTA-sorted order: each expert's rows are consecutive.
-        for (int i = tid; i < n; i += nthr) stage_r[i] = -1;  // ids outside [0, E)
-        __syncthreads();
+        if (nvalid < n) {  // ids outside [0, E) keep u2p = -1
+            for (int i = tid; i < n; i += nthr) stage_r[i] = -1;
+            __syncthreads();
+        }
         for (int j = tid; j < nvalid; j += nthr) {
             const int i = stage_sel[j];
             const int r = hist[sel[i]] + j;
@@ -1532,9 +1534,17 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
                 const int cnt = rows * K;
                 int32_t* gi = ids_out + tb * K;
                 float* gw = w + tb * K;
-                for (int j = lane; j < cnt; j += 32) {
-                    gi[j] = oi[j];
-                    gw[j] = ow[j];
+                if (((reinterpret_cast<uintptr_t>(gi) | reinterpret_cast<uintptr_t>(gw)) & 15u) == 0 &&
+                    (cnt & 3) == 0) {  // 16-byte stores when both rows start aligned
+                    for (int j = lane; j < (cnt >> 2); j += 32) {
+                        reinterpret_cast<int4*>(gi)[j] = reinterpret_cast<const int4*>(oi)[j];
+                        reinterpret_cast<float4*>(gw)[j] = reinterpret_cast<const float4*>(ow)[j];
+                    }
+                } else {
+                    for (int j = lane; j < cnt; j += 32) {
+                        gi[j] = oi[j];
+                        gw[j] = ow[j];
+                    }
                 }
             }
             __syncwarp();
