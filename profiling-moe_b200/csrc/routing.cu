@@ -1270,7 +1270,8 @@ __device__ __forceinline__ void topk_merge(uint32_t (&key)[KM], int (&idx)[KM], 
     idx[0] = gt[0] ? jj : idx[0];
 }
 
-template <int E_, int KT>
+// MAPS = false: the router alone (kb_router), a plain launch: no selections, no map phases.
+template <int E_, int KT, bool MAPS = true>
 __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
     const __grid_constant__ CUtensorMap tmap, const float* __restrict__ logits,
     const float* __restrict__ bias, int32_t* __restrict__ ids_out, float* __restrict__ w,
@@ -1297,7 +1298,11 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
     uint64_t* full = reinterpret_cast<uint64_t*>(scratch + 64);
     uint64_t* empty = full + nslot;
     int* whist = reinterpret_cast<int*>(ring);
-    if (ws_poisoned(ws, E_, offsets)) return;
+    if constexpr (MAPS) {
+        if (ws_poisoned(ws, E_, offsets)) return;
+    } else {
+        pdl_launch();
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x;
     const int64_t t0 = (int64_t)c * tpc;
@@ -1509,7 +1514,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
                     if (i < K) {
                         oi[lane * K + i] = idx[i];
                         ow[lane * K + i] = wv[i];
-                        sp[i] = (uint16_t)idx[i];
+                        if constexpr (MAPS) sp[i] = (uint16_t)idx[i];
                     }
                 }
             }
@@ -1525,7 +1530,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
                 if (lane < K) {
                     oi[l * K + lane] = id;
                     ow[l * K + lane] = wl;
-                    sel[(int)(tb + l - t0) * K + lane] = (uint16_t)id;
+                    if constexpr (MAPS) sel[(int)(tb + l - t0) * K + lane] = (uint16_t)id;
                 }
                 __syncwarp();
             }
@@ -1550,10 +1555,12 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
             __syncwarp();
         }
     }
-    const bool staged =
-        tile_maps_ints(blockDim.x, E_, n, true) <= (size_t)nslot * C::SLOT_FLOATS;
-    maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, whist, staged, counts,
-                         offsets, p2u, u2p);
+    if constexpr (MAPS) {
+        const bool staged =
+            tile_maps_ints(blockDim.x, E_, n, true) <= (size_t)nslot * C::SLOT_FLOATS;
+        maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, whist, staged,
+                             counts, offsets, p2u, u2p);
+    }
 }
 
 // Hybrid router for kb_router: each warp takes a contiguous range of tokens.
@@ -2400,6 +2407,41 @@ __global__ void zero_offsets_kernel(int64_t* offsets, int32_t* counts, int E) {
 
 using namespace kb;
 
+namespace kb {
+namespace {
+// kb_router through the tile kernel without its map phases (fp32 weights, E = 32*VPL in
+// {128, 256, 384}, K <= 8, T >= 32, when its shared memory fits).  Returns
+// KB_ERR_UNSUPPORTED, having launched nothing, when that path does not apply.
+template <int VPL>
+int tile_router(const float* logits, const float* bias, int32_t* ids, float* w, int64_t T, int E,
+                int K, int renorm, cudaStream_t st) {
+    constexpr int E_ = 32 * VPL;
+    if constexpr (E_ > 384) {
+        return KB_ERR_UNSUPPORTED;
+    } else {
+        MapsPlan p{};
+        if (!aligned16(logits) || !RouterMaps<VPL, true>::plan_tile(p, T, E, K))
+            return KB_ERR_UNSUPPORTED;
+        if (!make_tile_map(&p.tmap, logits, T, E)) return KB_ERR_UNSUPPORTED;
+        auto* kern = (K == 6) ? maps_tile_kernel<E_, 6, false> : maps_tile_kernel<E_, 0, false>;
+        int err = allow_smem(kern, p.smem_persist);
+        if (err) return err;
+        return launch(kern, dim3(p.grid), dim3(32 * (1 + 2 * p.tnw)), p.smem_persist, st, p.tmap,
+                      logits, bias, ids, w, T, K, renorm, p.tpc, p.tnw,
+                      static_cast<int32_t*>(nullptr), static_cast<int64_t*>(nullptr),
+                      static_cast<int32_t*>(nullptr), static_cast<int32_t*>(nullptr), PersistWs{});
+    }
+}
+int tile_router_any(const float* logits, const float* bias, int32_t* ids, float* w, int64_t T,
+                    int E, int K, int renorm, cudaStream_t st) {
+    if (E == 384) return tile_router<12>(logits, bias, ids, w, T, E, K, renorm, st);
+    if (E == 256) return tile_router<8>(logits, bias, ids, w, T, E, K, renorm, st);
+    if (E == 128) return tile_router<4>(logits, bias, ids, w, T, E, K, renorm, st);
+    return KB_ERR_UNSUPPORTED;
+}
+}  // namespace
+}  // namespace kb
+
 extern "C" int kb_router(const float* logits, const float* bias, int32_t* ids, void* weights,
                          int w_dtype, int64_t T, int E, int K, int renorm, kb_stream_t stream) {
     int st = check_common(T, E, K);
@@ -2408,6 +2450,11 @@ extern "C" int kb_router(const float* logits, const float* bias, int32_t* ids, v
     if (!logits || !ids || !weights) return KB_ERR_INVALID_ARG;
     if (w_dtype != KB_F32 && w_dtype != KB_BF16 && w_dtype != KB_F16) return KB_ERR_UNSUPPORTED;
     if ((E % 128 == 0) && (!aligned16(logits) || (bias && !aligned16(bias)))) return KB_ERR_ALIGNMENT;
+    if (w_dtype == KB_F32 && K <= 8) {  // large T: the tile kernel's routing phase alone
+        const int tr = tile_router_any(logits, bias, ids, static_cast<float*>(weights), T, E, K,
+                                       renorm, (cudaStream_t)stream);
+        if (tr != KB_ERR_UNSUPPORTED) return tr;
+    }
     return with_layout<RouterLaunch>(E, logits, bias, ids, weights, w_dtype, T, E, K, renorm,
                                      (cudaStream_t)stream);
 }

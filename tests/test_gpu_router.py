@@ -131,3 +131,21 @@ def test_router_reference_entry_points(api):
         api.kolibri_cuda_ops.forward(torch.randn(4, 100, device="cuda"), bc[:100], 6)
     with pytest.raises(RuntimeError, match="topk=6"):
         api.kolibri_cuda_ops.forward(lc, bc, 4)
+
+
+@pytest.mark.parametrize("E", [128, 256, 384])
+@pytest.mark.parametrize("k", [6, 8])
+def test_router_tile_path_adversarial_rows(E, k):
+    # T >= 32, fp32 weights, K <= 8: kb_router runs the tile kernel's routing phase.
+    from test_gpu_maps import _adversarial_logits
+    x = _adversarial_logits(E)
+    g = torch.Generator().manual_seed(7 * E + k)
+    bias = torch.randint(-1, 2, (E,), generator=g).float()
+    bias[::5] = -0.0
+    for b in (None, bias):
+        for renorm in (False, True):
+            ids, w = ops.router(x.cuda(), None if b is None else b.cuda(), k=k, renorm=renorm)
+            rid, rw = orc.router_ref(x, b, k=k, renorm=renorm)
+            assert torch.equal(ids.cpu(), rid), \
+                f"rows {torch.nonzero((ids.cpu() != rid).any(1))[:8].flatten().tolist()}"
+            torch.testing.assert_close(w.cpu(), rw, rtol=W_RTOL, atol=0, equal_nan=True)
