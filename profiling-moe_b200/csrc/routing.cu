@@ -1270,11 +1270,12 @@ __device__ __forceinline__ void topk_merge(uint32_t (&key)[KM], int (&idx)[KM], 
     idx[0] = gt[0] ? jj : idx[0];
 }
 
-// MAPS = false: the router alone (kb_router), a plain launch: no selections, no map phases.
-template <int E_, int KT, bool MAPS = true>
+// MAPS = false: the router alone (kb_router), a plain launch: no selections, no map phases;
+// WT: the weights' type (fp32 with the maps; fp32, bf16 or fp16 for the router alone).
+template <int E_, int KT, bool MAPS = true, typename WT = float>
 __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
     const __grid_constant__ CUtensorMap tmap, const float* __restrict__ logits,
-    const float* __restrict__ bias, int32_t* __restrict__ ids_out, float* __restrict__ w,
+    const float* __restrict__ bias, int32_t* __restrict__ ids_out, WT* __restrict__ w,
     int64_t T, int K_rt, int renorm, int tpc, int nslot, int32_t* __restrict__ counts,
     int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p,
     PersistWs ws) {
@@ -1538,8 +1539,9 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
             {
                 const int cnt = rows * K;
                 int32_t* gi = ids_out + tb * K;
-                float* gw = w + tb * K;
-                if (((reinterpret_cast<uintptr_t>(gi) | reinterpret_cast<uintptr_t>(gw)) & 15u) == 0 &&
+                WT* gw = w + tb * K;
+                if (sizeof(WT) == 4 &&
+                    ((reinterpret_cast<uintptr_t>(gi) | reinterpret_cast<uintptr_t>(gw)) & 15u) == 0 &&
                     (cnt & 3) == 0) {  // 16-byte stores when both rows start aligned
                     for (int j = lane; j < (cnt >> 2); j += 32) {
                         reinterpret_cast<int4*>(gi)[j] = reinterpret_cast<const int4*>(oi)[j];
@@ -1548,7 +1550,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
                 } else {
                     for (int j = lane; j < cnt; j += 32) {
                         gi[j] = oi[j];
-                        gw[j] = ow[j];
+                        gw[j] = Elem<WT>::from_f(ow[j]);
                     }
                 }
             }
@@ -2409,11 +2411,11 @@ using namespace kb;
 
 namespace kb {
 namespace {
-// kb_router through the tile kernel without its map phases (fp32 weights, E = 32*VPL in
-// {128, 256, 384}, K <= 8, T >= 32, when its shared memory fits).  Returns
+// kb_router through the tile kernel without its map phases (E = 32*VPL in {128, 256, 384},
+// K <= 8, T >= 32, when its shared memory fits; weights rounded to WT at the store).  Returns
 // KB_ERR_UNSUPPORTED, having launched nothing, when that path does not apply.
-template <int VPL>
-int tile_router(const float* logits, const float* bias, int32_t* ids, float* w, int64_t T, int E,
+template <int VPL, typename WT>
+int tile_router(const float* logits, const float* bias, int32_t* ids, WT* w, int64_t T, int E,
                 int K, int renorm, cudaStream_t st) {
     constexpr int E_ = 32 * VPL;
     if constexpr (E_ > 384) {
@@ -2423,7 +2425,7 @@ int tile_router(const float* logits, const float* bias, int32_t* ids, float* w, 
         if (!aligned16(logits) || !RouterMaps<VPL, true>::plan_tile(p, T, E, K))
             return KB_ERR_UNSUPPORTED;
         if (!make_tile_map(&p.tmap, logits, T, E)) return KB_ERR_UNSUPPORTED;
-        auto* kern = (K == 6) ? maps_tile_kernel<E_, 6, false> : maps_tile_kernel<E_, 0, false>;
+        auto* kern = (K == 6) ? maps_tile_kernel<E_, 6, false, WT> : maps_tile_kernel<E_, 0, false, WT>;
         int err = allow_smem(kern, p.smem_persist);
         if (err) return err;
         return launch(kern, dim3(p.grid), dim3(32 * (1 + 2 * p.tnw)), p.smem_persist, st, p.tmap,
@@ -2432,11 +2434,12 @@ int tile_router(const float* logits, const float* bias, int32_t* ids, float* w, 
                       static_cast<int32_t*>(nullptr), static_cast<int32_t*>(nullptr), PersistWs{});
     }
 }
-int tile_router_any(const float* logits, const float* bias, int32_t* ids, float* w, int64_t T,
+template <typename WT>
+int tile_router_any(const float* logits, const float* bias, int32_t* ids, WT* w, int64_t T,
                     int E, int K, int renorm, cudaStream_t st) {
-    if (E == 384) return tile_router<12>(logits, bias, ids, w, T, E, K, renorm, st);
-    if (E == 256) return tile_router<8>(logits, bias, ids, w, T, E, K, renorm, st);
-    if (E == 128) return tile_router<4>(logits, bias, ids, w, T, E, K, renorm, st);
+    if (E == 384) return tile_router<12, WT>(logits, bias, ids, w, T, E, K, renorm, st);
+    if (E == 256) return tile_router<8, WT>(logits, bias, ids, w, T, E, K, renorm, st);
+    if (E == 128) return tile_router<4, WT>(logits, bias, ids, w, T, E, K, renorm, st);
     return KB_ERR_UNSUPPORTED;
 }
 }  // namespace
@@ -2450,9 +2453,12 @@ extern "C" int kb_router(const float* logits, const float* bias, int32_t* ids, v
     if (!logits || !ids || !weights) return KB_ERR_INVALID_ARG;
     if (w_dtype != KB_F32 && w_dtype != KB_BF16 && w_dtype != KB_F16) return KB_ERR_UNSUPPORTED;
     if ((E % 128 == 0) && (!aligned16(logits) || (bias && !aligned16(bias)))) return KB_ERR_ALIGNMENT;
-    if (w_dtype == KB_F32 && K <= 8) {  // large T: the tile kernel's routing phase alone
-        const int tr = tile_router_any(logits, bias, ids, static_cast<float*>(weights), T, E, K,
-                                       renorm, (cudaStream_t)stream);
+    if (K <= 8) {  // large T: the tile kernel's routing phase alone
+        const cudaStream_t cs = (cudaStream_t)stream;
+        const int tr =
+            w_dtype == KB_F32 ? tile_router_any(logits, bias, ids, static_cast<float*>(weights), T, E, K, renorm, cs)
+            : w_dtype == KB_BF16 ? tile_router_any(logits, bias, ids, static_cast<__nv_bfloat16*>(weights), T, E, K, renorm, cs)
+                                 : tile_router_any(logits, bias, ids, static_cast<__half*>(weights), T, E, K, renorm, cs);
         if (tr != KB_ERR_UNSUPPORTED) return tr;
     }
     return with_layout<RouterLaunch>(E, logits, bias, ids, weights, w_dtype, T, E, K, renorm,

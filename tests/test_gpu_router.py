@@ -149,3 +149,20 @@ def test_router_tile_path_adversarial_rows(E, k):
             assert torch.equal(ids.cpu(), rid), \
                 f"rows {torch.nonzero((ids.cpu() != rid).any(1))[:8].flatten().tolist()}"
             torch.testing.assert_close(w.cpu(), rw, rtol=W_RTOL, atol=0, equal_nan=True)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_router_tile_path_tails_and_dtypes(dtype, api):
+    # Token counts around the 32-row tile and CTA boundaries, weights in each output type.
+    for T in (32, 33, 63, 4767, 148 * 32 * 3 + 5):
+        logits, bias = wl.router_inputs(T, seed=T + 1)
+        ids, w = api.fused_kolibri_router(logits.cuda(), bias.cuda(), k=6, output_dtype=dtype)
+        rid, rw = orc.router_ref(logits, bias)
+        assert torch.equal(ids.cpu(), rid), T
+        if dtype == torch.float32:
+            torch.testing.assert_close(w.cpu(), rw, rtol=W_RTOL, atol=0)
+        else:
+            # The fp32 weight agrees with the oracle to ~1e-6, so one that sits on a rounding
+            # boundary of the output type may round to the neighbouring value: 1 ulp.
+            ulp = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10  # 1 ulp, relative
+            torch.testing.assert_close(w.cpu().float(), rw.to(dtype).float(), rtol=ulp, atol=0)
