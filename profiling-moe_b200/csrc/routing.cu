@@ -659,9 +659,11 @@ __device__ bool grid_wait(const PersistWs& ws, unsigned target) {
 
 // Per-warp counts and ranks in one pass over each warp's chunk range: whist[w][e] (zeroed
 // here) ends as warp w's count of expert e, and lrk[i] is the count of sel[i]'s expert in
-// the warp's earlier chunks plus a position among the chunk's lanes of that expert.  A
-// shared-memory atomic hands these out, so the lanes of one chunk sharing an expert may come
-// out in any order; fix_order restores selection order.
+// the warp's earlier chunk groups plus a position among the group's selections of that
+// expert.  A shared-memory atomic hands these out, kCountGroup chunks (32 selections each)
+// at a time, so the selections of one group sharing an expert may come out in any order;
+// fix_order restores selection order.
+constexpr int kCountGroup = 4;
 __device__ void count_rank_warp(const uint16_t* sel, int n, int E, int* whist, uint16_t* lrk) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* h = whist + warp * E;
@@ -669,13 +671,16 @@ __device__ void count_rank_warp(const uint16_t* sel, int n, int E, int* whist, u
     __syncwarp();
     int c0, c1;
     warp_ranges(n, c0, c1);
-    for (int c = c0; c < c1; ++c) {  // every lane runs every chunk: the warp stays converged
-        const int i = c * 32 + lane;
-        if (i < n) {
-            const int e = (int)sel[i];
-            if (e < E) lrk[i] = (uint16_t)atomicAdd(h + e, 1);
+    for (int c = c0; c < c1; c += kCountGroup) {  // every lane runs every group: converged
+#pragma unroll
+        for (int u = 0; u < kCountGroup; ++u) {
+            const int i = (c + u) * 32 + lane;
+            if (c + u < c1 && i < n) {
+                const int e = (int)sel[i];
+                if (e < E) lrk[i] = (uint16_t)atomicAdd(h + e, 1);
+            }
         }
-        __syncwarp();  // chunk c's ranks are taken before chunk c + 1's
+        __syncwarp();  // this group's ranks are taken before the next group's
     }
 }
 
@@ -695,11 +700,12 @@ __device__ void place_sorted(const uint16_t* sel, int n, int E, const int* loc, 
 
 // Odd-even transposition over stage_sel[0..nvalid) (sorted by expert): swaps neighbours of
 // one expert whose selection indices are out of order.  Out-of-order entries only span the
-// lanes of one 32-wide chunk, so 16 double rounds sort them; the loop stops at the first
-// round without a swap.  Block-wide (barriers inside).
+// selections of one group of count_rank_warp (kCountGroup * 32), so kCountGroup * 16 double
+// rounds sort them; the loop stops at the first round without a swap.  Block-wide (barriers
+// inside).
 __device__ void fix_order(const uint16_t* sel, int nvalid, int* stage_sel) {
     const int tid = threadIdx.x, nthr = blockDim.x;
-    for (int round = 0; round < 17; ++round) {
+    for (int round = 0; round < kCountGroup * 16 + 1; ++round) {
         int swapped = 0;
 #pragma unroll 1
         for (int ph = 0; ph < 2; ++ph) {
