@@ -125,8 +125,11 @@ __device__ bool wait_geq(const unsigned* p, unsigned target, int* err) {
 }
 
 // Block-wide sums of n values at once; each value is reduced exactly as block_sum reduces
-// it (warp butterfly, then warp 0 over the warp partials).  red: n*33 floats, which may be
-// reused by the next call without a barrier in between.
+// it (warp butterfly, then a butterfly over the warp partials, lanes past the last warp
+// adding 0).  Every warp runs the second butterfly itself: a butterfly leaves the same bits
+// in every lane, so each warp gets warp 0's result, and one barrier does.  red: MAXN*33
+// floats, read after the barrier; the next call must take another buffer (two calls in
+// turn on two buffers are safe: a call's barrier follows every read of the buffer before).
 template <int MAXN>
 __device__ __forceinline__ void block_sum_n(float (&v)[MAXN], int n, float* red) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -139,20 +142,9 @@ __device__ __forceinline__ void block_sum_n(float (&v)[MAXN], int n, float* red)
         }
     }
     __syncthreads();
-    if (warp == 0) {
-        for (int m = 0; m < n; ++m) {
-            float s = (lane < nw) ? red[m * 33 + lane] : 0.0f;
-            s = warp_sum(s);
-            if (lane == 0) red[m * 33 + 32] = s;
-        }
-    }
-    __syncthreads();
 #pragma unroll
     for (int m = 0; m < MAXN; ++m)
-        if (m < n) v[m] = red[m * 33 + 32];
-    // No trailing barrier: a following reduction on the same buffer writes the partial slots
-    // before its first barrier and the result slot only after it, when every thread has
-    // read this result.
+        if (m < n) v[m] = warp_sum((lane < nw) ? red[m * 33 + lane] : 0.0f);
 }
 
 union V8 {
@@ -362,6 +354,7 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
 #pragma unroll
         for (int i = 0; i < VPT; ++i)
             if (tid + i * PT >= nvec) va[t][i].u = make_uint4(0, 0, 0, 0);
+    static_assert(2 * TT <= kRedRows, "two reduction buffers of TT rows");
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
         if (t < T) {
@@ -404,7 +397,7 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
             }
         }
     }
-    block_sum_n<TT>(ss2, T, red);
+    block_sum_n<TT>(ss2, T, red + TT * 33);
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
         if (t < T) {
@@ -596,6 +589,7 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
             s.sn[i] = sv;
         }
     }
+    if (threadIdx.x == 0) s.flag[0] = 1;  // cleared only on a failed wait, which returns
     __syncthreads();
     for (int l = 0; l < p.L; ++l) {
         const kb_chain_layer_t& Ly = s.layers[l];
@@ -624,11 +618,8 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
         stage_pair<VPT, TT>(p, p.attn_out, s.r, static_cast<const bf16*>(Ly.g_post_attn),
                         static_cast<const bf16*>(Ly.g_pre_moe), s.h, p.h, p.moe_in, s.x, s.red);
         __syncthreads();
-        if (threadIdx.x == 0) {  // the barrier above orders every thread's rows before it
-            s.flag[0] = 1;
-            st_rel(p.go, (unsigned)(l + 1));
-        }
-        __syncthreads();
+        // The barrier above orders every thread's rows before the release.
+        if (threadIdx.x == 0) st_rel(p.go, (unsigned)(l + 1));
         // One thread per gate CTA polls that CTA's logit records (all loads of a poll in
         // flight at once) until each carries this layer's tag; the logits arrive with it.
         for (unsigned c = threadIdx.x; c < gate_ctas; c += kCT)
