@@ -6,22 +6,21 @@
 
 namespace kb {
 
-// Block-wide fp32 sum; `red` is a 33-float smem scratch.  All threads get the result.
-__device__ __forceinline__ float block_sum(float v, float* red) {
+// Block-wide fp32 sum: a warp butterfly, then a butterfly over the warp partials (lanes past
+// the last warp adding 0).  Every warp runs the second butterfly itself, which leaves the
+// same bits in every lane of every warp, so one barrier does.  `red` is a 64-float smem
+// scratch of two 32-float buffers taken in turn (`turn` flips on each call and must start
+// equal in every thread): a call's barrier follows every read of the buffer it leaves
+// behind, so the call after it may write that buffer again.  All threads get the result.
+__device__ __forceinline__ float block_sum(float v, float* red, int& turn) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nw = (blockDim.x + 31) >> 5;
+    float* buf = red + 32 * turn;
+    turn ^= 1;
     v = warp_sum(v);
-    if (lane == 0) red[warp] = v;
+    if (lane == 0) buf[warp] = v;
     __syncthreads();
-    if (warp == 0) {
-        float s = (lane < nw) ? red[lane] : 0.0f;
-        s = warp_sum(s);
-        if (lane == 0) red[32] = s;
-    }
-    __syncthreads();
-    const float r = red[32];
-    __syncthreads();  // red is reused by the next reduction
-    return r;
+    return warp_sum((lane < nw) ? buf[lane] : 0.0f);
 }
 
 __device__ __forceinline__ float rms_scale(float ss, int H, float eps) {

@@ -29,7 +29,8 @@ __global__ void __launch_bounds__(1024) residual_norm_pair_kernel(
     pdl_launch();
     using V = Vec16<T>;
     constexpr int N = V::N;
-    __shared__ float red[33];
+    __shared__ float red[64];
+    int turn = 0;
     const int nvec = H / N;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const uint4* pa = reinterpret_cast<const uint4*>(a + row * H);
@@ -52,7 +53,7 @@ __global__ void __launch_bounds__(1024) residual_norm_pair_kernel(
                 ss = fmaf(x, x, ss);
             }
         }
-        const float r1 = rms_scale(block_sum(ss, red), H, eps);
+        const float r1 = rms_scale(block_sum(ss, red, turn), H, eps);
         float ss2 = 0.0f;
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(1024) residual_norm_pair_kernel(
                 reinterpret_cast<uint4*>(sum_out + row * H)[v] = vh.u;
             }
         }
-        const float r2 = rms_scale(block_sum(ss2, red), H, eps);
+        const float r2 = rms_scale(block_sum(ss2, red, turn), H, eps);
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
             const int v = threadIdx.x + i * blockDim.x;
@@ -100,7 +101,8 @@ __global__ void __launch_bounds__(1024) add_rms_norm_kernel(
     pdl_launch();
     using V = Vec16<T>;
     constexpr int N = V::N;
-    __shared__ float red[33];
+    __shared__ float red[64];
+    int turn = 0;
     const int nvec = H / N;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const uint4* pa = reinterpret_cast<const uint4*>(a + row * H);
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__(1024) add_rms_norm_kernel(
                 vs[i].u = make_uint4(0, 0, 0, 0);
             }
         }
-        const float r = rms_scale(block_sum(ss, red), H, eps);
+        const float r = rms_scale(block_sum(ss, red, turn), H, eps);
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
             const int v = threadIdx.x + i * blockDim.x;
@@ -153,7 +155,8 @@ __global__ void __launch_bounds__(512) residual_norm_pair_generic(
     pdl_wait();
     pdl_launch();
     extern __shared__ float rowbuf[];
-    __shared__ float red[33];
+    __shared__ float red[64];
+    int turn = 0;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         float ss = 0.0f;
         for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(512) residual_norm_pair_generic(
             rowbuf[i] = x;
             ss = fmaf(x, x, ss);
         }
-        const float r1 = rms_scale(block_sum(ss, red), H, eps);
+        const float r1 = rms_scale(block_sum(ss, red, turn), H, eps);
         float ss2 = 0.0f;
         for (int i = threadIdx.x; i < H; i += blockDim.x) {
             const float post = rnd<T>(__fmul_rn(__fmul_rn(rowbuf[i], r1), Elem<T>::to_f(g1[i])));
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(512) residual_norm_pair_generic(
             sum_out[row * H + i] = h;
             ss2 = fmaf(hf, hf, ss2);
         }
-        const float r2 = rms_scale(block_sum(ss2, red), H, eps);
+        const float r2 = rms_scale(block_sum(ss2, red, turn), H, eps);
         for (int i = threadIdx.x; i < H; i += blockDim.x)
             norm_out[row * H + i] =
                 Elem<T>::from_f(__fmul_rn(__fmul_rn(rowbuf[i], r2), Elem<T>::to_f(g2[i])));
@@ -186,7 +189,8 @@ __global__ void __launch_bounds__(512) add_rms_norm_generic(
     pdl_wait();
     pdl_launch();
     extern __shared__ float rowbuf[];
-    __shared__ float red[33];
+    __shared__ float red[64];
+    int turn = 0;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         float ss = 0.0f;
         for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -197,7 +201,7 @@ __global__ void __launch_bounds__(512) add_rms_norm_generic(
             rowbuf[i] = x;
             ss = fmaf(x, x, ss);
         }
-        const float r = rms_scale(block_sum(ss, red), H, eps);
+        const float r = rms_scale(block_sum(ss, red, turn), H, eps);
         for (int i = threadIdx.x; i < H; i += blockDim.x)
             out[row * H + i] =
                 Elem<T>::from_f(__fmul_rn(__fmul_rn(rowbuf[i], r), Elem<T>::to_f(g[i])));
