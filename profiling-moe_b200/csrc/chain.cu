@@ -178,8 +178,8 @@ struct MainSmem {
     float* cs;    // [kChainMaxT][64]
     float* sn;    // [kChainMaxT][64]
     float* red;   // [kRedRows][33]
-    int* hist;    // [E_MAX]
-    int* offs;    // [E_MAX + 4]
+    int* hist;    // [E_MAX]  routing: group maxima [kChainMaxT][32]
+    int* offs;    // [E_MAX + 4]  routing: candidates (u64) [kChainMaxT][32]
     int* sel;     // [32]
     int* perm;    // [32]  token of each permuted row
     int* scratch; // [64]
@@ -227,7 +227,7 @@ __device__ MainSmem carve_main(unsigned char* smem, int H) {
 // output, has the same bits.  The NeoX partner of element j (j +- 64) sits in lane p^2.
 constexpr int kQkChunk = 1;  // head groups per warp with loads in flight together
 
-__device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer_t& Ly,
+__device__ __forceinline__ void stage_qk(const ChainParams& p, const kb_chain_layer_t& Ly,
                                      const MainSmem& s) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = lane >> 2, pl = lane & 3;  // head slot in the warp, lane in the head
@@ -325,7 +325,7 @@ __device__ __noinline__ void stage_qk(const ChainParams& p, const kb_chain_layer
 // a comes from global memory (read-only during the launch), res from shared memory.
 // sum goes to sum_sm (and sum_g if non-null), norm to norm_g (and norm_sm if non-null).
 template <int VPT, int TT>
-__device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, const bf16* res_sm,
+__device__ __forceinline__ void stage_pair(const ChainParams& p, const bf16* a, const bf16* res_sm,
                            const bf16* g1, const bf16* g2, bf16* sum_sm, bf16* sum_g,
                            bf16* norm_g, bf16* norm_sm, float* red) {
     const int T = p.T, H = p.H, nvec = H / 8;
@@ -420,63 +420,119 @@ __device__ __noinline__ void stage_pair(const ChainParams& p, const bf16* a, con
     }
 }
 
+// Top-K of token t by K rounds over all of its keys (lane l holds experts l, l + 32, ...):
+// each round takes the warp's largest key, the lowest expert among equal keys (redux max,
+// then redux min), and clears it.  The path for rows whose keys tie at the threshold.
+__device__ void topk_rounds(const MainSmem& s, const float* bias_sm, int t, int E, int K) {
+    const int lane = threadIdx.x & 31;
+    uint32_t key[kMaxChunks];
+#pragma unroll
+    for (int j = 0; j < kMaxChunks; ++j) {
+        const int e = lane + 32 * j;
+        key[j] = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
+    }
+    static_assert(kMaxChunks == 16, "four-level tournament");
+    for (int r = 0; r < K; ++r) {
+        // Lane maximum by a 4-level tournament of (key, j); the right side wins only on a
+        // strictly larger key, so the lowest j (expert) of the lane wins ties.
+        uint32_t k8[8], k4[4], k2[2];
+        int j8[8], j4[4], j2[2];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const bool rt = key[2 * u + 1] > key[2 * u];
+            k8[u] = rt ? key[2 * u + 1] : key[2 * u];
+            j8[u] = rt ? 2 * u + 1 : 2 * u;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const bool rt = k8[2 * u + 1] > k8[2 * u];
+            k4[u] = rt ? k8[2 * u + 1] : k8[2 * u];
+            j4[u] = rt ? j8[2 * u + 1] : j8[2 * u];
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const bool rt = k4[2 * u + 1] > k4[2 * u];
+            k2[u] = rt ? k4[2 * u + 1] : k4[2 * u];
+            j2[u] = rt ? j4[2 * u + 1] : j4[2 * u];
+        }
+        const bool rt = k2[1] > k2[0];
+        const uint32_t best = rt ? k2[1] : k2[0];
+        const int bj = rt ? j2[1] : j2[0];
+        const uint32_t wmax = __reduce_max_sync(FULL_MASK, best);
+        const unsigned cand = (best == wmax && best != 0u) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
+        const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
+        if (cand == widx) {
+#pragma unroll
+            for (int j = 0; j < kMaxChunks; ++j)
+                if (j == bj) key[j] = 0u;
+        }
+        if (lane == 0) s.sel[t * K + r] = (int)widx;
+    }
+}
+
 // D: exact top-K per token, then the weights and the maps of the T*K <= 32 selections.
 // Same keys and tie rule as the router kernels: score = logit + (bias + 0), ordered by okey
-// (NaN highest), the lower expert index first.  Warp t ranks token t on its own: lane l
-// holds experts l, l + 32, ... (kMaxChunks keys), and each of K rounds takes the warp's
-// largest key, the lowest expert among equal keys (redux max, then redux min), and clears
-// it.  The bias row (bias_sm, filled at the start of the layer) and the layer's logits
-// (xrow, filled from the gate records) sit in shared memory.
-__device__ __noinline__ void stage_route_maps(const ChainParams& p, const float* bias_sm,
+// (NaN highest), the lower expert index first.  The bias row (bias_sm) and the layer's
+// logits (xrow, filled from the gate records) sit in shared memory, complete at entry.
+//  1. Every warp, per (token, 32-expert chunk): the key of each expert and the maximum of
+//     each group of G consecutive experts, G the smallest power of two giving ng <= 32
+//     groups (so ng >= K: ng > 16 whenever G > 1, and ng = E >= K when G = 1).
+//  2. Per (token, chunk) again: tau = the K-th largest group maximum (the least maximum
+//     with fewer than K maxima above it).  The K groups with the largest maxima hold K keys
+//     >= tau, so every key of the top K is >= tau; those keys are the candidates, appended
+//     to the token's list (a shared-memory counter hands out the slots).
+//  3. Warp t: with C <= 32 candidates, each one's rank is the number of candidates above it
+//     in (key, then lower expert) order, found in one pass; ranks below K are the output.
+//     Rows with more candidates (ties at tau) take the K rounds of topk_rounds.
+__device__ __forceinline__ void stage_route_maps(const ChainParams& p, const float* bias_sm,
                                              const MainSmem& s) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int T = p.T, E = p.E, K = p.K, n = T * K;
-    cp_wait<0>();  // the bias row of this layer
+    const int nch = (E + 31) >> 5, units = T * nch;
+    int lg = 0;  // log2 G
+    while (((E + (1 << lg) - 1) >> lg) > 32) ++lg;
+    const int ng = (E + (1 << lg) - 1) >> lg;
+    uint32_t* gmax = reinterpret_cast<uint32_t*>(s.hist);                  // [kChainMaxT][32]
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(s.offs);  // [kChainMaxT][32]
+    int* ncand = s.scratch;                                                 // [kChainMaxT]
+    if ((int)threadIdx.x < T) ncand[threadIdx.x] = 0;
+    for (int u = warp; u < units; u += kCW) {  // 1: uniform trip count within the warp
+        const int t = u / nch, e = (u - t * nch) * 32 + lane;
+        uint32_t k = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+            if (o < (1 << lg)) k = max(k, __shfl_xor_sync(FULL_MASK, k, o));
+        if ((lane & ((1 << lg) - 1)) == 0 && e < E) gmax[t * 32 + (e >> lg)] = k;
+    }
     __syncthreads();
-    if (warp < T) {
+    for (int u = warp; u < units; u += kCW) {  // 2
+        const int t = u / nch, e = (u - t * nch) * 32 + lane;
+        const uint32_t m = lane < ng ? gmax[t * 32 + lane] : 0u;  // valid maxima are > 0
+        int above = 0;
+#pragma unroll
+        for (int h = 0; h < 32; ++h) above += (__shfl_sync(FULL_MASK, m, h) > m) ? 1 : 0;
+        const uint32_t tau = __reduce_min_sync(FULL_MASK, (lane < ng && above < K) ? m : 0xffffffffu);
+        const uint32_t k = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
+        const bool take = e < E && k >= tau;
+        const unsigned b = __ballot_sync(FULL_MASK, take);
+        int base = 0;
+        if (lane == 0 && b) base = atomicAdd(ncand + t, __popc(b));
+        base = __shfl_sync(FULL_MASK, base, 0);
+        const int slot = base + __popc(b & ((1u << lane) - 1u));
+        if (take && slot < 32)
+            cand[t * 32 + slot] = ((unsigned long long)k << 32) | (unsigned)(0xffffffffu - (unsigned)e);
+    }
+    __syncthreads();
+    if (warp < T) {  // 3
         const int t = warp;
-        uint32_t key[kMaxChunks];
-#pragma unroll
-        for (int j = 0; j < kMaxChunks; ++j) {  // logits arrived with the gate records
-            const int e = lane + 32 * j;
-            key[j] = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
-        }
-        static_assert(kMaxChunks == 16, "four-level tournament");
-        for (int r = 0; r < K; ++r) {
-            // Lane maximum by a 4-level tournament of (key, j); the right side wins only on a
-            // strictly larger key, so the lowest j (expert) of the lane wins ties.
-            uint32_t k8[8], k4[4], k2[2];
-            int j8[8], j4[4], j2[2];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const bool rt = key[2 * u + 1] > key[2 * u];
-                k8[u] = rt ? key[2 * u + 1] : key[2 * u];
-                j8[u] = rt ? 2 * u + 1 : 2 * u;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const bool rt = k8[2 * u + 1] > k8[2 * u];
-                k4[u] = rt ? k8[2 * u + 1] : k8[2 * u];
-                j4[u] = rt ? j8[2 * u + 1] : j8[2 * u];
-            }
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const bool rt = k4[2 * u + 1] > k4[2 * u];
-                k2[u] = rt ? k4[2 * u + 1] : k4[2 * u];
-                j2[u] = rt ? j4[2 * u + 1] : j4[2 * u];
-            }
-            const bool rt = k2[1] > k2[0];
-            const uint32_t best = rt ? k2[1] : k2[0];
-            const int bj = rt ? j2[1] : j2[0];
-            const uint32_t wmax = __reduce_max_sync(FULL_MASK, best);
-            const unsigned cand = (best == wmax && best != 0u) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
-            const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
-            if (cand == widx) {
-#pragma unroll
-                for (int j = 0; j < kMaxChunks; ++j)
-                    if (j == bj) key[j] = 0u;
-            }
-            if (lane == 0) s.sel[t * K + r] = (int)widx;
+        const int C = ncand[t];
+        if (C <= 32) {
+            const unsigned long long mine = lane < C ? cand[t * 32 + lane] : 0ull;
+            int rank = 0;
+            for (int j = 0; j < C; ++j) rank += (cand[t * 32 + j] > mine) ? 1 : 0;
+            if (lane < C && rank < K) s.sel[t * K + rank] = (int)(0xffffffffu - (unsigned)mine);
+        } else {
+            topk_rounds(s, bias_sm, t, E, K);
         }
         __syncwarp();
         if (lane < K) {
@@ -520,7 +576,7 @@ __device__ __noinline__ void stage_route_maps(const ChainParams& p, const float*
 // E: permuted rows straight from the moe_in rows held in shared memory (T > 1).  At T == 1
 // every selection is token 0, so the K permuted rows are copies of moe_in whatever the
 // routing: the gate CTAs write them while they compute the router GEMV (chain_gate).
-__device__ __noinline__ void stage_expand(const ChainParams& p, const MainSmem& s) {
+__device__ __forceinline__ void stage_expand(const ChainParams& p, const MainSmem& s) {
     const int nvec = p.H / 8, n = p.T * p.K;
     for (int r = 0; r < n; ++r) {
         const uint4* src = reinterpret_cast<const uint4*>(s.x + (size_t)s.perm[r] * p.H);
@@ -566,7 +622,7 @@ __device__ bool take_records(const ChainParams& p, unsigned c, unsigned gate_cta
 }
 
 template <int VPT, int TT>
-__device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* smem) {
+__device__ __forceinline__ void chain_main(const ChainParams& p, unsigned char* smem) {
     const int T = p.T, H = p.H, nvec = H / 8;
     const MainSmem s = carve_main(smem, H);
     const unsigned gate_ctas = gridDim.x - 1;
@@ -602,16 +658,17 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
         cp_commit();
         if (l + 1 < p.L) {  // the next layer's small weights into L2
             const kb_chain_layer_t& Ln = s.layers[l + 1];
-            const char* bases[4] = {static_cast<const char*>(Ln.g_post_attn),
-                                    static_cast<const char*>(Ln.g_pre_moe),
-                                    static_cast<const char*>(Ln.g_post_ffn),
-                                    static_cast<const char*>(Ln.g_input_ln)};
             if (Ln.gate_bias && threadIdx.x < (p.E * 4 + 127) / 128)
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(
                     reinterpret_cast<const char*>(Ln.gate_bias) + threadIdx.x * 128));
             const int lines = (H * 2 + 127) / 128;
-            for (int i = threadIdx.x; i < 4 * lines; i += kCT)
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(bases[i / lines] + (size_t)(i % lines) * 128));
+            for (int i = threadIdx.x; i < 4 * lines; i += kCT) {
+                const int w = i / lines;  // selects, not an indexed array (which lives on the stack)
+                const void* base = w == 0 ? Ln.g_post_attn : w == 1 ? Ln.g_pre_moe
+                                 : w == 2 ? Ln.g_post_ffn : Ln.g_input_ln;
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(
+                    static_cast<const char*>(base) + (size_t)(i - w * lines) * 128));
+            }
         }
         stage_qk(p, Ly, s);
         __syncthreads();
@@ -624,6 +681,7 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
         // flight at once) until each carries this layer's tag; the logits arrive with it.
         for (unsigned c = threadIdx.x; c < gate_ctas; c += kCT)
             if (!take_records(p, c, gate_ctas, (unsigned)(l + 1), s.xrow)) s.flag[0] = 0;
+        cp_wait<0>();  // this thread's part of the bias row; the barrier shares it
         __syncthreads();
         if (!s.flag[0]) {
             for (int e = threadIdx.x; e <= p.E; e += kCT) p.offsets[e] = -1;
@@ -648,7 +706,7 @@ __device__ __noinline__ void chain_main(const ChainParams& p, unsigned char* sme
 constexpr int kQuarters = kCW / kGateMaxExperts;  // warps sharing one expert's dot product
 
 template <int VQ, int TT>
-__device__ __noinline__ void chain_gate(const ChainParams& p, unsigned char* smem) {
+__device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* smem) {
     const int G1 = gridDim.x - 1, j = blockIdx.x - 1;
     const int H = p.H, E = p.E, T = p.T, nvec = H / 8;
     bf16* wb = reinterpret_cast<bf16*>(smem);  // [2][kGateMaxExperts][H]

@@ -145,3 +145,54 @@ def test_decode_chain_kernel_rejects_large_batches():
     chain = dc.DecodeChain(5, dc.make_layers(1, dev), dev)
     with pytest.raises(ValueError):
         chain.run_mega(torch.cuda.current_stream())
+
+
+def _tied_layers(case, dev):
+    """One layer whose router rows make the kernel's candidate filter meet ties, NaN and
+    small expert counts: (E, K, layers)."""
+    E, K = {"all_equal": (384, 6), "tie40": (384, 6), "tie20": (384, 8),
+            "nan_inf": (384, 6), "e40": (40, 6), "e24": (24, 8), "e8": (8, 8)}[case]
+    layers = dc.make_layers(1, dev, E=E)
+    L = layers[0]
+    g = torch.Generator(device="cpu").manual_seed(11)
+    if case == "all_equal":        # every score equal: more than 32 candidates
+        L.w_gate_t[:] = L.w_gate_t[0].clone()
+        L.gate_bias.zero_()
+    elif case in ("tie40", "tie20"):
+        n = 40 if case == "tie40" else 20
+        S = torch.randperm(E, generator=g)[:n].to(dev)
+        L.w_gate_t[S] = L.w_gate_t[0].clone()
+        L.gate_bias[S] = 10.0     # the tied set on top; tie40 overflows the 32 candidates
+    elif case == "nan_inf":
+        S = torch.randperm(E, generator=g)[:5].to(dev)
+        L.gate_bias[S[:3]] = float("nan")
+        L.gate_bias[S[3:]] = float("-inf")
+    return E, K, layers
+
+
+@pytest.mark.parametrize("case", ["all_equal", "tie40", "tie20", "nan_inf", "e40", "e24", "e8"])
+@pytest.mark.parametrize("T", [1, 3])
+def test_decode_chain_kernel_routing_ties_and_small_E(case, T):
+    """kb_decode_chain's router on rows with tied scores (more and fewer than 32 keys at the
+    threshold), NaN and -inf biases, and expert counts below 32 * K: ids, weights, maps and
+    expansion against the oracle on the kernel's own logits."""
+    dev = torch.device("cuda")
+    E, K, layers = _tied_layers(case, dev)
+    chain = dc.DecodeChain(T, layers, dev, E=E, K=K)
+    s = torch.cuda.Stream()
+    trace = torch.full((1, T, E), float("nan"), device=dev)
+    chain.run_mega(s, trace=trace)
+    torch.cuda.synchronize()
+    last = trace[0].cpu()
+    bias = layers[0].gate_bias.cpu()
+    rid, rw = orc.router_ref(last, bias, k=K)
+    assert torch.equal(chain.ids.cpu(), rid)
+    torch.testing.assert_close(chain.w.cpu(), rw, rtol=1e-6, atol=0)
+    rc, roff, rp2u, ru2p = orc.expert_maps_ref(rid, E)
+    np.testing.assert_array_equal(np_of(chain.counts), rc)
+    np.testing.assert_array_equal(np_of(chain.offsets), roff)
+    np.testing.assert_array_equal(np_of(chain.p2u), rp2u)
+    np.testing.assert_array_equal(np_of(chain.u2p), ru2p)
+    assert torch.equal(chain.permuted.cpu(), orc.expansion_ref(chain.moe_in.cpu(), rp2u))
+    if case == "all_equal":
+        assert rid.tolist() == [list(range(K))] * T
