@@ -289,20 +289,19 @@ __device__ __forceinline__ void stage_qk(const ChainParams& p, const kb_chain_la
                 // cos/sin of this lane's elements k: angles j = (pl*32 + k) mod 64, 4 at a time
                 const float4* cs4 = reinterpret_cast<const float4*>(s.cs + t * kHalfD + ((pl * 32) & (kHalfD - 1)));
                 const float4* sn4 = reinterpret_cast<const float4*>(s.sn + t * kHalfD + ((pl * 32) & (kHalfD - 1)));
-                float cv[32], svv[32];
 #pragma unroll
-                for (int m = 0; m < 8; ++m) {
+                for (int m = 0; m < 8; ++m) {  // four elements per float4 of cos and of sin
                     const float4 a = cs4[m], b = sn4[m];
-                    cv[4 * m] = a.x; cv[4 * m + 1] = a.y; cv[4 * m + 2] = a.z; cv[4 * m + 3] = a.w;
-                    svv[4 * m] = b.x; svv[4 * m + 1] = b.y; svv[4 * m + 2] = b.z; svv[4 * m + 3] = b.w;
-                }
+                    const float cc4[4] = {a.x, a.y, a.z, a.w}, sv4[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    const float other = __shfl_xor_sync(FULL_MASK, y[k], 2);
-                    const float cc = cv[k], sv = svv[k];
-                    const float v = first_half ? __fsub_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv))
-                                               : __fadd_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv));
-                    o[k >> 3].e[k & 7] = __float2bfloat16_rn(v);
+                    for (int q = 0; q < 4; ++q) {
+                        const int k = 4 * m + q;
+                        const float other = __shfl_xor_sync(FULL_MASK, y[k], 2);
+                        const float cc = cc4[q], sv = sv4[q];
+                        const float v = first_half ? __fsub_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv))
+                                                   : __fadd_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv));
+                        o[k >> 3].e[k & 7] = __float2bfloat16_rn(v);
+                    }
                 }
             } else {
 #pragma unroll
@@ -712,20 +711,16 @@ __device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* 
     bf16* wb = reinterpret_cast<bf16*>(smem);  // [2][kGateMaxExperts][H]
     float* red = reinterpret_cast<float*>(wb + (size_t)2 * kGateMaxExperts * H);
     __shared__ int ok;
-    int ex[kGateMaxExperts];
-    int ne = 0;
+    int ne = 0;  // this CTA's experts: j + m * G1 for m < ne
 #pragma unroll
-    for (int m = 0; m < kGateMaxExperts; ++m) {
-        const int e = j + m * G1;
-        ex[m] = e;
-        if (e < E) ne = m + 1;
-    }
+    for (int m = 0; m < kGateMaxExperts; ++m)
+        if (j + m * G1 < E) ne = m + 1;
     auto issue = [&](int l) {
         const bf16* W = static_cast<const bf16*>(p.layers[l].w_gate_t);
         bf16* dst = wb + (size_t)(l & 1) * kGateMaxExperts * H;
         for (int m = 0; m < ne; ++m)
             for (int v = threadIdx.x; v < nvec; v += kCT)
-                cp16(dst + (size_t)m * H + v * 8, W + (size_t)ex[m] * H + v * 8);
+                cp16(dst + (size_t)m * H + v * 8, W + (size_t)(j + m * G1) * H + v * 8);
         cp_commit();
     };
     issue(0);
@@ -739,14 +734,16 @@ __device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* 
             cp_wait<0>();
             return;
         }
-        if (T == 1 && p.permuted) {  // this CTA's share of the K copies of moe_in (expansion)
-            const int total = p.K * nvec, per = (total + G1 - 1) / G1;
-            for (int i = j * per + threadIdx.x; i < min(total, (j + 1) * per); i += kCT) {
-                const int v = i % nvec;
-                st_stream(reinterpret_cast<uint4*>(p.permuted) + i,
-                          __ldcg(reinterpret_cast<const uint4*>(p.moe_in) + v));
-            }
-        }
+        // T == 1: this CTA's share [x0, x1) of the K copies of moe_in (the expansion).  The
+        // first vector of each thread is loaded here and stored after the dot products, so
+        // its L2 round trip overlaps them; every copy is stored before the barrier that
+        // precedes this CTA's records, so moe_in is read before the main CTA can move on.
+        const int xtotal = (T == 1 && p.permuted) ? p.K * nvec : 0;
+        const int xper = (xtotal + G1 - 1) / G1;
+        const int x0 = min(xtotal, j * xper), x1 = min(xtotal, x0 + xper);
+        const int xi = x0 + (int)threadIdx.x;
+        uint4 xcopy = make_uint4(0, 0, 0, 0);
+        if (xi < x1) xcopy = __ldcg(reinterpret_cast<const uint4*>(p.moe_in) + xi % nvec);
         const bf16* wl = wb + (size_t)(l & 1) * kGateMaxExperts * H;
         // Warp w computes expert m = w / kQuarters over quarter q = w % kQuarters of H for
         // every token: its W vectors once from shared memory, each token's moe_in vectors
@@ -787,6 +784,10 @@ __device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* 
                 if (lane == 0) red[(m * kQuarters + q) * TT + t] = sum;
             }
         }
+        if (xi < x1) st_stream(reinterpret_cast<uint4*>(p.permuted) + xi, xcopy);
+        for (int i = xi + kCT; i < x1; i += kCT)  // shares longer than one vector per thread
+            st_stream(reinterpret_cast<uint4*>(p.permuted) + i,
+                      __ldcg(reinterpret_cast<const uint4*>(p.moe_in) + i % nvec));
         __syncthreads();
         if (threadIdx.x < ne * TT) {
             const int mm = threadIdx.x / TT, t = threadIdx.x - mm * TT;
