@@ -702,7 +702,6 @@ __device__ __forceinline__ void chain_main(const ChainParams& p, unsigned char* 
 // ------------------------------------------------------------------------------------
 // Gate CTAs: router GEMV for experts j, j + G1, ... (G1 = gate CTAs).
 // ------------------------------------------------------------------------------------
-constexpr int kQuarters = kCW / kGateMaxExperts;  // warps sharing one expert's dot product
 
 template <int VQ, int TT>
 __device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* smem) {
@@ -745,45 +744,48 @@ __device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* 
         uint4 xcopy = make_uint4(0, 0, 0, 0);
         if (xi < x1) xcopy = __ldcg(reinterpret_cast<const uint4*>(p.moe_in) + xi % nvec);
         const bf16* wl = wb + (size_t)(l & 1) * kGateMaxExperts * H;
-        // Warp w computes expert m = w / kQuarters over quarter q = w % kQuarters of H for
-        // every token: its W vectors once from shared memory, each token's moe_in vectors
-        // from L2, two accumulator chains per token, a warp sum; the quarters are then added
-        // in order by one thread per (token, expert).
+        // Warp w takes slice w of H (kCW slices) for every expert of the CTA and every token:
+        // its moe_in vectors once from L2 (one read of moe_in per CTA), the experts' W
+        // vectors from shared memory, one accumulator per (expert, token), a warp sum; the
+        // slices are then added in order by one thread per (expert, token).
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        const int m = warp / kQuarters, q = warp - m * kQuarters;
-        const int Q = (nvec + kQuarters - 1) / kQuarters;
-        if (m < ne) {
-            V8 wv[VQ];
+        const int S = (nvec + kCW - 1) / kCW;  // vectors per slice
+        const int v0 = warp * S, v1 = min(v0 + S, nvec);
+        float acc[kGateMaxExperts][TT];
 #pragma unroll
-            for (int i = 0; i < VQ; ++i) {
-                const int v = q * Q + lane + 32 * i;
-                wv[i].u = reinterpret_cast<const uint4*>(wl + (size_t)m * H)[min(v, nvec - 1)];
-            }
+        for (int m = 0; m < kGateMaxExperts; ++m)
 #pragma unroll
-            for (int t = 0; t < TT; ++t) {
-                V8 xv[VQ];
+            for (int t = 0; t < TT; ++t) acc[m][t] = 0.0f;
 #pragma unroll
-                for (int i = 0; i < VQ; ++i) {
-                    const int v = q * Q + lane + 32 * i;
-                    xv[i].u = __ldcg(reinterpret_cast<const uint4*>(p.moe_in + (size_t)t * H) +
-                                     min(v, nvec - 1));
+        for (int i = 0; i < VQ; ++i) {
+            const int v = v0 + lane + 32 * i;
+            const bool in = v < v1;
+            const int vc = in ? v : v0;  // clamped: every load in flight at once
+            V8 xv[TT];
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+                xv[t].u = __ldcg(reinterpret_cast<const uint4*>(p.moe_in + (size_t)min(t, T - 1) * H) + vc);
+#pragma unroll
+            for (int m = 0; m < kGateMaxExperts; ++m) {
+                if (m < ne && in) {
+                    V8 wv;
+                    wv.u = reinterpret_cast<const uint4*>(wl + (size_t)m * H)[vc];
+#pragma unroll
+                    for (int t = 0; t < TT; ++t)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            acc[m][t] = fmaf(__bfloat162float(xv[t].e[e]), __bfloat162float(wv.e[e]), acc[m][t]);
                 }
-                float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-                for (int i = 0; i < VQ; ++i) {
-                    const int v = q * Q + lane + 32 * i;
-                    if (v < min((q + 1) * Q, nvec)) {
-#pragma unroll
-                        for (int e = 0; e < 8; e += 2) {
-                            a0 = fmaf(__bfloat162float(xv[i].e[e]), __bfloat162float(wv[i].e[e]), a0);
-                            a1 = fmaf(__bfloat162float(xv[i].e[e + 1]), __bfloat162float(wv[i].e[e + 1]), a1);
-                        }
-                    }
-                }
-                const float sum = warp_sum(a0 + a1);
-                if (lane == 0) red[(m * kQuarters + q) * TT + t] = sum;
             }
         }
+#pragma unroll
+        for (int m = 0; m < kGateMaxExperts; ++m)
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+                if (m < ne && t < T) {  // ne and T are uniform over the CTA
+                    const float sum = warp_sum(acc[m][t]);
+                    if (lane == 0) red[(m * kCW + warp) * TT + t] = sum;
+                }
         if (xi < x1) st_stream(reinterpret_cast<uint4*>(p.permuted) + xi, xcopy);
         for (int i = xi + kCT; i < x1; i += kCT)  // shares longer than one vector per thread
             st_stream(reinterpret_cast<uint4*>(p.permuted) + i,
@@ -793,7 +795,7 @@ __device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* 
             const int mm = threadIdx.x / TT, t = threadIdx.x - mm * TT;
             float sum = 0.0f;
 #pragma unroll
-            for (int qq = 0; qq < kQuarters; ++qq) sum += red[(mm * kQuarters + qq) * TT + t];
+            for (int w = 0; w < kCW; ++w) sum += red[(mm * kCW + w) * TT + t];
             const float v = __bfloat162float(__float2bfloat16_rn(sum));
             const int e = j + mm * G1;
             p.logits[(size_t)t * E + e] = v;
@@ -821,7 +823,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
         reinterpret_cast<int*>(&ps)[i] = reinterpret_cast<const int*>(&p)[i];
     __syncthreads();
     if (blockIdx.x == 0) chain_main<VPT, TT>(ps, smem);
-    else chain_gate<VPT * kCT / (kQuarters * 32), TT>(ps, smem);
+    else chain_gate<VPT, TT>(ps, smem);  // a slice of H / kCW vectors: at most VPT per lane
 }
 
 // ------------------------------------------------------------------------------------
