@@ -53,8 +53,6 @@ def parse():
     p.add_argument("--chain-tokens", default="1,32,256,8192",
                    help="batch sizes of the 50-layer decode chain ('' = skip)")
     p.add_argument("--chain-layers", type=int, default=50)
-    p.add_argument("--hang-dump", type=float, default=0.0,
-                   help="seconds after which every thread's Python stack goes to stderr (0 = off)")
     return p.parse_args()
 
 
@@ -288,9 +286,6 @@ def ep_round_trip(dev, world, rank, T=4096, H=6144, steps=10, warmup=3):
 # ------------------------------------------------------------------------------------
 def main():
     args = parse()
-    if args.hang_dump > 0:
-        import faulthandler
-        faulthandler.dump_traceback_later(args.hang_dump, repeat=True)
     if args.impl == "reference":
         run_reference(args)
         return

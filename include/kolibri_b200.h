@@ -133,6 +133,8 @@ KB_API int kb_maps_describe(int64_t T, int E, int K, int route, int mode, int *p
  *   Zero state: the scratch must hold zeros when a call starts; every completed call
  *   leaves it so.  If a bounded wait inside the kernel gave up (offsets all -1), pass
  *   flags = KB_NOALLOC_REZERO on the next call to zero-fill it again first.
+ *   Device: the scratch used is the CURRENT device's; `stream` must belong to that device
+ *   (a stream of another device returns KB_ERR_INVALID_ARG).
  *   Concurrency: all calls on one device share the scratch.  Calls must be ordered
  *   (one stream, or streams joined by events); two calls in flight at once on the same
  *   device race on the scratch and give wrong maps.
@@ -220,13 +222,23 @@ KB_API int kb_add_rms_norm(const void *a, const void *b, const void *g, void *ou
  *   residual, next = post-MoE pair of moe_out and h (as kb_residual_norm_pair)
  * attn_out, moe_out, q and k are the outputs of the attention / expert GEMMs, which are
  * outside this library: the same buffers feed every layer.  The residual stream starts as
- * residual_in and ends in residual_out (which may alias it); h, moe_in, next, q_out, k_out,
- * logits, ids, weights, maps and permuted hold the last layer's values.  trace_logits
- * (NULL or fp32 [n_layers, T, E]) receives every layer's logits.  `layers` is a DEVICE
- * array of n_layers descriptors.  pos == NULL makes every layer RNoPE.
- * The workspace (kb_decode_chain_workspace_bytes, 16-byte aligned) must be zero-filled
- * before the first call and is left zero-filled.  The kernel is cooperative (one CTA per
- * SM): calls must not overlap other work that needs every SM to make progress.
+ * residual_in and ends in residual_out (which may alias it); no other output may overlap an
+ * input (KB_ERR_INVALID_ARG).  h, moe_in, next, q_out, k_out, logits, ids, weights, maps and
+ * permuted hold the last layer's values.  trace_logits (NULL or fp32 [n_layers, T, E])
+ * receives every layer's logits.  `layers` is a DEVICE array of n_layers descriptors whose
+ * weight pointers are 16-byte aligned (the bias 4-byte aligned).  pos == NULL makes every
+ * layer RNoPE.
+ * Launch: one cooperative launch of one CTA per SM.  Every CTA runs every stage on whole rows;
+ * the CTAs meet once per layer, in the all-gather of the router GEMV's logits (each CTA owns
+ * ceil(E / SMs) <= 4 experts).  Calls must not overlap other work that needs every SM.
+ * Workspace (kb_decode_chain_workspace_bytes, 16-byte aligned): zero-fill it once before the
+ * first call; later calls keep it consistent (a call epoch and the logit records live there),
+ * so successive calls on one workspace must be ordered (one stream).
+ * Failure contract: every wait inside the kernel is bounded.  If one gives up (or a layer's
+ * weight pointer is misaligned), the call sets the workspace's error word, writes offsets[0..E]
+ * = -1 and its other outputs are invalid; every later call on that workspace does nothing but
+ * write offsets = -1 until the workspace is zero-filled again.  kb_workspace_status reads the
+ * error word.
  * No single counterpart in the reference: it chains the entry points above.
  */
 typedef struct {

@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 namespace kb {
 
@@ -17,6 +18,20 @@ std::atomic<int> g_pdl{initial_pdl()};
 }  // namespace
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
+int device_sm_count() {
+    static std::mutex mu;
+    static int cache[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    int& v = cache[dev & 63];
+    if (v == 0) {
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        if (v <= 0) v = 148;
+    }
+    return v;
+}
 
 }  // namespace kb
 

@@ -4,49 +4,79 @@
 // Per layer, in the order of the reference harness's decoder_layer
 // (benchmarks/11_profile_2block_e2e.py:215-266, with the next layer's input_layernorm
 // :222-227 fused into the post-MoE pair), each stage starting after the previous one ended:
-//   A  Q/K RMSNorm + NeoX RoPE of q, k (RNoPE layers: the norm only)           main CTA
-//   B  sandwich: h = r + RMSNorm(attn_out)*g1 ; moe_in = RMSNorm(h)*g2          main CTA
-//   C  router GEMV: logits[t][e] = float(bf16(moe_in[t] . W[e]))                gate CTAs
-//   D  router (top-K of logits + bias, sigmoid weights) and expert maps         main CTA
-//   E  activation expansion: permuted[r] = moe_in[p2u[r] % T]     main CTA (gate CTAs at T=1)
-//   F  post-MoE pair: r = h + RMSNorm(moe_out)*g3 ; next = RMSNorm(r)*g4         main CTA
-// The main CTA (block 0) runs every stage but C and keeps r, h and moe_in of its rows in
-// shared memory.  Every other CTA (one per remaining SM) owns up to four experts of the
-// router GEMV: it streams its rows of W for the next layer into shared memory while the main
-// CTA works, waits for the layer's `go` word, computes its logits and publishes each one with
-// the layer's tag in a 64-bit record, which the main CTA polls (the logits arrive with the
-// tag).  `go` and the records are the only cross-CTA synchronisation; every wait is bounded
-// and sets an error word when it gives up.  The arithmetic is that of the stand-alone kernels
-// (norm_math.cuh, route_math.cuh, the Q/K formula of qk_norm_rope.cu), so each stage gives
-// the same bits as its own kernel would on the same inputs.
+//   A  Q/K RMSNorm + NeoX RoPE of q, k (RNoPE layers: the norm only)
+//   B  sandwich: h = r + RMSNorm(attn_out)*g1 ; moe_in = RMSNorm(h)*g2
+//   C  router GEMV: logits[t][e] = float(bf16(moe_in[t] . W[e]))
+//   D  router (top-K of logits + bias, sigmoid weights) and expert maps
+//   E  activation expansion: permuted[r] = moe_in[p2u[r] % T]
+//   F  post-MoE pair: r = h + RMSNorm(moe_out)*g3 ; next = RMSNorm(r)*g4
+//
+// Every CTA (one per SM) runs every stage on whole rows.  The residual stream, h and moe_in of
+// the T tokens stay in its registers, so a stage never waits for another CTA except where the
+// data really is spread over the GPU: the router GEMV.  CTA c owns experts c, c + G, ... (G
+// CTAs); it keeps their W rows in shared memory, computes their logits and publishes each one
+// as a 64-bit record: the call's layer tag in the high word, the value in the low word.
+// 64-bit accesses are single-copy atomic, so the poll that sees the tag also delivers the
+// value.  Every CTA then polls the E records of the layer, and all CTAs rank the same logits
+// with the same code, so they all hold the same selections.  That all-gather is the only
+// cross-CTA wait of a layer; records alternate between two banks by layer parity, and a CTA
+// can be at most one layer ahead of another (it needs the other's records to leave a layer).
+//
+// Each output element is written once, by an owner CTA: vector v of token t of h, moe_in,
+// next and the residual by CTA (t*nvec + v) mod G, Q/K head j by CTA j mod G, map entries and
+// logits by the CTA that owns them, so the writes are spread over all SMs.
+// The next layer's weights (gammas, the owned W rows, the bias) arrive in shared memory by bulk
+// copies (cp.async.bulk into this CTA's own memory, no cluster multicast) while the current
+// layer runs; loads of the GEMM stand-ins (q, k, attn_out, moe_out) are issued only when their
+// stage starts and bypass L1, as loads of a tensor that a GEMM has just written would.
+//
+// The arithmetic is that of the stand-alone kernels (norm_math.cuh and the row shape of
+// norms.cu, route_math.cuh, the Q/K formula and lane layout of qk_norm_rope.cu), so every
+// routing-independent output is bit-identical to the stage-by-stage path.  Every wait is
+// bounded; a wait that gives up sets the workspace error word, the CTAs leave at the end of
+// the layer, and later calls report offsets = -1 until the workspace is zero-filled again.
 #include "kb_common.cuh"
 #include "norm_math.cuh"
 #include "route_math.cuh"
 
 #include <algorithm>
-#include <mutex>
 
 namespace kb {
 namespace {
 
 using bf16 = __nv_bfloat16;
 
-constexpr int kCT = 512;                     // threads per CTA
+constexpr int kCT = 384;                     // threads per CTA (a 6144-wide row: 2 vectors each)
 constexpr int kCW = kCT / 32;                // warps per CTA
-constexpr int kMaxGateCtas = 960;            // gate CTAs with logit records in the workspace
 constexpr int kChainMaxLayers = 256;         // layer descriptors held in shared memory
-constexpr int kMaxChunks = E_MAX / 32;       // 32-expert chunks of the router
 constexpr int kChainMaxT = 4;                // tokens per call
 constexpr int kChainMaxK = 8;                // top-K
-constexpr int kGateMaxExperts = 4;           // experts per gate CTA
+constexpr int kMaxOwn = 4;                   // router experts per CTA
 constexpr int kHalfD = 64;                   // head_dim 128
+constexpr int kQkChunk = 6;                  // heads per warp with their loads in flight together
+constexpr int kMaxChunks = E_MAX / 32;       // 32-expert chunks of a router row
 constexpr long long kChainSpin = 1LL << 21;  // bounded waits (about a second of polling)
-constexpr int kRedRows = kChainMaxT * kGateMaxExperts;
+constexpr int kRedVals = kMaxOwn * kChainMaxT;
+// The threshold of the router stage is the K-th largest of the kCW warp maxima.
+static_assert(kChainMaxK <= kCW, "the router threshold needs at least K expert groups");
+static_assert(kChainMaxK * kChainMaxT <= 32, "the selections of one call fit one warp");
+
+// Workspace (zero-filled before the first call): epoch word (+1 per completed call), exit
+// counter, error word, then the logit records [2 banks][kChainMaxT][E_MAX].
+constexpr size_t kWsEpoch = 0, kWsDone = 64, kWsErr = 128, kWsRec = 256;
+constexpr size_t kWsBytes = kWsRec + sizeof(unsigned long long) * 2 * kChainMaxT * E_MAX;
+// Error-word values.
+constexpr int kErrTimeout = 1;    // a bounded wait gave up
+constexpr int kErrAlignment = 2;  // a layer's weight pointer is not 16-byte aligned
+
+enum : int { kBarQK = 0, kBarA = 1, kBarW = 2, kBarB = 3, kNumBars = 4 };
 
 struct ChainParams {
     const kb_chain_layer_t* layers;
     int L, T, H, Hq, Hkv, E, K;
-    int pair_threads;  // threads owning row vectors in the norm stages (row_shape)
+    int pt;    // threads owning row vectors (row_shape of the stand-alone norm kernels)
+    int vpt;   // row vectors per such thread (1 or 2)
+    int nown;  // router experts per CTA
     float eps;
     const bf16* attn_out;
     const bf16* moe_out;
@@ -70,24 +100,143 @@ struct ChainParams {
     int32_t* p2u;
     int32_t* u2p;
     float* trace_logits;
-    unsigned* go;    // layers whose moe_in rows are published; 0 between calls
-    // [gate CTAs][kGateMaxExperts][kChainMaxT] logit records: (layer + 1) << 32 | float bits,
-    // written by the gate CTAs with one 64-bit store each; 0 between calls
+    unsigned* epoch;
+    unsigned* done;
+    int* err;
     unsigned long long* rec;
-    int* err;        // non-zero once a wait gave up (the workspace must be re-zeroed)
 };
 
-__device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+// ------------------------------------------------------------------------------------
+// Shared memory
+// ------------------------------------------------------------------------------------
+struct SmemLayout {
+    size_t bar, gqk, ga, gb, w, bias, layers, xrow, cs, sn, red, wmax, cand, ncand, sel, perm,
+        flag, total;
+};
+__host__ __device__ constexpr size_t al128(size_t v) { return (v + 127) & ~size_t(127); }
+__host__ __device__ inline SmemLayout smem_layout(int H, int nown, int L) {
+    SmemLayout s{};
+    size_t o = 0;
+    s.bar = o;    o = al128(o + kNumBars * sizeof(uint64_t));
+    s.gqk = o;    o = al128(o + 2 * 128 * sizeof(bf16));
+    s.ga = o;     o = al128(o + (size_t)2 * H * sizeof(bf16));
+    s.gb = o;     o = al128(o + (size_t)2 * H * sizeof(bf16));
+    s.w = o;      o = al128(o + (size_t)nown * H * sizeof(bf16));
+    s.bias = o;   o = al128(o + E_MAX * sizeof(float));
+    s.layers = o; o = al128(o + (size_t)L * sizeof(kb_chain_layer_t));
+    s.xrow = o;   o = al128(o + (size_t)kChainMaxT * E_MAX * sizeof(float));
+    s.cs = o;     o = al128(o + kChainMaxT * kHalfD * sizeof(float));
+    s.sn = o;     o = al128(o + kChainMaxT * kHalfD * sizeof(float));
+    s.red = o;    o = al128(o + (size_t)2 * kRedVals * 33 * sizeof(float));
+    s.wmax = o;   o = al128(o + kChainMaxT * 32 * sizeof(uint32_t));
+    s.cand = o;   o = al128(o + kChainMaxT * 32 * sizeof(unsigned long long));
+    s.ncand = o;  o = al128(o + kChainMaxT * sizeof(int));
+    s.sel = o;    o = al128(o + 32 * sizeof(int));
+    s.perm = o;   o = al128(o + 32 * sizeof(int));
+    s.flag = o;   o = al128(o + 8 * sizeof(int));
+    s.total = o;
+    return s;
 }
-__device__ __forceinline__ void st_rel(unsigned* p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+
+struct Smem {
+    uint64_t* bar;             // [kNumBars] one mbarrier per weight buffer
+    bf16* gqk;                 // [2][128]  g_q, g_k
+    bf16* ga;                  // [2][H]    g_post_attn, g_pre_moe
+    bf16* gb;                  // [2][H]    g_post_ffn, g_input_ln
+    bf16* w;                   // [nown][H] router rows of the owned experts
+    float* bias;               // [E_MAX]   gate bias (+0 for -0), zeros without one
+    kb_chain_layer_t* layers;  // [L]
+    float* xrow;               // [kChainMaxT][E_MAX] logits of the layer
+    float* cs;                 // [kChainMaxT][64]
+    float* sn;                 // [kChainMaxT][64]
+    float* red;                // [2][kRedVals][33] block reductions, two buffers in turn
+    uint32_t* wmax;            // [kChainMaxT][32] warp maxima of the router keys
+    unsigned long long* cand;  // [kChainMaxT][32] router candidates
+    int* ncand;                // [kChainMaxT]
+    int* sel;                  // [32] selections, (token, slot) order
+    int* perm;                 // [32] token of each permuted row
+    int* flag;                 // [8]  flag[0]: leave at the end of this layer;
+                               //      flag[4 + b]: bulk-copy phases issued on buffer b
+};
+
+__device__ __forceinline__ Smem carve(unsigned char* base, const SmemLayout& l) {
+    Smem s;
+    s.bar = reinterpret_cast<uint64_t*>(base + l.bar);
+    s.gqk = reinterpret_cast<bf16*>(base + l.gqk);
+    s.ga = reinterpret_cast<bf16*>(base + l.ga);
+    s.gb = reinterpret_cast<bf16*>(base + l.gb);
+    s.w = reinterpret_cast<bf16*>(base + l.w);
+    s.bias = reinterpret_cast<float*>(base + l.bias);
+    s.layers = reinterpret_cast<kb_chain_layer_t*>(base + l.layers);
+    s.xrow = reinterpret_cast<float*>(base + l.xrow);
+    s.cs = reinterpret_cast<float*>(base + l.cs);
+    s.sn = reinterpret_cast<float*>(base + l.sn);
+    s.red = reinterpret_cast<float*>(base + l.red);
+    s.wmax = reinterpret_cast<uint32_t*>(base + l.wmax);
+    s.cand = reinterpret_cast<unsigned long long*>(base + l.cand);
+    s.ncand = reinterpret_cast<int*>(base + l.ncand);
+    s.sel = reinterpret_cast<int*>(base + l.sel);
+    s.perm = reinterpret_cast<int*>(base + l.perm);
+    s.flag = reinterpret_cast<int*>(base + l.flag);
+    return s;
 }
-// 64-bit accesses are single-copy atomic: a record's tag and value are seen together.
+
+// ------------------------------------------------------------------------------------
+// Memory primitives
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ unsigned su32(const void* p) {
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mb_init(uint64_t* b, unsigned n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mb_expect(uint64_t* b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+                 : "memory");
+}
+// Non-blocking test of the phase of parity `parity`.
+__device__ __forceinline__ bool mb_try(uint64_t* b, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(su32(b)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// One bulk copy global -> this CTA's shared memory (16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(su32(dst)), "l"(src), "r"(bytes), "r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void cp4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Loads of the GEMM stand-ins: cached in L2 only.
+__device__ __forceinline__ uint4 ld_cg16(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint2 ld_cg8(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+// 64-bit accesses are single-copy atomic: a record's tag and value are seen together.  The
+// record is published with an atomic exchange, which is performed at L2 at once (a plain
+// relaxed store measured up to ~3 us before other SMs saw it).
 __device__ __forceinline__ void st_rec(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+    unsigned long long old;
+    asm volatile("atom.relaxed.gpu.global.exch.b64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    (void)old;
 }
 __device__ __forceinline__ unsigned long long ld_rec(const unsigned long long* p) {
     unsigned long long v;
@@ -95,326 +244,340 @@ __device__ __forceinline__ unsigned long long ld_rec(const unsigned long long* p
     return v;
 }
 
-__device__ __forceinline__ void cp16(void* dst, const void* src) {
-    const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp4(void* dst, const void* src) {
-    const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// Thread 0 waits until *p >= target.  Gives up (sets err) after kChainSpin polls, or as soon
-// as another CTA has given up.
-__device__ bool wait_geq(const unsigned* p, unsigned target, int* err) {
-    unsigned v = ld_acq(p);
-    long long it = 0;
-    while (v < target) {
-        if (++it > kChainSpin) {
-            atomicExch(err, 1);
-            return false;
-        }
-        if ((it & 1023) == 0 && *(volatile int*)err) return false;
-        __nanosleep(32);
-        v = ld_acq(p);
-    }
-    return true;
-}
-
-// Block-wide sums of n values at once; each value is reduced exactly as block_sum reduces
-// it (warp butterfly, then a butterfly over the warp partials, lanes past the last warp
-// adding 0).  Every warp runs the second butterfly itself: a butterfly leaves the same bits
-// in every lane, so each warp gets warp 0's result, and one barrier does.  red: MAXN*33
-// floats, read after the barrier; the next call must take another buffer (two calls in
-// turn on two buffers are safe: a call's barrier follows every read of the buffer before).
-template <int MAXN>
-__device__ __forceinline__ void block_sum_n(float (&v)[MAXN], int n, float* red) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nw = (blockDim.x + 31) >> 5;
-#pragma unroll
-    for (int m = 0; m < MAXN; ++m) {
-        if (m < n) {
-            const float s = warp_sum(v[m]);
-            if (lane == 0) red[m * 33 + warp] = s;
-        }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int m = 0; m < MAXN; ++m)
-        if (m < n) v[m] = warp_sum((lane < nw) ? red[m * 33 + lane] : 0.0f);
-}
-
 union V8 {
     uint4 u;
+    uint32_t w[4];
     bf16 e[8];
 };
 
-template <typename... KArgs, typename... Args>
-int launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE round-to-nearest operations per
+// instruction, the same results as the scalar __fmul_rn / __fadd_rn / fmaf).
+typedef unsigned long long f2_t;
+__device__ __forceinline__ f2_t f2_pack(float lo, float hi) {
+    f2_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
 }
-
-// ------------------------------------------------------------------------------------
-// Main CTA stages.
-// ------------------------------------------------------------------------------------
-struct MainSmem {
-    bf16* r;      // [kChainMaxT][H] residual stream
-    bf16* h;      // [kChainMaxT][H] sandwich sum
-    bf16* x;      // [kChainMaxT][H] moe_in
-    float* cs;    // [kChainMaxT][64]
-    float* sn;    // [kChainMaxT][64]
-    float* red;   // [kRedRows][33]
-    int* hist;    // [E_MAX]  routing: group maxima [kChainMaxT][32]
-    int* offs;    // [E_MAX + 4]  routing: candidates (u64) [kChainMaxT][32]
-    int* sel;     // [32]
-    int* perm;    // [32]  token of each permuted row
-    int* scratch; // [64]
-    int* flag;    // [4]
-    kb_chain_layer_t* layers;  // [kChainMaxLayers]
-    float* xrow;  // [kChainMaxT][E_MAX] logits of the layer
-    float* bias;  // [E_MAX] gate bias of the layer (+0 for -0), 0 without one
+__device__ __forceinline__ void f2_unpack(f2_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2_t f2_mul(f2_t a, f2_t b) {
+    f2_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
+    f2_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+    f2_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// bf16 pair (element 2j in the low half) -> fp32 pair, exactly.
+__device__ __forceinline__ f2_t bf2_to_f2(uint32_t u) {
+    return f2_pack(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+// fp32 pair -> bf16 pair, round to nearest even (as __float2bfloat16_rn on each).
+__device__ __forceinline__ uint32_t f2_to_bf2(f2_t v) {
+    float lo, hi;
+    f2_unpack(v, lo, hi);
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+union V4 {
+    uint2 u;
+    bf16 e[4];
 };
 
-__host__ __device__ constexpr size_t main_smem_bytes(int H) {
-    return (size_t)3 * kChainMaxT * H * sizeof(bf16) + 2 * kChainMaxT * kHalfD * sizeof(float) +
-           (size_t)kRedRows * 33 * sizeof(float) + (2 * E_MAX + 4 + 32 + 32 + 64 + 4) * sizeof(int) +
-           (size_t)kChainMaxLayers * sizeof(kb_chain_layer_t) +
-           (size_t)(kChainMaxT * E_MAX + E_MAX) * 4;
+// Marks this CTA to leave at the end of the layer, and the call as failed (error word).
+__device__ __forceinline__ void give_up(const ChainParams& p, const Smem& s, int code) {
+    s.flag[0] = 1;
+    atomicCAS(p.err, 0, code);
 }
-__host__ __device__ constexpr size_t gate_smem_bytes(int H) {
-    return (size_t)2 * kGateMaxExperts * H * sizeof(bf16) + (size_t)kRedRows * 33 * sizeof(float) +
-           16;
+__device__ __forceinline__ bool leaving(const ChainParams& p, const Smem& s) {
+    return *(volatile int*)s.flag || *(volatile int*)p.err;
 }
 
-__device__ MainSmem carve_main(unsigned char* smem, int H) {
-    MainSmem m;
-    m.r = reinterpret_cast<bf16*>(smem);
-    m.h = m.r + (size_t)kChainMaxT * H;
-    m.x = m.h + (size_t)kChainMaxT * H;
-    m.cs = reinterpret_cast<float*>(m.x + (size_t)kChainMaxT * H);
-    m.sn = m.cs + kChainMaxT * kHalfD;
-    m.red = m.sn + kChainMaxT * kHalfD;
-    m.hist = reinterpret_cast<int*>(m.red + kRedRows * 33);
-    m.offs = m.hist + E_MAX;
-    m.sel = m.offs + E_MAX + 4;
-    m.perm = m.sel + 32;
-    m.scratch = m.perm + 32;
-    m.flag = m.scratch + 64;
-    m.layers = reinterpret_cast<kb_chain_layer_t*>(m.flag + 4);
-    m.xrow = reinterpret_cast<float*>(m.layers + kChainMaxLayers);
-    m.bias = m.xrow + kChainMaxT * E_MAX;
-    return m;
+// Every thread waits for the phase of parity `par` of weight buffer b (bounded).
+__device__ __forceinline__ void wait_weights(const ChainParams& p, const Smem& s, int b, unsigned par) {
+    long long it = 0;
+    while (!mb_try(s.bar + b, par)) {
+        if (++it > kChainSpin || ((it & 255) == 0 && leaving(p, s))) {
+            give_up(p, s, kErrTimeout);
+            return;
+        }
+        __nanosleep(20);
+    }
 }
 
-// A: per-head RMSNorm + NeoX RoPE.  Four lanes per (token, head), 32 elements per lane,
-// eight heads per warp.  Lane p of a head holds the elements of lanes 8p..8p+7 of the
-// one-warp-per-head kernel (qk_norm_rope.cu); its butterfly levels 16, 8 become lane
-// exchanges 2, 1 and levels 4, 2, 1 register adds, so the sum of squares, and with it every
-// output, has the same bits.  The NeoX partner of element j (j +- 64) sits in lane p^2.
-constexpr int kQkChunk = 1;  // head groups per warp with loads in flight together
+// Thread 0: bulk copies of layer l's weights for buffer b.  Issued only after every thread
+// saw the buffer's previous phase complete (no wait of this CTA gave up), so a buffer never
+// has two phases in flight.
+__device__ void issue_weights(const ChainParams& p, const Smem& s, int b, int l) {
+    const kb_chain_layer_t& Ly = s.layers[l];
+    const unsigned row = (unsigned)p.H * (unsigned)sizeof(bf16);
+    s.flag[4 + b] += 1;
+    fence_proxy_async();  // earlier generic reads of the buffer come before the copy's writes
+    if (b == kBarQK) {
+        mb_expect(s.bar + b, 2 * 128 * sizeof(bf16));
+        bulk_g2s(s.gqk, Ly.g_q, 128 * sizeof(bf16), s.bar + b);
+        bulk_g2s(s.gqk + 128, Ly.g_k, 128 * sizeof(bf16), s.bar + b);
+    } else if (b == kBarA || b == kBarB) {
+        bf16* dst = b == kBarA ? s.ga : s.gb;
+        mb_expect(s.bar + b, 2 * row);
+        bulk_g2s(dst, b == kBarA ? Ly.g_post_attn : Ly.g_post_ffn, row, s.bar + b);
+        bulk_g2s(dst + p.H, b == kBarA ? Ly.g_pre_moe : Ly.g_input_ln, row, s.bar + b);
+    } else {
+        const int c = blockIdx.x, G = gridDim.x;
+        int mine = 0;
+        for (int m = 0; m < p.nown; ++m)
+            if (c + m * G < p.E) mine = m + 1;
+        mb_expect(s.bar + b, (unsigned)mine * row);
+        const bf16* W = static_cast<const bf16*>(Ly.w_gate_t);
+        for (int m = 0; m < mine; ++m)
+            bulk_g2s(s.w + (size_t)m * p.H, W + (size_t)(c + m * G) * p.H, row, s.bar + b);
+    }
+}
 
-__device__ __forceinline__ void stage_qk(const ChainParams& p, const kb_chain_layer_t& Ly,
-                                     const MainSmem& s) {
+// Layer l's gate bias into shared memory (+0 for -0, zeros without a bias): 4-byte
+// asynchronous copies, completed by cp_wait_all before the router reads them.
+__device__ __forceinline__ void issue_bias(const ChainParams& p, const Smem& s, int l) {
+    const float* b = s.layers[l].gate_bias;
+    for (int e = threadIdx.x; e < p.E; e += kCT) {
+        if (b) cp4(s.bias + e, b + e);
+        else s.bias[e] = 0.0f;
+    }
+    cp_commit();
+}
+
+// Block-wide sums of n values at once; each value is reduced exactly as block_sum reduces it
+// (warp butterfly, then a butterfly over the warp partials, lanes past the last warp adding
+// 0).  One barrier; the next call must take the other buffer.
+template <int MAXN>
+__device__ __forceinline__ void block_sum_n(float (&v)[MAXN], float* red) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int slot = lane >> 2, pl = lane & 3;  // head slot in the warp, lane in the head
-    const int HH = p.Hq + p.Hkv, nh = p.T * HH;
-    const int ngroups = (nh + 7) >> 3;
-    const bool rope = !Ly.rnope && p.pos != nullptr;
-    for (int g0 = warp; g0 < ngroups; g0 += kCW * kQkChunk) {
-        V8 xv[kQkChunk][4], gv[kQkChunk][4];
 #pragma unroll
-        for (int c = 0; c < kQkChunk; ++c) {  // clamped heads: every load in flight at once
-            const int hd = min((g0 + c * kCW) * 8 + slot, nh - 1);
-            const int t = hd / HH, hh = hd - t * HH;
-            const bf16* src = hh < p.Hq ? p.q + ((size_t)t * p.Hq + hh) * 128
-                                        : p.k + ((size_t)t * p.Hkv + (hh - p.Hq)) * 128;
-            const bf16* gsrc = static_cast<const bf16*>(hh < p.Hq ? Ly.g_q : Ly.g_k) + pl * 32;
+    for (int m = 0; m < MAXN; ++m) {
+        const float s = warp_sum(v[m]);
+        if (lane == 0) red[m * 33 + warp] = s;
+    }
+    __syncthreads();
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                xv[c][u].u = ld_stream(reinterpret_cast<const uint4*>(src + pl * 32) + u);
-                gv[c][u].u = __ldg(reinterpret_cast<const uint4*>(gsrc) + u);
+    for (int m = 0; m < MAXN; ++m) v[m] = warp_sum((lane < kCW) ? red[m * 33 + lane] : 0.0f);
+}
+
+// ------------------------------------------------------------------------------------
+// Stages
+// ------------------------------------------------------------------------------------
+
+// A: per-head RMSNorm + NeoX RoPE of every head of the T tokens (one warp per head, four
+// consecutive elements per lane, as qk_norm_rope_kernel<128>: the NeoX partner of lane l is
+// lane l^16).  Head j (over tokens and q then k heads) is stored by CTA j mod G (j < 3G).  A
+// warp takes kQkChunk heads at once and runs each step for all of them together (independent
+// chains side by side); lane i < kQkChunk computes head i's 1/sqrt and hands it out by a
+// shuffle.  The sum of squares of each head is the butterfly of warp_sum, so every bit
+// matches.  The q/k loads are issued before the wait for the layer's g_q/g_k.
+template <int TT>
+__device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bool rope, unsigned par) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x, G = gridDim.x;
+    const int HH = p.Hq + p.Hkv, nh = TT * HH;
+    constexpr int QC = TT <= 2 ? kQkChunk : kQkChunk / 2;  // fewer heads at once at larger T
+    bool waited = false;
+    for (int base = warp; base < nh; base += kCW * QC) {
+        V4 xv[QC];
+        int tt[QC], hq[QC];
+#pragma unroll
+        for (int cc = 0; cc < QC; ++cc) {  // clamped heads: all loads in flight at once
+            const int hd = min(base + cc * kCW, nh - 1);
+            const int t = TT == 1 ? 0 : (hd >= HH) + (hd >= 2 * HH) + (hd >= 3 * HH);
+            tt[cc] = t;
+            hq[cc] = hd - t * HH;
+            const bf16* src = hq[cc] < p.Hq ? p.q + ((size_t)t * p.Hq + hq[cc]) * 128
+                                            : p.k + ((size_t)t * p.Hkv + (hq[cc] - p.Hq)) * 128;
+            xv[cc].u = ld_cg8(src + lane * 4);
+        }
+        if (!waited) {
+            wait_weights(p, s, kBarQK, par);
+            waited = true;
+        }
+        V4 gq, gk;
+        gq.u = reinterpret_cast<const uint2*>(s.gqk)[lane];
+        gk.u = reinterpret_cast<const uint2*>(s.gqk + 128)[lane];
+        float y[QC][4], ss[QC];
+#pragma unroll
+        for (int cc = 0; cc < QC; ++cc) {
+            ss[cc] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                y[cc][i] = __bfloat162float(xv[cc].e[i]);
+                ss[cc] = fmaf(y[cc][i], y[cc][i], ss[cc]);
             }
         }
 #pragma unroll
-        for (int c = 0; c < kQkChunk; ++c) {
-            if (g0 + c * kCW >= ngroups) break;
-            const int hd = (g0 + c * kCW) * 8 + slot;
-            const bool act = hd < nh;
-            const int t = act ? hd / HH : 0, hh = act ? hd - t * HH : 0;
-            const bool is_q = hh < p.Hq;
-            float y[32];
-            float part[8];
+        for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-            for (int sub = 0; sub < 8; ++sub) {
-                part[sub] = 0.0f;
+            for (int cc = 0; cc < QC; ++cc) ss[cc] += __shfl_xor_sync(FULL_MASK, ss[cc], o);
+        float mine = ss[0];
+#pragma unroll
+        for (int cc = 1; cc < QC; ++cc) mine = (lane == cc) ? ss[cc] : mine;
+        const float rl = 1.0f / sqrtf(mine / 128.0f + p.eps);
+        float rr[QC];
+#pragma unroll
+        for (int cc = 0; cc < QC; ++cc) rr[cc] = __shfl_sync(FULL_MASK, rl, cc);
+#pragma unroll
+        for (int cc = 0; cc < QC; ++cc) {
+            const bool is_q = hq[cc] < p.Hq;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                y[cc][i] = __fmul_rn(__fmul_rn(y[cc][i], rr[cc]), __bfloat162float(is_q ? gq.e[i] : gk.e[i]));
+        }
+        V4 o[QC];
+        if (rope) {
+            const bool first_half = lane < 16;
+            float cs4[QC][4], sn4[QC][4];
+#pragma unroll
+            for (int cc = 0; cc < QC; ++cc) {
+                const int t = TT == 1 ? 0 : tt[cc];
+                if (TT == 1 && cc > 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) { cs4[cc][i] = cs4[0][i]; sn4[cc][i] = sn4[0][i]; }
+                } else {
+                    const float4 c4 = reinterpret_cast<const float4*>(s.cs + t * kHalfD)[lane & 15];
+                    const float4 s4 = reinterpret_cast<const float4*>(s.sn + t * kHalfD)[lane & 15];
+                    cs4[cc][0] = c4.x; cs4[cc][1] = c4.y; cs4[cc][2] = c4.z; cs4[cc][3] = c4.w;
+                    sn4[cc][0] = s4.x; sn4[cc][1] = s4.y; sn4[cc][2] = s4.z; sn4[cc][3] = s4.w;
+                }
+            }
+            float other[QC][4];
+#pragma unroll
+            for (int cc = 0; cc < QC; ++cc)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) other[cc][i] = __shfl_xor_sync(FULL_MASK, y[cc][i], 16);
+#pragma unroll
+            for (int cc = 0; cc < QC; ++cc)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const int k = sub * 4 + i;
-                    y[k] = act ? __bfloat162float(xv[c][k >> 3].e[k & 7]) : 0.0f;
-                    part[sub] = fmaf(y[k], y[k], part[sub]);
+                    const float v = first_half
+                        ? __fsub_rn(__fmul_rn(y[cc][i], cs4[cc][i]), __fmul_rn(other[cc][i], sn4[cc][i]))
+                        : __fadd_rn(__fmul_rn(y[cc][i], cs4[cc][i]), __fmul_rn(other[cc][i], sn4[cc][i]));
+                    o[cc].e[i] = __float2bfloat16_rn(v);
                 }
-            }
+        } else {
 #pragma unroll
-            for (int o = 2; o > 0; o >>= 1)  // levels 16, 8
+            for (int cc = 0; cc < QC; ++cc)
 #pragma unroll
-                for (int sub = 0; sub < 8; ++sub)
-                    part[sub] += __shfl_xor_sync(FULL_MASK, part[sub], o);
-            float a4[4];
+                for (int i = 0; i < 4; ++i) o[cc].e[i] = __float2bfloat16_rn(y[cc][i]);
+        }
 #pragma unroll
-            for (int sub = 0; sub < 4; ++sub) a4[sub] = part[sub] + part[sub + 4];  // level 4
-            const float a20 = a4[0] + a4[2], a21 = a4[1] + a4[3];                  // level 2
-            const float ss = a20 + a21;                                             // level 1
-            const float r = 1.0f / sqrtf(ss / 128.0f + p.eps);
-            const V8* g = gv[c];  // this lane's gamma slice, loaded with the head
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-                y[k] = __fmul_rn(__fmul_rn(y[k], r), __bfloat162float(g[k >> 3].e[k & 7]));
-            V8 o[4];
-            if (rope) {
-                const bool first_half = pl < 2;
-                // cos/sin of this lane's elements k: angles j = (pl*32 + k) mod 64, 4 at a time
-                const float4* cs4 = reinterpret_cast<const float4*>(s.cs + t * kHalfD + ((pl * 32) & (kHalfD - 1)));
-                const float4* sn4 = reinterpret_cast<const float4*>(s.sn + t * kHalfD + ((pl * 32) & (kHalfD - 1)));
-#pragma unroll
-                for (int m = 0; m < 8; ++m) {  // four elements per float4 of cos and of sin
-                    const float4 a = cs4[m], b = sn4[m];
-                    const float cc4[4] = {a.x, a.y, a.z, a.w}, sv4[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int k = 4 * m + q;
-                        const float other = __shfl_xor_sync(FULL_MASK, y[k], 2);
-                        const float cc = cc4[q], sv = sv4[q];
-                        const float v = first_half ? __fsub_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv))
-                                                   : __fadd_rn(__fmul_rn(y[k], cc), __fmul_rn(other, sv));
-                        o[k >> 3].e[k & 7] = __float2bfloat16_rn(v);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < 32; ++k) o[k >> 3].e[k & 7] = __float2bfloat16_rn(y[k]);
-            }
-            if (act) {
-                bf16* dst = is_q ? p.q_out + ((size_t)t * p.Hq + hh) * 128
-                                 : p.k_out + ((size_t)t * p.Hkv + (hh - p.Hq)) * 128;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) reinterpret_cast<uint4*>(dst + pl * 32)[u] = o[u].u;
+        for (int cc = 0; cc < QC; ++cc) {
+            const int hd = base + cc * kCW;
+            if (hd < nh && (hd == c || hd == c + G || hd == c + 2 * G)) {  // hd mod G == c
+                const int t = tt[cc];
+                bf16* dst = hq[cc] < p.Hq ? p.q_out + ((size_t)t * p.Hq + hq[cc]) * 128
+                                          : p.k_out + ((size_t)t * p.Hkv + (hq[cc] - p.Hq)) * 128;
+                reinterpret_cast<uint2*>(dst)[lane] = o[cc].u;
             }
         }
     }
+    if (!waited) wait_weights(p, s, kBarQK, par);
 }
 
-// B / F: sum = res + RMSNorm(a)*g1 (rounded) ; norm = RMSNorm(sum)*g2, for the T rows.
-// Threads below pair_threads own vectors tid + i*pair_threads, exactly as the stand-alone
-// kernel's threads do (row_shape); the others add zeros to the reductions, which changes no
-// bit.
-// a comes from global memory (read-only during the launch), res from shared memory.
-// sum goes to sum_sm (and sum_g if non-null), norm to norm_g (and norm_sm if non-null).
-template <int VPT, int TT>
-__device__ __forceinline__ void stage_pair(const ChainParams& p, const bf16* a, const bf16* res_sm,
-                           const bf16* g1, const bf16* g2, bf16* sum_sm, bf16* sum_g,
-                           bf16* norm_g, bf16* norm_sm, float* red) {
-    const int T = p.T, H = p.H, nvec = H / 8;
-    // Threads past pair_threads own no vector: their index lands past the row.
-    const int PT = p.pair_threads;
-    const int tid = (int)threadIdx.x < PT ? (int)threadIdx.x : nvec;
-    V8 va[TT][VPT];
-    V8 vg1[VPT], vg2[VPT];
+// Row vectors of this thread: k-th = tid + k*pt (k < 2), valid if ok[k]; voff = v (uint4 index).
+struct RowSlots {
+    int v[2];
+    bool ok[2];
+};
+
+// B / F: sum = res + RMSNorm(a)*g1 (rounded) ; norm = RMSNorm(sum)*g2 for the TT rows.  Thread
+// i < pt owns row vectors i + k*pt (k < vpt), as the stand-alone kernel's threads do; the
+// others add zeros to the reductions, which changes no bit.  a comes from global memory, res
+// from registers, g1/g2 from shared memory.  sum goes to registers (and the owned vectors to
+// sum_g); norm to registers if NORM_ALL (else only the owned vectors are computed), and the
+// owned vectors to norm_g.  own: bit 2t+k marks vector k of token t as owned by this CTA.
+// Products and sums run on fp32 pairs with the scalar kernel's roundings; the sums of squares
+// stay sequential fmaf in element order, as in the stand-alone kernel.
+template <int TT, bool NORM_ALL>
+__device__ __forceinline__ void stage_pair(const ChainParams& p, const Smem& s, const RowSlots& rs,
+                                           const bf16* a, const V8 (&res)[TT][2], int gbar,
+                                           unsigned par, const bf16* g1, const bf16* g2,
+                                           V8 (&sum)[TT][2], V8 (&norm)[TT][2], bf16* sum_g,
+                                           bf16* norm_g, unsigned own, float* red_a, float* red_b) {
+    const int H = p.H;
+    V8 va[TT][2];
     float ss[TT];
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) {  // weights first: every load of the stage is in flight at once
-        const int v = min(tid + i * PT, nvec - 1);
-        vg1[i].u = __ldg(reinterpret_cast<const uint4*>(g1) + v);
-        vg2[i].u = __ldg(reinterpret_cast<const uint4*>(g2) + v);
-    }
-#pragma unroll
-    for (int t = 0; t < TT; ++t) {  // clamped addresses: every load in flight at once
-        ss[t] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < VPT; ++i)
-            va[t][i].u = ld_stream(reinterpret_cast<const uint4*>(a + (size_t)min(t, T - 1) * H) +
-                                   min(tid + i * PT, nvec - 1));
-    }
 #pragma unroll
     for (int t = 0; t < TT; ++t)
 #pragma unroll
-        for (int i = 0; i < VPT; ++i)
-            if (tid + i * PT >= nvec) va[t][i].u = make_uint4(0, 0, 0, 0);
-    static_assert(2 * TT <= kRedRows, "two reduction buffers of TT rows");
+        for (int k = 0; k < 2; ++k)
+            va[t][k].u = rs.ok[k] ? ld_cg16(a + (size_t)t * H + (size_t)rs.v[k] * 8) : make_uint4(0, 0, 0, 0);
+    wait_weights(p, s, gbar, par);  // the gammas are read after the first reduction
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
-        if (t < T) {
+        ss[t] = 0.0f;
 #pragma unroll
-            for (int i = 0; i < VPT; ++i)
+        for (int k = 0; k < 2; ++k)
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float x = __bfloat162float(va[t][i].e[e]);
-                    ss[t] = fmaf(x, x, ss[t]);
-                }
-        }
+            for (int j = 0; j < 4; ++j) {
+                const float x0 = __uint_as_float(va[t][k].w[j] << 16);
+                const float x1 = __uint_as_float(va[t][k].w[j] & 0xffff0000u);
+                ss[t] = fmaf(x0, x0, ss[t]);
+                ss[t] = fmaf(x1, x1, ss[t]);
+            }
     }
-    block_sum_n<TT>(ss, T, red);
+    block_sum_n<TT>(ss, red_a);
     float ss2[TT];
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
         ss2[t] = 0.0f;
-        if (t < T) {
-            const float r1 = rms_scale(ss[t], H, p.eps);
+        const float r1 = rms_scale(ss[t], H, p.eps);
+        const f2_t r1r1 = f2_pack(r1, r1);
 #pragma unroll
-            for (int i = 0; i < VPT; ++i) {
-                const int v = tid + i * PT;
-                if (v < nvec) {
-                    V8 vr, vh;
-                    const V8& vg = vg1[i];
-                    vr.u = reinterpret_cast<const uint4*>(res_sm + (size_t)t * H)[v];
+        for (int k = 0; k < 2; ++k) {
+            V8 vh;
+            vh.u = make_uint4(0, 0, 0, 0);
+            if (rs.ok[k]) {
+                V8 vg;
+                vg.u = reinterpret_cast<const uint4*>(g1)[rs.v[k]];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float post = rnd<bf16>(__fmul_rn(
-                            __fmul_rn(__bfloat162float(va[t][i].e[e]), r1), __bfloat162float(vg.e[e])));
-                        const bf16 hv = __float2bfloat16_rn(__fadd_rn(__bfloat162float(vr.e[e]), post));
-                        vh.e[e] = hv;
-                        const float hf = __bfloat162float(hv);
-                        ss2[t] = fmaf(hf, hf, ss2[t]);
-                    }
-                    va[t][i].u = vh.u;
-                    reinterpret_cast<uint4*>(sum_sm + (size_t)t * H)[v] = vh.u;
-                    if (sum_g) reinterpret_cast<uint4*>(sum_g + (size_t)t * H)[v] = vh.u;
+                for (int j = 0; j < 4; ++j) {
+                    const f2_t m = f2_mul(f2_mul(bf2_to_f2(va[t][k].w[j]), r1r1), bf2_to_f2(vg.w[j]));
+                    const f2_t post = bf2_to_f2(f2_to_bf2(m));
+                    const uint32_t hb = f2_to_bf2(f2_add(bf2_to_f2(res[t][k].w[j]), post));
+                    vh.w[j] = hb;
+                    const float h0 = __uint_as_float(hb << 16), h1 = __uint_as_float(hb & 0xffff0000u);
+                    ss2[t] = fmaf(h0, h0, ss2[t]);
+                    ss2[t] = fmaf(h1, h1, ss2[t]);
                 }
+                if (sum_g && ((own >> (2 * t + k)) & 1u))
+                    reinterpret_cast<uint4*>(sum_g + (size_t)t * H)[rs.v[k]] = vh.u;
             }
+            sum[t][k] = vh;
         }
     }
-    block_sum_n<TT>(ss2, T, red + TT * 33);
+    block_sum_n<TT>(ss2, red_b);
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
-        if (t < T) {
-            const float r2 = rms_scale(ss2[t], H, p.eps);
+        const float r2 = rms_scale(ss2[t], H, p.eps);
+        const f2_t r2r2 = f2_pack(r2, r2);
 #pragma unroll
-            for (int i = 0; i < VPT; ++i) {
-                const int v = tid + i * PT;
-                if (v < nvec) {
-                    V8 vx;
-                    const V8& vg = vg2[i];
+        for (int k = 0; k < 2; ++k) {
+            const bool mine = (own >> (2 * t + k)) & 1u;
+            V8 vx;
+            vx.u = make_uint4(0, 0, 0, 0);
+            if (rs.ok[k] && (NORM_ALL || mine)) {
+                V8 vg;
+                vg.u = reinterpret_cast<const uint4*>(g2)[rs.v[k]];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        vx.e[e] = __float2bfloat16_rn(__fmul_rn(
-                            __fmul_rn(__bfloat162float(va[t][i].e[e]), r2), __bfloat162float(vg.e[e])));
-                    reinterpret_cast<uint4*>(norm_g + (size_t)t * H)[v] = vx.u;
-                    if (norm_sm) reinterpret_cast<uint4*>(norm_sm + (size_t)t * H)[v] = vx.u;
-                }
+                for (int j = 0; j < 4; ++j)
+                    vx.w[j] = f2_to_bf2(f2_mul(f2_mul(bf2_to_f2(sum[t][k].w[j]), r2r2), bf2_to_f2(vg.w[j])));
+                if (norm_g && mine) reinterpret_cast<uint4*>(norm_g + (size_t)t * H)[rs.v[k]] = vx.u;
             }
+            if (NORM_ALL) norm[t][k] = vx;
         }
     }
 }
@@ -422,13 +585,13 @@ __device__ __forceinline__ void stage_pair(const ChainParams& p, const bf16* a, 
 // Top-K of token t by K rounds over all of its keys (lane l holds experts l, l + 32, ...):
 // each round takes the warp's largest key, the lowest expert among equal keys (redux max,
 // then redux min), and clears it.  The path for rows whose keys tie at the threshold.
-__device__ void topk_rounds(const MainSmem& s, const float* bias_sm, int t, int E, int K) {
+__device__ void topk_rounds(const Smem& s, int t, int E, int K) {
     const int lane = threadIdx.x & 31;
     uint32_t key[kMaxChunks];
 #pragma unroll
     for (int j = 0; j < kMaxChunks; ++j) {
         const int e = lane + 32 * j;
-        key[j] = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
+        key[j] = (e < E) ? okey(s.xrow[t * E_MAX + e] + (s.bias[e] + 0.0f)) : 0u;
     }
     static_assert(kMaxChunks == 16, "four-level tournament");
     for (int r = 0; r < K; ++r) {
@@ -457,10 +620,10 @@ __device__ void topk_rounds(const MainSmem& s, const float* bias_sm, int t, int 
         const bool rt = k2[1] > k2[0];
         const uint32_t best = rt ? k2[1] : k2[0];
         const int bj = rt ? j2[1] : j2[0];
-        const uint32_t wmax = __reduce_max_sync(FULL_MASK, best);
-        const unsigned cand = (best == wmax && best != 0u) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
-        const unsigned widx = __reduce_min_sync(FULL_MASK, cand);
-        if (cand == widx) {
+        const uint32_t wmx = __reduce_max_sync(FULL_MASK, best);
+        const unsigned cnd = (best == wmx && best != 0u) ? (unsigned)(lane + 32 * bj) : 0xffffffffu;
+        const unsigned widx = __reduce_min_sync(FULL_MASK, cnd);
+        if (cnd == widx) {
 #pragma unroll
             for (int j = 0; j < kMaxChunks; ++j)
                 if (j == bj) key[j] = 0u;
@@ -469,82 +632,97 @@ __device__ void topk_rounds(const MainSmem& s, const float* bias_sm, int t, int 
     }
 }
 
-// D: exact top-K per token, then the weights and the maps of the T*K <= 32 selections.
-// Same keys and tie rule as the router kernels: score = logit + (bias + 0), ordered by okey
-// (NaN highest), the lower expert index first.  The bias row (bias_sm) and the layer's
-// logits (xrow, filled from the gate records) sit in shared memory, complete at entry.
-//  1. Every warp, per (token, 32-expert chunk): the key of each expert and the maximum of
-//     each group of G consecutive experts, G the smallest power of two giving ng <= 32
-//     groups (so ng >= K: ng > 16 whenever G > 1, and ng = E >= K when G = 1).
-//  2. Per (token, chunk) again: tau = the K-th largest group maximum (the least maximum
-//     with fewer than K maxima above it).  The K groups with the largest maxima hold K keys
-//     >= tau, so every key of the top K is >= tau; those keys are the candidates, appended
-//     to the token's list (a shared-memory counter hands out the slots).
-//  3. Warp t: with C <= 32 candidates, each one's rank is the number of candidates above it
+// D: exact top-K of every token; the same keys and tie rule as the router kernels: score =
+// logit + (bias + 0), ordered by okey (NaN highest), the lower expert first.
+//  1. Thread i keys experts i and i + kCT; each warp's largest key of token t is its group
+//     maximum (warp w's group: experts 32w.. and kCT + 32w..).
+//  2. tau = the K-th largest group maximum: the K groups with the largest maxima each hold a
+//     key >= tau, so every key of the top K is >= tau.  With fewer than K groups, tau = 0
+//     (every key is a candidate).
+//  3. Keys >= tau are the candidates, appended to the token's list.
+//  4. Warp t: with C <= 32 candidates, each one's rank is the number of candidates above it
 //     in (key, then lower expert) order, found in one pass; ranks below K are the output.
-//     Rows with more candidates (ties at tau) take the K rounds of topk_rounds.
-__device__ __forceinline__ void stage_route_maps(const ChainParams& p, const float* bias_sm,
-                                             const MainSmem& s) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int T = p.T, E = p.E, K = p.K, n = T * K;
-    const int nch = (E + 31) >> 5, units = T * nch;
-    int lg = 0;  // log2 G
-    while (((E + (1 << lg) - 1) >> lg) > 32) ++lg;
-    const int ng = (E + (1 << lg) - 1) >> lg;
-    uint32_t* gmax = reinterpret_cast<uint32_t*>(s.hist);                  // [kChainMaxT][32]
-    unsigned long long* cand = reinterpret_cast<unsigned long long*>(s.offs);  // [kChainMaxT][32]
-    int* ncand = s.scratch;                                                 // [kChainMaxT]
-    if ((int)threadIdx.x < T) ncand[threadIdx.x] = 0;
-    for (int u = warp; u < units; u += kCW) {  // 1: uniform trip count within the warp
-        const int t = u / nch, e = (u - t * nch) * 32 + lane;
-        uint32_t k = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
+//     More candidates (ties at tau) take the K rounds of topk_rounds.
+// Leaves sel (all tokens) complete for every thread; writes ids and weights (CTA 0).
+template <int TT>
+__device__ __forceinline__ void stage_route(const ChainParams& p, const Smem& s) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int T = TT;
+    const int E = p.E, K = p.K;
+    const int ng = min(kCW, (E + 31) >> 5);  // warps holding at least one expert
+    uint32_t key[TT][2];
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1)
-            if (o < (1 << lg)) k = max(k, __shfl_xor_sync(FULL_MASK, k, o));
-        if ((lane & ((1 << lg) - 1)) == 0 && e < E) gmax[t * 32 + (e >> lg)] = k;
+    for (int t = 0; t < TT; ++t) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int e = tid + j * kCT;
+            key[t][j] = (t < T && e < E) ? okey(s.xrow[t * E_MAX + e] + (s.bias[e] + 0.0f)) : 0u;
+        }
+        const uint32_t m = __reduce_max_sync(FULL_MASK, max(key[t][0], key[t][1]));
+        if (lane == 0) s.wmax[t * 32 + warp] = m;
     }
+    if (tid < TT) s.ncand[tid] = 0;
     __syncthreads();
-    for (int u = warp; u < units; u += kCW) {  // 2
-        const int t = u / nch, e = (u - t * nch) * 32 + lane;
-        const uint32_t m = lane < ng ? gmax[t * 32 + lane] : 0u;  // valid maxima are > 0
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+        if (t >= T) break;
+        const uint32_t mj = lane < ng ? s.wmax[t * 32 + lane] : 0u;
         int above = 0;
 #pragma unroll
-        for (int h = 0; h < 32; ++h) above += (__shfl_sync(FULL_MASK, m, h) > m) ? 1 : 0;
-        const uint32_t tau = __reduce_min_sync(FULL_MASK, (lane < ng && above < K) ? m : 0xffffffffu);
-        const uint32_t k = (e < E) ? okey(s.xrow[t * E_MAX + e] + (bias_sm[e] + 0.0f)) : 0u;
-        const bool take = e < E && k >= tau;
-        const unsigned b = __ballot_sync(FULL_MASK, take);
-        int base = 0;
-        if (lane == 0 && b) base = atomicAdd(ncand + t, __popc(b));
-        base = __shfl_sync(FULL_MASK, base, 0);
-        const int slot = base + __popc(b & ((1u << lane) - 1u));
-        if (take && slot < 32)
-            cand[t * 32 + slot] = ((unsigned long long)k << 32) | (unsigned)(0xffffffffu - (unsigned)e);
+        for (int i = 0; i < kCW; ++i) above += (__shfl_sync(FULL_MASK, mj, i) > mj) ? 1 : 0;
+        const uint32_t tau = (ng >= K)
+            ? __reduce_min_sync(FULL_MASK, (lane < ng && above < K) ? mj : 0xffffffffu) : 0u;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int e = tid + j * kCT;
+            const bool take = e < E && key[t][j] >= tau;
+            const unsigned b = __ballot_sync(FULL_MASK, take);
+            if (b) {  // uniform over the warp
+                int base = 0;
+                if (lane == 0) base = atomicAdd(s.ncand + t, __popc(b));
+                base = __shfl_sync(FULL_MASK, base, 0);
+                const int slot = base + __popc(b & ((1u << lane) - 1u));
+                if (take && slot < 32)
+                    s.cand[t * 32 + slot] =
+                        ((unsigned long long)key[t][j] << 32) | (unsigned)(0xffffffffu - (unsigned)e);
+            }
+        }
     }
     __syncthreads();
-    if (warp < T) {  // 3
+    if (warp < T) {
         const int t = warp;
-        const int C = ncand[t];
+        const int C = s.ncand[t];
         if (C <= 32) {
-            const unsigned long long mine = lane < C ? cand[t * 32 + lane] : 0ull;
+            const unsigned long long mine = lane < C ? s.cand[t * 32 + lane] : 0ull;
             int rank = 0;
-            for (int j = 0; j < C; ++j) rank += (cand[t * 32 + j] > mine) ? 1 : 0;
+            for (int j = 0; j < C; ++j) rank += (s.cand[t * 32 + j] > mine) ? 1 : 0;
             if (lane < C && rank < K) s.sel[t * K + rank] = (int)(0xffffffffu - (unsigned)mine);
         } else {
-            topk_rounds(s, bias_sm, t, E, K);
+            topk_rounds(s, t, E, K);
         }
         __syncwarp();
-        if (lane < K) {
+        if (lane < K && blockIdx.x == 0) {
             const int id = s.sel[t * K + lane];
             p.ids[t * K + lane] = id;
             p.w[t * K + lane] = sigmoid_acc(s.xrow[t * E_MAX + id]);
         }
     }
     __syncthreads();
-    // Maps of n <= 32 selections without a scan: offsets[e] = selections below e,
-    // counts[e] = selections equal to e, rank of selection i = selections below its expert
-    // + equal ones before it (selections are in (token, slot) order).
-    for (int e = threadIdx.x; e <= E; e += kCT) {
+}
+
+// D (maps) + E: maps of the n = T*K <= 32 selections without a scan: offsets[e] = selections
+// below e, counts[e] = selections equal to e, rank of selection i = selections below its
+// expert + equal ones before it (selections are in (token, slot) order).  Entry e of offsets
+// and counts is written by CTA e mod G, p2u and u2p by CTA 0.  Every CTA derives the token of
+// each permuted row and stores its share of the expansion from the moe_in rows it holds.
+template <int TT>
+__device__ __forceinline__ void stage_maps_expand(const ChainParams& p, const Smem& s,
+                                                  const V8 (&x)[TT][2], unsigned long long own_perm) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x, G = gridDim.x;
+    constexpr int T = TT;
+    const int E = p.E, K = p.K, n = T * K, nvec = p.H / 8;
+    for (int e = c + tid * G; e <= E; e += kCT * G) {
         int below = 0, equal = 0;
         for (int i = 0; i < n; ++i) {
             const int v = s.sel[i];
@@ -554,89 +732,67 @@ __device__ __forceinline__ void stage_route_maps(const ChainParams& p, const flo
         p.offsets[e] = (int64_t)below;
         if (p.counts && e < E) p.counts[e] = equal;
     }
-    if (warp == 0) {
-        const int e = (lane < n) ? s.sel[lane] : 0x7fffffff;
-        int rank = 0;
-        for (int i = 0; i < n; ++i) {
-            const int v = s.sel[i];
-            rank += (v < e || (v == e && i < lane)) ? 1 : 0;
-        }
-        if (lane < n) {
-            const int tok = lane / K, slot = lane - tok * K;
-            const int u = slot * T + tok;
-            p.p2u[rank] = u;
-            if (p.u2p) p.u2p[u] = rank;
-            s.perm[rank] = tok;
-        }
-    }
-    __syncthreads();
-}
-
-// E: permuted rows straight from the moe_in rows held in shared memory (T > 1).  At T == 1
-// every selection is token 0, so the K permuted rows are copies of moe_in whatever the
-// routing: the gate CTAs write them while they compute the router GEMV (chain_gate).
-__device__ __forceinline__ void stage_expand(const ChainParams& p, const MainSmem& s) {
-    const int nvec = p.H / 8, n = p.T * p.K;
-    for (int r = 0; r < n; ++r) {
-        const uint4* src = reinterpret_cast<const uint4*>(s.x + (size_t)s.perm[r] * p.H);
-        uint4* dst = reinterpret_cast<uint4*>(p.permuted + (size_t)r * p.H);
-        for (int v = threadIdx.x; v < nvec; v += kCT) st_stream(dst + v, src[v]);
-    }
-}
-
-// Waits (bounded) until every logit record of gate CTA c carries `tag`, then stores the
-// logits in xrow[t][e].  A failed wait sets the error word.
-__device__ bool take_records(const ChainParams& p, unsigned c, unsigned gate_ctas, unsigned tag,
-                             float* xrow) {
-    const unsigned long long* rc = p.rec + (size_t)c * kGateMaxExperts * kChainMaxT;
-    const int T = p.T, E = p.E;
-    long long it = 0;
-    while (true) {
-        unsigned long long r[kGateMaxExperts][kChainMaxT];
-        bool all = true;
-#pragma unroll
-        for (int m = 0; m < kGateMaxExperts; ++m)
-#pragma unroll
-            for (int t = 0; t < kChainMaxT; ++t) {
-                const bool used = (int)(c + m * gate_ctas) < E && t < T;
-                r[m][t] = used ? ld_rec(rc + m * kChainMaxT + t) : ((unsigned long long)tag << 32);
-                all = all && (unsigned)(r[m][t] >> 32) == tag;
+    if (TT > 1 || c == 0) {
+        if (warp == 0) {
+            const int e = (lane < n) ? s.sel[lane] : 0x7fffffff;
+            int rank = 0;
+            for (int i = 0; i < n; ++i) {
+                const int v = s.sel[i];
+                rank += (v < e || (v == e && i < lane)) ? 1 : 0;
             }
-        if (all) {
-#pragma unroll
-            for (int m = 0; m < kGateMaxExperts; ++m)
-#pragma unroll
-                for (int t = 0; t < kChainMaxT; ++t) {
-                    const int e = (int)(c + m * gate_ctas);
-                    if (e < E && t < T) xrow[t * E_MAX + e] = __uint_as_float((unsigned)r[m][t]);
+            if (lane < n) {
+                const int tok = lane / K, slot = lane - tok * K;
+                const int u = slot * T + tok;
+                if (c == 0) {
+                    p.p2u[rank] = u;
+                    if (p.u2p) p.u2p[u] = rank;
                 }
-            return true;
+                s.perm[rank] = tok;
+            }
         }
-        if (++it > kChainSpin || ((it & 1023) == 0 && *(volatile int*)p.err)) {
-            atomicExch(p.err, 1);
-            return false;
+        if (TT > 1) __syncthreads();
+    }
+    if (p.permuted) {
+        // own_perm bit 2r+k: vector k of this thread in permuted row r is this CTA's to store.
+        unsigned long long bits = own_perm;
+        while (bits) {
+            const int b = __ffsll((long long)bits) - 1;
+            bits &= bits - 1ull;
+            const int r = b >> 1, k = b & 1;
+            const int tok = TT > 1 ? s.perm[r] : 0;
+            uint4 val = k ? x[0][1].u : x[0][0].u;
+#pragma unroll
+            for (int t = 1; t < TT; ++t)
+                if (t == tok) val = k ? x[t][1].u : x[t][0].u;
+            st_stream(reinterpret_cast<uint4*>(p.permuted) + (size_t)r * nvec + tid + k * p.pt, val);
         }
-        __nanosleep(32);
     }
 }
 
-template <int VPT, int TT>
-__device__ __forceinline__ void chain_main(const ChainParams& p, unsigned char* smem) {
-    const int T = p.T, H = p.H, nvec = H / 8;
-    const MainSmem s = carve_main(smem, H);
-    const unsigned gate_ctas = gridDim.x - 1;
+template <int TT>
+__global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_constant__ ChainParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int tid = threadIdx.x;
+    const int c = blockIdx.x, G = gridDim.x;
+    const int H = p.H, E = p.E, nvec = H / 8;  // p.T == TT
+    if (*(volatile int*)p.err) {  // an earlier call gave up: report and do nothing
+        if (c == 0)
+            for (int e = tid; e <= E; e += kCT) p.offsets[e] = -1;
+        return;
+    }
+    const Smem s = carve(smem_raw, smem_layout(H, p.nown, p.L));
     {  // every layer descriptor into shared memory once
         const int words = p.L * (int)(sizeof(kb_chain_layer_t) / sizeof(int));
-        for (int i = threadIdx.x; i < words; i += kCT)
+        for (int i = tid; i < words; i += kCT)
             reinterpret_cast<int*>(s.layers)[i] = reinterpret_cast<const int*>(p.layers)[i];
     }
-    for (int i = threadIdx.x; i < T * nvec; i += kCT) {
-        const int t = i / nvec, v = i - t * nvec;
-        reinterpret_cast<uint4*>(s.r + (size_t)t * H)[v] =
-            reinterpret_cast<const uint4*>(p.r_in + (size_t)t * H)[v];
+    if (tid == 0) {
+        for (int b = 0; b < kNumBars; ++b) mb_init(s.bar + b, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (tid < 8) s.flag[tid] = 0;
     if (p.pos) {
-        for (int i = threadIdx.x; i < T * kHalfD; i += kCT) {
+        for (int i = tid; i < TT * kHalfD; i += kCT) {
             const int t = i / kHalfD, j = i - t * kHalfD;
             float sv, cv;
             sincosf(__fmul_rn((float)__ldg(p.pos + t), __ldg(p.inv_freq + j)), &sv, &cv);
@@ -644,194 +800,239 @@ __device__ __forceinline__ void chain_main(const ChainParams& p, unsigned char* 
             s.sn[i] = sv;
         }
     }
-    if (threadIdx.x == 0) s.flag[0] = 1;  // cleared only on a failed wait, which returns
     __syncthreads();
-    for (int l = 0; l < p.L; ++l) {
+    // Bulk copies need 16-byte aligned sources: check every layer's weights before any copy.
+    int bad = 0;
+    for (int l = tid; l < p.L; l += kCT) {
         const kb_chain_layer_t& Ly = s.layers[l];
-        // This layer's gate bias into shared memory, in the background until the router.
-        if (Ly.gate_bias) {
-            for (int e = threadIdx.x; e < p.E; e += kCT) cp4(s.bias + e, Ly.gate_bias + e);
-        } else {
-            for (int e = threadIdx.x; e < p.E; e += kCT) s.bias[e] = 0.0f;
-        }
-        cp_commit();
-        if (l + 1 < p.L) {  // the next layer's small weights into L2
-            const kb_chain_layer_t& Ln = s.layers[l + 1];
-            if (Ln.gate_bias && threadIdx.x < (p.E * 4 + 127) / 128)
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(
-                    reinterpret_cast<const char*>(Ln.gate_bias) + threadIdx.x * 128));
-            const int lines = (H * 2 + 127) / 128;
-            for (int i = threadIdx.x; i < 4 * lines; i += kCT) {
-                const int w = i / lines;  // selects, not an indexed array (which lives on the stack)
-                const void* base = w == 0 ? Ln.g_post_attn : w == 1 ? Ln.g_pre_moe
-                                 : w == 2 ? Ln.g_post_ffn : Ln.g_input_ln;
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(
-                    static_cast<const char*>(base) + (size_t)(i - w * lines) * 128));
-            }
-        }
-        stage_qk(p, Ly, s);
-        __syncthreads();
-        stage_pair<VPT, TT>(p, p.attn_out, s.r, static_cast<const bf16*>(Ly.g_post_attn),
-                        static_cast<const bf16*>(Ly.g_pre_moe), s.h, p.h, p.moe_in, s.x, s.red);
-        __syncthreads();
-        // The barrier above orders every thread's rows before the release.
-        if (threadIdx.x == 0) st_rel(p.go, (unsigned)(l + 1));
-        // One thread per gate CTA polls that CTA's logit records (all loads of a poll in
-        // flight at once) until each carries this layer's tag; the logits arrive with it.
-        for (unsigned c = threadIdx.x; c < gate_ctas; c += kCT)
-            if (!take_records(p, c, gate_ctas, (unsigned)(l + 1), s.xrow)) s.flag[0] = 0;
-        cp_wait<0>();  // this thread's part of the bias row; the barrier shares it
-        __syncthreads();
-        if (!s.flag[0]) {
-            for (int e = threadIdx.x; e <= p.E; e += kCT) p.offsets[e] = -1;
-            return;
-        }
-        stage_route_maps(p, s.bias, s);
-        if (p.T > 1) stage_expand(p, s);  // T == 1: the gate CTAs wrote it
-        stage_pair<VPT, TT>(p, p.moe_out, s.h, static_cast<const bf16*>(Ly.g_post_ffn),
-                        static_cast<const bf16*>(Ly.g_input_ln), s.r, p.r_out, p.nxt, nullptr,
-                        s.red);
-        __syncthreads();
+        const uintptr_t a16 = reinterpret_cast<uintptr_t>(Ly.g_post_attn) |
+                              reinterpret_cast<uintptr_t>(Ly.g_pre_moe) |
+                              reinterpret_cast<uintptr_t>(Ly.g_post_ffn) |
+                              reinterpret_cast<uintptr_t>(Ly.g_input_ln) |
+                              reinterpret_cast<uintptr_t>(Ly.g_q) | reinterpret_cast<uintptr_t>(Ly.g_k) |
+                              reinterpret_cast<uintptr_t>(Ly.w_gate_t);
+        const bool nul = !Ly.g_post_attn || !Ly.g_pre_moe || !Ly.g_post_ffn || !Ly.g_input_ln ||
+                         !Ly.g_q || !Ly.g_k || !Ly.w_gate_t;
+        if ((a16 & 15u) || (reinterpret_cast<uintptr_t>(Ly.gate_bias) & 3u) || nul) bad = 1;
     }
-    // Every gate CTA has written its last records: they and go can return to zero.
-    for (unsigned i = threadIdx.x; i < gate_ctas * kGateMaxExperts * kChainMaxT; i += kCT)
-        p.rec[i] = 0ull;
-    if (threadIdx.x == 0) *p.go = 0u;
-}
+    if (__syncthreads_or(bad)) {
+        if (tid == 0) atomicCAS(p.err, 0, kErrAlignment);
+        if (c == 0)
+            for (int e = tid; e <= E; e += kCT) p.offsets[e] = -1;
+        return;
+    }
+    if (tid == 0)
+        for (int b = 0; b < kNumBars; ++b) issue_weights(p, s, b, 0);
+    issue_bias(p, s, 0);
+    const unsigned epoch = *(volatile unsigned*)p.epoch;
 
-// ------------------------------------------------------------------------------------
-// Gate CTAs: router GEMV for experts j, j + G1, ... (G1 = gate CTAs).
-// ------------------------------------------------------------------------------------
-
-template <int VQ, int TT>
-__device__ __forceinline__ void chain_gate(const ChainParams& p, unsigned char* smem) {
-    const int G1 = gridDim.x - 1, j = blockIdx.x - 1;
-    const int H = p.H, E = p.E, T = p.T, nvec = H / 8;
-    bf16* wb = reinterpret_cast<bf16*>(smem);  // [2][kGateMaxExperts][H]
-    float* red = reinterpret_cast<float*>(wb + (size_t)2 * kGateMaxExperts * H);
-    __shared__ int ok;
-    int ne = 0;  // this CTA's experts: j + m * G1 for m < ne
+    // Vectors of this thread: k-th = tid + k*pt; own bit 2t+k: vector (t, k) of a row output
+    // is this CTA's to store; own_perm bit 2r+k: the same in permuted row r.
+    RowSlots rs;
+    unsigned own = 0u;
+    unsigned long long own_perm = 0ull;
 #pragma unroll
-    for (int m = 0; m < kGateMaxExperts; ++m)
-        if (j + m * G1 < E) ne = m + 1;
-    auto issue = [&](int l) {
-        const bf16* W = static_cast<const bf16*>(p.layers[l].w_gate_t);
-        bf16* dst = wb + (size_t)(l & 1) * kGateMaxExperts * H;
-        for (int m = 0; m < ne; ++m)
-            for (int v = threadIdx.x; v < nvec; v += kCT)
-                cp16(dst + (size_t)m * H + v * 8, W + (size_t)(j + m * G1) * H + v * 8);
-        cp_commit();
-    };
-    issue(0);
-    for (int l = 0; l < p.L; ++l) {
-        if (l + 1 < p.L) issue(l + 1);
-        else cp_commit();
-        if (threadIdx.x == 0) ok = wait_geq(p.go, (unsigned)(l + 1), p.err) ? 1 : 0;
-        cp_wait<1>();
-        __syncthreads();
-        if (!ok) {
-            cp_wait<0>();
-            return;
-        }
-        // T == 1: this CTA's share [x0, x1) of the K copies of moe_in (the expansion).  The
-        // first vector of each thread is loaded here and stored after the dot products, so
-        // its L2 round trip overlaps them; every copy is stored before the barrier that
-        // precedes this CTA's records, so moe_in is read before the main CTA can move on.
-        const int xtotal = (T == 1 && p.permuted) ? p.K * nvec : 0;
-        const int xper = (xtotal + G1 - 1) / G1;
-        const int x0 = min(xtotal, j * xper), x1 = min(xtotal, x0 + xper);
-        const int xi = x0 + (int)threadIdx.x;
-        uint4 xcopy = make_uint4(0, 0, 0, 0);
-        if (xi < x1) xcopy = __ldcg(reinterpret_cast<const uint4*>(p.moe_in) + xi % nvec);
-        const bf16* wl = wb + (size_t)(l & 1) * kGateMaxExperts * H;
-        // Warp w takes slice w of H (kCW slices) for every expert of the CTA and every token:
-        // its moe_in vectors once from L2 (one read of moe_in per CTA), the experts' W
-        // vectors from shared memory, one accumulator per (expert, token), a warp sum; the
-        // slices are then added in order by one thread per (expert, token).
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        const int S = (nvec + kCW - 1) / kCW;  // vectors per slice
-        const int v0 = warp * S, v1 = min(v0 + S, nvec);
-        float acc[kGateMaxExperts][TT];
-#pragma unroll
-        for (int m = 0; m < kGateMaxExperts; ++m)
-#pragma unroll
-            for (int t = 0; t < TT; ++t) acc[m][t] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < VQ; ++i) {
-            const int v = v0 + lane + 32 * i;
-            const bool in = v < v1;
-            const int vc = in ? v : v0;  // clamped: every load in flight at once
-            V8 xv[TT];
-#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int v = tid + k * p.pt;
+        rs.v[k] = v;
+        rs.ok[k] = tid < p.pt && k < p.vpt && v < nvec;
+        if (rs.ok[k]) {
             for (int t = 0; t < TT; ++t)
-                xv[t].u = __ldcg(reinterpret_cast<const uint4*>(p.moe_in + (size_t)min(t, T - 1) * H) + vc);
+                if ((t * nvec + v) % G == c) own |= 1u << (2 * t + k);
+            for (int rr = 0; rr < TT * p.K; ++rr)
+                if ((rr * nvec + v) % G == c) own_perm |= 1ull << (2 * rr + k);
+        }
+    }
+    V8 r[TT][2], hh[TT][2], x[TT][2];
 #pragma unroll
-            for (int m = 0; m < kGateMaxExperts; ++m) {
-                if (m < ne && in) {
-                    V8 wv;
-                    wv.u = reinterpret_cast<const uint4*>(wl + (size_t)m * H)[vc];
+    for (int t = 0; t < TT; ++t)
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            r[t][k].u = rs.ok[k] ? reinterpret_cast<const uint4*>(p.r_in + (size_t)t * H)[rs.v[k]]
+                                 : make_uint4(0, 0, 0, 0);
+    int mine = 0;  // experts owned: c + m*G, m < mine
+    for (int m = 0; m < p.nown; ++m)
+        if (c + m * G < E) mine = m + 1;
+    const int warp = tid >> 5, lane = tid & 31;
+
+    float* red0 = s.red;
+    float* red1 = s.red + kRedVals * 33;
+    int l = 0;
+    for (; l < p.L; ++l) {
+        const kb_chain_layer_t& Ly = s.layers[l];
+        const unsigned par = (unsigned)(l & 1);
+        const unsigned tag = epoch * 256u + (unsigned)l + 1u;
+        const bool more = l + 1 < p.L;
+
+        // ---- A: Q/K norm + RoPE ----
+        stage_qk<TT>(p, s, !Ly.rnope && p.pos != nullptr, par);
+        __syncthreads();
+        if (tid == 0 && more && !s.flag[0]) issue_weights(p, s, kBarQK, l + 1);
+
+        // ---- B: sandwich ----
+        stage_pair<TT, true>(p, s, rs, p.attn_out, r, kBarA, par, s.ga, s.ga + H, hh, x, p.h, p.moe_in,
+                             own, red0, red1);
+
+        // ---- C: router GEMV over the owned experts, records out ----
+        // Each thread's dot products run on fp32 pairs (even and odd elements), added at the end.
+        wait_weights(p, s, kBarW, par);
+        float acc[kMaxOwn * TT];
+        {
+            f2_t acc2[kMaxOwn][TT];
+#pragma unroll
+            for (int m = 0; m < kMaxOwn; ++m)
+#pragma unroll
+                for (int t = 0; t < TT; ++t) acc2[m][t] = 0ull;  // (+0, +0)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                if (rs.ok[k]) {
+                    f2_t xf[TT][4];
 #pragma unroll
                     for (int t = 0; t < TT; ++t)
 #pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            acc[m][t] = fmaf(__bfloat162float(xv[t].e[e]), __bfloat162float(wv.e[e]), acc[m][t]);
+                        for (int j = 0; j < 4; ++j) xf[t][j] = bf2_to_f2(x[t][k].w[j]);
+#pragma unroll
+                    for (int m = 0; m < kMaxOwn; ++m) {
+                        if (m < mine) {
+                            V8 wv;
+                            wv.u = reinterpret_cast<const uint4*>(s.w + (size_t)m * H)[rs.v[k]];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const f2_t wf = bf2_to_f2(wv.w[j]);
+#pragma unroll
+                                for (int t = 0; t < TT; ++t) acc2[m][t] = f2_fma(xf[t][j], wf, acc2[m][t]);
+                            }
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < kMaxOwn; ++m)
+#pragma unroll
+                for (int t = 0; t < TT; ++t) {
+                    float lo, hi;
+                    f2_unpack(acc2[m][t], lo, hi);
+                    acc[m * TT + t] = lo + hi;
+                }
+        }
+        block_sum_n<kMaxOwn * TT>(acc, red0);
+        unsigned long long* bank = p.rec + (size_t)par * kChainMaxT * E_MAX;
+#pragma unroll
+        for (int m = 0; m < kMaxOwn; ++m)
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+                if (tid == m * TT + t && m < mine) {
+                    const float v = __bfloat162float(__float2bfloat16_rn(acc[m * TT + t]));
+                    const int e = c + m * G;
+                    st_rec(bank + (size_t)t * E_MAX + e, ((unsigned long long)tag << 32) | __float_as_uint(v));
+                    p.logits[(size_t)t * E + e] = v;
+                    if (p.trace_logits) p.trace_logits[((size_t)l * TT + t) * E + e] = v;
+                }
+        // Every read of ga and of the W rows is behind block_sum_n's barrier; the copies are
+        // issued by the last warp, after the records are out.
+        if (tid == kCT - 32 && more && !s.flag[0]) {
+            issue_weights(p, s, kBarA, l + 1);
+            issue_weights(p, s, kBarW, l + 1);
+        }
+
+        // ---- all-gather of the layer's logits: thread i polls records i and i + kCT ----
+        {
+            unsigned pending = 0u;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int t = 0; t < TT; ++t)
+                    if (tid + j * kCT < E) pending |= 1u << (j * TT + t);
+            long long it = 0;
+            while (pending) {
+                unsigned long long v[2][TT];
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int t = 0; t < TT; ++t)
+                        v[j][t] = ((pending >> (j * TT + t)) & 1u)
+                                      ? ld_rec(bank + (size_t)t * E_MAX + tid + j * kCT) : 0ull;
+#pragma unroll
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int t = 0; t < TT; ++t)
+                        if (((pending >> (j * TT + t)) & 1u) && (unsigned)(v[j][t] >> 32) == tag) {
+                            s.xrow[t * E_MAX + tid + j * kCT] = __uint_as_float((unsigned)v[j][t]);
+                            pending &= ~(1u << (j * TT + t));
+                        }
+                if (pending) {
+                    if (++it > kChainSpin || ((it & 1023) == 0 && leaving(p, s))) {
+                        give_up(p, s, kErrTimeout);
+                        break;
+                    }
+                    __nanosleep(32);
                 }
             }
         }
-#pragma unroll
-        for (int m = 0; m < kGateMaxExperts; ++m)
-#pragma unroll
-            for (int t = 0; t < TT; ++t)
-                if (m < ne && t < T) {  // ne and T are uniform over the CTA
-                    const float sum = warp_sum(acc[m][t]);
-                    if (lane == 0) red[(m * kCW + warp) * TT + t] = sum;
-                }
-        if (xi < x1) st_stream(reinterpret_cast<uint4*>(p.permuted) + xi, xcopy);
-        for (int i = xi + kCT; i < x1; i += kCT)  // shares longer than one vector per thread
-            st_stream(reinterpret_cast<uint4*>(p.permuted) + i,
-                      __ldcg(reinterpret_cast<const uint4*>(p.moe_in) + i % nvec));
+        cp_wait_all();  // this thread's part of the bias row
         __syncthreads();
-        if (threadIdx.x < ne * TT) {
-            const int mm = threadIdx.x / TT, t = threadIdx.x - mm * TT;
-            float sum = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kCW; ++w) sum += red[(mm * kCW + w) * TT + t];
-            const float v = __bfloat162float(__float2bfloat16_rn(sum));
-            const int e = j + mm * G1;
-            p.logits[(size_t)t * E + e] = v;
-            if (p.trace_logits) p.trace_logits[((size_t)l * T + t) * E + e] = v;
-            st_rec(p.rec + ((size_t)j * kGateMaxExperts + mm) * kChainMaxT + t,
-                   ((unsigned long long)(l + 1) << 32) | __float_as_uint(v));
-        }
-        __syncthreads();  // this layer's reads of moe_in and of the W buffer are over
-    }
-}
 
-template <int VPT, int TT>
-__global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_constant__ ChainParams p) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    if (*(volatile int*)p.err) {  // an earlier call gave up: report and do nothing
-        if (blockIdx.x == 0)
-            for (int e = threadIdx.x; e <= p.E; e += kCT) p.offsets[e] = -1;
-        return;
+        // ---- D: router, maps; E: expansion ----
+        stage_route<TT>(p, s);
+        if (more) issue_bias(p, s, l + 1);  // every bias read is behind stage_route's barrier
+        stage_maps_expand<TT>(p, s, x, own_perm);
+
+        // ---- F: post-MoE + next layer's input norm ----
+        V8 unused[TT][2];
+        stage_pair<TT, false>(p, s, rs, p.moe_out, hh, kBarB, par, s.gb, s.gb + H, r, unused, p.r_out,
+                              p.nxt, own, red1, red0);
+        __syncthreads();
+        if (tid == 0 && more && !s.flag[0]) issue_weights(p, s, kBarB, l + 1);
+        if (s.flag[0]) break;  // uniform: read after the barrier, written before it
     }
-    // The stages read the parameters from a shared-memory copy (short, fixed latency).
-    __shared__ ChainParams ps;
-    constexpr int kWords = (int)(sizeof(ChainParams) / sizeof(int));
-    static_assert(sizeof(ChainParams) % sizeof(int) == 0, "ChainParams copy");
-    for (int i = threadIdx.x; i < kWords; i += kCT)
-        reinterpret_cast<int*>(&ps)[i] = reinterpret_cast<const int*>(&p)[i];
-    __syncthreads();
-    if (blockIdx.x == 0) chain_main<VPT, TT>(ps, smem);
-    else chain_gate<VPT, TT>(ps, smem);  // a slice of H / kCW vectors: at most VPT per lane
+    if (l < p.L) {  // left early: no copy may still be writing when the CTA exits
+        if (tid == 0) {
+            // The last phase issued on each buffer (every earlier one completed) is the current
+            // phase or, complete, the one before it; its parity waits only in the first case.
+            for (int b = 0; b < kNumBars; ++b) {
+                const int n = s.flag[4 + b];
+                long long it = 0;
+                while (n > 0 && !mb_try(s.bar + b, (unsigned)((n - 1) & 1)) && ++it < kChainSpin)
+                    __nanosleep(20);
+            }
+        }
+        cp_wait_all();
+        for (int e = c + tid * G; e <= E; e += kCT * G) p.offsets[e] = -1;
+        __syncthreads();
+    }
+    // The last CTA out advances the epoch (every CTA read it at the start) and resets the exit
+    // counter; the kernel boundary publishes both to the next call.
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(p.done, 1u) == (unsigned)G - 1u) {
+            atomicExch(p.done, 0u);
+            atomicAdd(p.epoch, 1u);
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------------
 // Host
 // ------------------------------------------------------------------------------------
-template <int VPT, int TT>
+template <typename... KArgs, typename... Args>
+int launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+template <int TT>
 int run_chain(const ChainParams& prm, size_t smem, int grid, cudaStream_t st) {
-    auto* kern = decode_chain_kernel<VPT, TT>;
+    auto* kern = decode_chain_kernel<TT>;
     int err = allow_smem(kern, smem);
     if (err) return err;
     int nb = 0;
@@ -840,29 +1041,9 @@ int run_chain(const ChainParams& prm, size_t smem, int grid, cudaStream_t st) {
     return launch_coop(kern, dim3((unsigned)grid), dim3(kCT), smem, st, prm);
 }
 
-template <int VPT>
-int run_tokens(int T, const ChainParams& prm, size_t smem, int grid, cudaStream_t st) {
-    switch (T) {
-        case 1: return run_chain<VPT, 1>(prm, smem, grid, st);
-        case 2: return run_chain<VPT, 2>(prm, smem, grid, st);
-        case 3: return run_chain<VPT, 3>(prm, smem, grid, st);
-        case 4: return run_chain<VPT, 4>(prm, smem, grid, st);
-        default: return KB_ERR_UNSUPPORTED;
-    }
-}
-
-int sm_count() {
-    static std::mutex mu;
-    static int cache[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lk(mu);
-    int& v = cache[dev & 63];
-    if (v == 0) {
-        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-        if (v <= 0) v = 148;
-    }
-    return v;
+bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + nb && y < x + na;
 }
 
 }  // namespace
@@ -870,9 +1051,7 @@ int sm_count() {
 
 using namespace kb;
 
-extern "C" size_t kb_decode_chain_workspace_bytes(void) {
-    return 256 + (size_t)8 * kMaxGateCtas * kGateMaxExperts * kChainMaxT;
-}
+extern "C" size_t kb_decode_chain_workspace_bytes(void) { return kWsBytes; }
 
 extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, const void* attn_out,
                                const void* moe_out, const void* q, const void* k,
@@ -887,21 +1066,37 @@ extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, con
     if (n_layers > kChainMaxLayers) return KB_ERR_UNSUPPORTED;
     if (T < 1 || n_layers < 1 || H <= 0 || Hq < 0 || Hkv < 0 || E <= 0 || K <= 0)
         return KB_ERR_INVALID_ARG;
-    if (T > kChainMaxT || D != 128 || H % 8 != 0 || row_shape(H / 8).vpt == 0 || row_shape(H / 8).vpt > 3 || E > E_MAX ||
-        K > kChainMaxK || K > E || Hq + Hkv <= 0)
+    const RowShape rs = H % 8 == 0 ? row_shape(H / 8) : RowShape{0, 0};
+    if (T > kChainMaxT || D != 128 || H % 8 != 0 || rs.vpt == 0 || rs.vpt > 2 || rs.threads > kCT ||
+        E > E_MAX || K > kChainMaxK || K > E || Hq + Hkv <= 0)
         return KB_ERR_UNSUPPORTED;
     if (!layers || !attn_out || !moe_out || !q || !k || !residual_in || !residual_out || !h ||
         !moe_in || !next || !q_out || !k_out || !logits || !ids || !weights || !offsets ||
         !p2u || !permuted || (pos && !inv_freq))
         return KB_ERR_INVALID_ARG;
-    if (!workspace || workspace_bytes < kb_decode_chain_workspace_bytes()) return KB_ERR_WORKSPACE;
+    if (!workspace || workspace_bytes < kWsBytes) return KB_ERR_WORKSPACE;
     const void* vec_ptrs[] = {attn_out, moe_out, q, k, residual_in, residual_out, h, moe_in,
                               next, q_out, k_out, permuted, workspace};
     for (const void* v : vec_ptrs)
         if (!aligned16(v)) return KB_ERR_ALIGNMENT;
-    const int sms = sm_count();
-    const int gate = std::min(std::min(sms - 1, E), kMaxGateCtas);
-    if (gate < 1 || (int64_t)gate * kGateMaxExperts < E) return KB_ERR_UNSUPPORTED;
+    // Every CTA reads the GEMM stand-ins in every layer while owners store the outputs, so no
+    // output may overlap an input (the residual stream may be updated in place: every CTA
+    // reads residual_in before any CTA can finish the first layer's router all-gather).
+    const size_t row = (size_t)T * H * sizeof(bf16);
+    const size_t qb = (size_t)T * Hq * D * sizeof(bf16), kbb = (size_t)T * Hkv * D * sizeof(bf16);
+    const void* ins[] = {attn_out, moe_out, q, k};
+    const size_t in_b[] = {row, row, qb, kbb};
+    const void* outs[] = {h, moe_in, next, q_out, k_out, permuted, residual_out};
+    const size_t out_b[] = {row, row, row, qb, kbb, (size_t)T * K * H * sizeof(bf16), row};
+    for (int i = 0; i < 4; ++i)
+        for (int j = 0; j < 7; ++j)
+            if (in_b[i] && out_b[j] && overlaps(ins[i], in_b[i], outs[j], out_b[j])) return KB_ERR_INVALID_ARG;
+    const int G = device_sm_count();
+    const int nown = (E + G - 1) / G;
+    if ((int64_t)T * (Hq + Hkv) > 3 * (int64_t)G) return KB_ERR_UNSUPPORTED;  // head owners
+    if (nown > kMaxOwn) return KB_ERR_UNSUPPORTED;
+    const size_t smem = smem_layout(H, nown, n_layers).total;
+    if (smem > (size_t)227 * 1024) return KB_ERR_UNSUPPORTED;
     ChainParams prm;
     prm.layers = layers;
     prm.L = n_layers;
@@ -911,6 +1106,9 @@ extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, con
     prm.Hkv = Hkv;
     prm.E = E;
     prm.K = K;
+    prm.pt = rs.threads;
+    prm.vpt = rs.vpt;
+    prm.nown = nown;
     prm.eps = eps;
     prm.attn_out = static_cast<const bf16*>(attn_out);
     prm.moe_out = static_cast<const bf16*>(moe_out);
@@ -935,18 +1133,16 @@ extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, con
     prm.u2p = u2p;
     prm.trace_logits = trace_logits;
     unsigned char* wsb = static_cast<unsigned char*>(workspace);
-    prm.go = reinterpret_cast<unsigned*>(wsb);
-    prm.err = reinterpret_cast<int*>(wsb + 128);
-    prm.rec = reinterpret_cast<unsigned long long*>(wsb + 256);
-    const size_t smem = std::max(main_smem_bytes(H), gate_smem_bytes(H));
-    const RowShape rs = row_shape(H / 8);
-    const int vpt = rs.vpt;
-    prm.pair_threads = rs.threads;
+    prm.epoch = reinterpret_cast<unsigned*>(wsb + kWsEpoch);
+    prm.done = reinterpret_cast<unsigned*>(wsb + kWsDone);
+    prm.err = reinterpret_cast<int*>(wsb + kWsErr);
+    prm.rec = reinterpret_cast<unsigned long long*>(wsb + kWsRec);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    switch (vpt) {
-        case 1: return run_tokens<1>((int)T, prm, smem, 1 + gate, st);
-        case 2: return run_tokens<2>((int)T, prm, smem, 1 + gate, st);
-        case 3: return run_tokens<3>((int)T, prm, smem, 1 + gate, st);
+    switch (T) {
+        case 1: return run_chain<1>(prm, smem, G, st);
+        case 2: return run_chain<2>(prm, smem, G, st);
+        case 3: return run_chain<3>(prm, smem, G, st);
+        case 4: return run_chain<4>(prm, smem, G, st);
         default: return KB_ERR_UNSUPPORTED;
     }
 }

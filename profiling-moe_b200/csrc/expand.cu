@@ -71,7 +71,8 @@ extern "C" int kb_expand_rows(const void* x, void* out, const int32_t* p2u, int6
     if (rows == 0 || row_bytes == 0) return KB_OK;
     if (T == 0 || !x || !out || !p2u) return KB_ERR_INVALID_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    const int64_t ctas = std::min<int64_t>((rows + 7) / 8, 148 * 64);
+    // Eight rows per CTA (one per warp), at most 8 resident CTAs of 256 threads per SM.
+    const int64_t ctas = std::min<int64_t>((rows + 7) / 8, (int64_t)device_sm_count() * 8);
     dim3 grid((unsigned)ctas), block(256);
     if (row_bytes % 16 == 0 && aligned16(x) && aligned16(out)) {
         return launch(expand_rows_vec_kernel<4>, grid, block, 0, st,

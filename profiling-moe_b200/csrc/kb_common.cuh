@@ -30,6 +30,9 @@ __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.laun
 // Host: launch with optional PDL attribute.  Returns a cudaError_t (0 = success).
 bool pdl_enabled();
 
+// Host: multiprocessor count of the current device (cached per device; 148 on B200).
+int device_sm_count();
+
 template <typename... KArgs, typename... Args>
 inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                   cudaStream_t stream, Args&&... args) {

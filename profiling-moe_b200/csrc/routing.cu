@@ -2570,6 +2570,12 @@ int noalloc_scratch(cudaStream_t st, int flags, void** out) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return static_cast<int>(e);
     if (dev < 0 || dev >= 64) return KB_ERR_UNSUPPORTED;
+    if (st != nullptr) {  // the scratch address is per device: the stream must be this device's
+        int sdev = -1;
+        e = cudaStreamGetDevice(st, &sdev);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        if (sdev != dev) return KB_ERR_INVALID_ARG;
+    }
     std::lock_guard<std::mutex> lk(mu);
     void* p = ptrs[dev];
     const bool first = (p == nullptr);

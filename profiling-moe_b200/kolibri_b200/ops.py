@@ -170,9 +170,13 @@ def expert_maps_noalloc(ids: torch.Tensor, c: torch.Tensor, off: torch.Tensor,
         _contig(t, name)
         if t.dtype != dt or t.numel() != n:
             raise ValueError(f"{name} must be {dt} with {n} elements")
-    check(load().kb_expert_maps_noalloc(_p(ids), _p(c), _p(off), _p(p2u), _p(u2p), T, E, k,
-                                        KB_NOALLOC_REZERO if rezero else 0, _stream(ids.device)),
-          "kb_expert_maps_noalloc")
+        if t.device != ids.device:
+            raise ValueError(f"{name} must be on {ids.device}")
+    with torch.cuda.device(ids.device):  # the library resolves the scratch of the current device
+        check(load().kb_expert_maps_noalloc(_p(ids), _p(c), _p(off), _p(p2u), _p(u2p), T, E, k,
+                                            KB_NOALLOC_REZERO if rezero else 0,
+                                            _stream(ids.device)),
+              "kb_expert_maps_noalloc")
 
 
 def router_maps(logits: torch.Tensor, bias: Optional[torch.Tensor] = None, k: int = 6,

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference's own eager code.
 
-Run in a container that has the reference checkout (default /root/reference, or
-KOLIBRI_REFERENCE=<path>):
+Run with the reference checkout named by the KOLIBRI_REFERENCE environment variable
+(required; there is no default path):
 
-    python tests/golden/make_golden.py
+    KOLIBRI_REFERENCE=<path to the profiling-moe checkout> python tests/golden/make_golden.py
 
 The reference scripts import CUDA extensions at module level, so each eager function is
 pulled out of its source file with `ast` (only that function's definition is executed) and
@@ -37,7 +37,14 @@ REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO / "profiling-moe_b200"))
 from kolibri_b200 import workloads as wl  # noqa: E402
 
-REF = Path(os.environ.get("KOLIBRI_REFERENCE", "/root/reference"))
+def _reference_root() -> Path:
+    root = os.environ.get("KOLIBRI_REFERENCE")
+    if not root:
+        raise SystemExit("set KOLIBRI_REFERENCE to the reference checkout (no default path)")
+    return Path(root)
+
+
+REF = _reference_root()
 
 
 def extract(rel: str, name: str, extra_globals: dict | None = None):
