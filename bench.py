@@ -53,6 +53,11 @@ def parse():
     p.add_argument("--chain-tokens", default="1,32,256,8192",
                    help="batch sizes of the 50-layer decode chain ('' = skip)")
     p.add_argument("--chain-layers", type=int, default=50)
+    p.add_argument("--no-kernels", action="store_true",
+                   help="skip the per-kernel table (configs 2/3, expansion, finalize, maps)")
+    p.add_argument("--only-kernel", default="",
+                   help="time one kernel of the per-kernel table alone (profiling runs)")
+    p.add_argument("--only-T", type=int, default=0)
     return p.parse_args()
 
 
@@ -165,6 +170,88 @@ def cpu_reference_rate(T: int, steps: int, warmup: int, budget_s: float):
             "ms_per_step": med * 1e3}
 
 
+def cpu_kernel_times(entries: dict, budget_s: float = 120.0):
+    """The reference's eager CPU path of every kernel of the per-kernel table, on the host
+    cores, at the same T (median of up to 5 reps after one warm-up, each (kernel, T) capped
+    at about 2 s): fills cpu_us_per_call / cpu_cores / cpu_kind into the entries in place."""
+    from kolibri_b200 import workloads as wl
+    from oracle import kolibri_oracle as orc  # CPU baseline leg only
+    torch.set_num_threads(os.cpu_count() or 1)
+    t_all = time.perf_counter()
+    cache = {}
+
+    def cached(key, make):
+        if key not in cache:
+            cache.clear()  # one input family at a time (bounded host memory)
+            cache[key] = make()
+        return cache[key]
+
+    def inputs(name, T):
+        if name.startswith("qk_norm_rope"):
+            q, k, gq, gk, pos = cached(("qk", T), lambda: wl.qk_inputs(T))
+            pos_ = None if name.endswith("rnope") else pos
+            return lambda: orc.qk_norm_rope_ref(q, k, gq, gk, pos_, wl.EPS)
+        if name in ("sandwich", "post_moe_pre_attn", "add_rms_norm"):
+            ni = cached(("norm", T), lambda: wl.norm_inputs(T))
+        if name == "sandwich":
+            return lambda: orc.sandwich_ref(ni.attn_out, ni.residual, ni.g_post_attn,
+                                            ni.g_pre_moe, wl.EPS)
+        if name == "post_moe_pre_attn":
+            return lambda: orc.post_moe_pre_attn_ref(ni.moe_out, ni.residual, ni.g_post_moe,
+                                                     ni.g_pre_attn, wl.EPS)
+        if name == "add_rms_norm":
+            return lambda: orc.add_post_moe_norm_ref(ni.moe_out, ni.residual, ni.g_post_moe,
+                                                     wl.EPS)
+        logits, bias = cached(("router", T), lambda: wl.router_inputs(T, seed=1))
+        if name == "router_maps":
+            return lambda: orc.router_maps_eager_reference(logits, bias)
+        ids, w, *_ = orc.router_maps_eager_reference(logits, bias)
+        if name == "expert_maps":
+            return lambda: orc.maps_eager_reference(ids)
+        _, _, _, _, p2u, u2p = orc.router_maps_eager_reference(logits, bias)
+        x = torch.randn(T, wl.HIDDEN).to(torch.bfloat16)
+        if name == "expansion":
+            return lambda: orc.expansion_ref(x, p2u.numpy())
+        rows = torch.randn(T * wl.TOP_K, wl.HIDDEN).to(torch.bfloat16)
+        return lambda: orc.finalize_ref(rows, u2p.numpy(), w)
+
+    order = sorted(((name, T) for name, by_t in entries.items() for T in by_t),
+                   key=lambda nt: (nt[0].startswith("qk"), nt[0] in ("sandwich", "post_moe_pre_attn",
+                                                                      "add_rms_norm"), int(nt[1])))
+    for name, T in order:
+        rec = entries[name][T]
+        if time.perf_counter() - t_all > budget_s:
+            rec["cpu_us_per_call"] = None
+            continue
+        fn = inputs(name, int(T))
+        fn()
+        times = []
+        t0 = time.perf_counter()
+        while len(times) < 5 and time.perf_counter() - t0 < 2.0:
+            a = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - a)
+        rec["cpu_us_per_call"] = round(statistics.median(times) * 1e6, 1)
+        rec["cpu_cores"] = torch.get_num_threads()
+        rec["cpu_kind"] = "port"
+
+
+def kernel_table(dev, stream, peak, only=None, only_T=0):
+    """Per-kernel device timings (kolibri_b200.kbench) at every BASELINE token count."""
+    from kolibri_b200 import kbench
+    out = {}
+    for name, Ts in kbench.KERNEL_T.items():
+        if only and name != only:
+            continue
+        out[name] = {}
+        for T in Ts:
+            if only_T and T != only_T:
+                continue
+            out[name][str(T)] = kbench.run_kernel(name, dev, T, peak, stream)
+            torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -256,6 +343,19 @@ def ep_round_trip(dev, world, rank, T=4096, H=6144, steps=10, warmup=3):
     logits, bias = wl.router_inputs(T, seed=41 + rank)
     logits, bias = logits.to(dev), bias.to(dev)
     ep = ExpertParallel(E, K)
+    # Parity: with identity experts, combine(dispatch(x)) equals the one-GPU path
+    # finalize(expand(x)) of the same routing, bit for bit, on every rank.
+    from kolibri_b200 import ops
+    d0 = ep.dispatch(x, logits, bias)
+    out0 = ep.combine(d0, d0.rows)
+    _, w0, _, _, p2u0, u2p0 = ops.router_maps(logits, bias)
+    ref0 = ops.moe_finalize(ops.expand_rows(x, p2u0), u2p0, w0)
+    Er = E // world
+    owned = bool(((d0.meta[:, 0] >= rank * Er) & (d0.meta[:, 0] < (rank + 1) * Er)).all())
+    ok = torch.tensor([1 if (torch.equal(out0, ref0) and owned) else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    parity = bool(ok.item())
+    del d0, out0, ref0
     sent = 0
     for i in range(warmup + steps):
         if i == warmup:
@@ -274,6 +374,7 @@ def ep_round_trip(dev, world, rank, T=4096, H=6144, steps=10, warmup=3):
     ms = float(ms.item())
     nvlink_bytes = 2 * sent * (H * 2 + 12)  # rows and metadata out, rows back
     return {"tokens_per_gpu": T, "hidden": H, "experts_per_gpu": E // world,
+            "ep_parity": parity,
             "us_per_step": round(ms * 1e3, 2),
             "stages": "router+maps, expansion, count all-gather, row+meta all-to-all, "
                       "grouping by local expert, reverse all-to-all, finalize",
@@ -300,6 +401,15 @@ def main():
 
     from kolibri_b200 import _lib, ops
     from kolibri_b200 import workloads as wl
+
+    if args.only_kernel:  # one kernel of the per-kernel table alone (profiling runs)
+        peak, _ = measured_peak()
+        tab = kernel_table(dev, torch.cuda.Stream(dev), peak, args.only_kernel, args.only_T)
+        if rank == 0:
+            print(json.dumps({"kernels": tab}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     T = args.tokens
     nsets = 4
@@ -445,6 +555,12 @@ def main():
 
     ep = ep_round_trip(dev, world, rank) if world > 1 else None
 
+    kernels = None
+    if not args.no_kernels and world == 1:
+        kernels = kernel_table(dev, stream, peak)
+        if rank == 0 and not args.no_cpu_baseline:
+            cpu_kernel_times(kernels)
+
     chain = None
     if args.chain_tokens:
         chain = decode_chain_times(dev, [int(t) for t in args.chain_tokens.split(",") if t],
@@ -479,6 +595,7 @@ def main():
         "cpu_baseline": cpu,
         "e2e": e2e,
         "decode_chain": chain,
+        "kernels": kernels,
         "ep_dispatch": ep,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),

@@ -93,6 +93,22 @@ def expert_maps_ref(ids, num_experts: int = 384):
     return counts, offsets, p2u, u2p
 
 
+def maps_eager_reference(ids: torch.Tensor, num_experts: int = 384):
+    """The map part of benchmarks/08_benchmark_router_dispatch.py:24-49 on the CPU (slot-major
+    flatten, stable argsort, bincount, cumsum) plus the inverse map: the eager counterpart of
+    kb_expert_maps that the timed CPU baseline runs.  -> (counts, offsets, p2u, u2p)."""
+    T, k = ids.shape
+    flat_experts = ids.t().contiguous().view(-1).long()
+    order = torch.argsort(flat_experts, stable=True)
+    p2u = order.to(torch.int32)
+    counts = torch.bincount(flat_experts, minlength=num_experts)
+    offsets = torch.zeros(num_experts + 1, dtype=torch.int64)
+    offsets[1:] = torch.cumsum(counts, dim=0)
+    u2p = torch.empty(T * k, dtype=torch.int32)
+    u2p[order] = torch.arange(T * k, dtype=torch.int32)
+    return counts, offsets, p2u, u2p
+
+
 def router_maps_eager_reference(logits: torch.Tensor, bias: torch.Tensor, k: int = 6,
                                 num_experts: int = 384):
     """The reference's eager router + dispatch-map path on the CPU, the baseline that the

@@ -357,6 +357,28 @@ __device__ __forceinline__ void issue_bias(const ChainParams& p, const Smem& s, 
 // Block-wide sums of n values at once; each value is reduced exactly as block_sum reduces it
 // (warp butterfly, then a butterfly over the warp partials, lanes past the last warp adding
 // 0).  One barrier; the next call must take the other buffer.
+// The butterfly of warp_sum over the kCW warp partials w[0..kCW) (lanes past kCW holding
+// 0.0f), as lane 0 would compute it, from shared memory: the same additions in the same tree,
+// so the same bits (every lane of a xor butterfly ends with identical bits).
+__device__ __forceinline__ float butterfly_of_partials(const float* w) {
+    static_assert(kCW <= 16, "partials fit the lower half-warp");
+    float a[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = (i < kCW ? w[i] : 0.0f) + 0.0f;  // level 16: + lane i+16
+    float b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = a[i] + a[i + 8];  // level 8
+    float c4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c4[i] = b[i] + b[i + 4];  // level 4
+    const float d0 = c4[0] + c4[2], d1 = c4[1] + c4[3];  // level 2
+    return d0 + d1;                                       // level 1
+}
+
+// Block-wide sums of MAXN values at once; each value is reduced exactly as block_sum reduces
+// it (warp butterfly, then a butterfly over the warp partials, lanes past the last warp
+// adding 0), the second butterfly replayed from shared memory.  One barrier; the next call
+// must take the other buffer.
 template <int MAXN>
 __device__ __forceinline__ void block_sum_n(float (&v)[MAXN], float* red) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -367,7 +389,7 @@ __device__ __forceinline__ void block_sum_n(float (&v)[MAXN], float* red) {
     }
     __syncthreads();
 #pragma unroll
-    for (int m = 0; m < MAXN; ++m) v[m] = warp_sum((lane < kCW) ? red[m * 33 + lane] : 0.0f);
+    for (int m = 0; m < MAXN; ++m) v[m] = butterfly_of_partials(red + m * 33);
 }
 
 // ------------------------------------------------------------------------------------
@@ -377,17 +399,21 @@ __device__ __forceinline__ void block_sum_n(float (&v)[MAXN], float* red) {
 // A: per-head RMSNorm + NeoX RoPE of every head of the T tokens (one warp per head, four
 // consecutive elements per lane, as qk_norm_rope_kernel<128>: the NeoX partner of lane l is
 // lane l^16).  Head j (over tokens and q then k heads) is stored by CTA j mod G (j < 3G).  A
-// warp takes kQkChunk heads at once and runs each step for all of them together (independent
-// chains side by side); lane i < kQkChunk computes head i's 1/sqrt and hands it out by a
-// shuffle.  The sum of squares of each head is the butterfly of warp_sum, so every bit
-// matches.  The q/k loads are issued before the wait for the layer's g_q/g_k.
+// warp takes QC heads at once and runs each step for all of them together (independent
+// chains side by side); lane i < QC computes head i's 1/sqrt and hands it out by a shuffle.
+// The sum of squares of each head is the butterfly of warp_sum, so every bit matches; the
+// products run on fp32 pairs (the scalar kernel's roundings; the first half's y*c - o*s is
+// y*c + o*(-s), the same bits).  The q/k loads are issued before the wait for g_q/g_k.
+// rot (TT == 1): the lane's rotation pairs (cos, then sin negated on the first half).
 template <int TT>
-__device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bool rope, unsigned par) {
+__device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bool rope, unsigned par,
+                                         const f2_t (&rot)[4]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x, G = gridDim.x;
     const int HH = p.Hq + p.Hkv, nh = TT * HH;
     constexpr int QC = TT <= 2 ? kQkChunk : kQkChunk / 2;  // fewer heads at once at larger T
     bool waited = false;
+    f2_t gq[2], gk[2];
     for (int base = warp; base < nh; base += kCW * QC) {
         V4 xv[QC];
         int tt[QC], hq[QC];
@@ -404,19 +430,23 @@ __device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bo
         if (!waited) {
             wait_weights(p, s, kBarQK, par);
             waited = true;
+            const uint2 a = reinterpret_cast<const uint2*>(s.gqk)[lane];
+            const uint2 b = reinterpret_cast<const uint2*>(s.gqk + 128)[lane];
+            gq[0] = bf2_to_f2(a.x);
+            gq[1] = bf2_to_f2(a.y);
+            gk[0] = bf2_to_f2(b.x);
+            gk[1] = bf2_to_f2(b.y);
         }
-        V4 gq, gk;
-        gq.u = reinterpret_cast<const uint2*>(s.gqk)[lane];
-        gk.u = reinterpret_cast<const uint2*>(s.gqk + 128)[lane];
-        float y[QC][4], ss[QC];
+        f2_t y[QC][2];
+        float ss[QC];
 #pragma unroll
         for (int cc = 0; cc < QC; ++cc) {
-            ss[cc] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                y[cc][i] = __bfloat162float(xv[cc].e[i]);
-                ss[cc] = fmaf(y[cc][i], y[cc][i], ss[cc]);
-            }
+            y[cc][0] = bf2_to_f2(xv[cc].u.x);
+            y[cc][1] = bf2_to_f2(xv[cc].u.y);
+            float a0, a1, a2, a3;
+            f2_unpack(y[cc][0], a0, a1);
+            f2_unpack(y[cc][1], a2, a3);
+            ss[cc] = fmaf(a3, a3, fmaf(a2, a2, fmaf(a1, a1, fmaf(a0, a0, 0.0f))));
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
@@ -426,52 +456,44 @@ __device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bo
 #pragma unroll
         for (int cc = 1; cc < QC; ++cc) mine = (lane == cc) ? ss[cc] : mine;
         const float rl = 1.0f / sqrtf(mine / 128.0f + p.eps);
-        float rr[QC];
-#pragma unroll
-        for (int cc = 0; cc < QC; ++cc) rr[cc] = __shfl_sync(FULL_MASK, rl, cc);
 #pragma unroll
         for (int cc = 0; cc < QC; ++cc) {
+            const float r = __shfl_sync(FULL_MASK, rl, cc);
+            const f2_t rr = f2_pack(r, r);
             const bool is_q = hq[cc] < p.Hq;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                y[cc][i] = __fmul_rn(__fmul_rn(y[cc][i], rr[cc]), __bfloat162float(is_q ? gq.e[i] : gk.e[i]));
+            y[cc][0] = f2_mul(f2_mul(y[cc][0], rr), is_q ? gq[0] : gk[0]);
+            y[cc][1] = f2_mul(f2_mul(y[cc][1], rr), is_q ? gq[1] : gk[1]);
         }
-        V4 o[QC];
+        uint2 o[QC];
         if (rope) {
-            const bool first_half = lane < 16;
-            float cs4[QC][4], sn4[QC][4];
 #pragma unroll
             for (int cc = 0; cc < QC; ++cc) {
-                const int t = TT == 1 ? 0 : tt[cc];
-                if (TT == 1 && cc > 0) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) { cs4[cc][i] = cs4[0][i]; sn4[cc][i] = sn4[0][i]; }
+                f2_t cp0, cp1, sp0, sp1;
+                if (TT == 1) {
+                    cp0 = rot[0]; cp1 = rot[1]; sp0 = rot[2]; sp1 = rot[3];
                 } else {
-                    const float4 c4 = reinterpret_cast<const float4*>(s.cs + t * kHalfD)[lane & 15];
-                    const float4 s4 = reinterpret_cast<const float4*>(s.sn + t * kHalfD)[lane & 15];
-                    cs4[cc][0] = c4.x; cs4[cc][1] = c4.y; cs4[cc][2] = c4.z; cs4[cc][3] = c4.w;
-                    sn4[cc][0] = s4.x; sn4[cc][1] = s4.y; sn4[cc][2] = s4.z; sn4[cc][3] = s4.w;
+                    const float4 c4 = reinterpret_cast<const float4*>(s.cs + tt[cc] * kHalfD)[lane & 15];
+                    const float4 s4 = reinterpret_cast<const float4*>(s.sn + tt[cc] * kHalfD)[lane & 15];
+                    const float sg = lane < 16 ? -1.0f : 1.0f;
+                    cp0 = f2_pack(c4.x, c4.y);
+                    cp1 = f2_pack(c4.z, c4.w);
+                    sp0 = f2_pack(sg * s4.x, sg * s4.y);
+                    sp1 = f2_pack(sg * s4.z, sg * s4.w);
                 }
+                float y0, y1, y2, y3;
+                f2_unpack(y[cc][0], y0, y1);
+                f2_unpack(y[cc][1], y2, y3);
+                const f2_t o0 = f2_pack(__shfl_xor_sync(FULL_MASK, y0, 16), __shfl_xor_sync(FULL_MASK, y1, 16));
+                const f2_t o1 = f2_pack(__shfl_xor_sync(FULL_MASK, y2, 16), __shfl_xor_sync(FULL_MASK, y3, 16));
+                o[cc].x = f2_to_bf2(f2_add(f2_mul(y[cc][0], cp0), f2_mul(o0, sp0)));
+                o[cc].y = f2_to_bf2(f2_add(f2_mul(y[cc][1], cp1), f2_mul(o1, sp1)));
             }
-            float other[QC][4];
-#pragma unroll
-            for (int cc = 0; cc < QC; ++cc)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) other[cc][i] = __shfl_xor_sync(FULL_MASK, y[cc][i], 16);
-#pragma unroll
-            for (int cc = 0; cc < QC; ++cc)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float v = first_half
-                        ? __fsub_rn(__fmul_rn(y[cc][i], cs4[cc][i]), __fmul_rn(other[cc][i], sn4[cc][i]))
-                        : __fadd_rn(__fmul_rn(y[cc][i], cs4[cc][i]), __fmul_rn(other[cc][i], sn4[cc][i]));
-                    o[cc].e[i] = __float2bfloat16_rn(v);
-                }
         } else {
 #pragma unroll
-            for (int cc = 0; cc < QC; ++cc)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) o[cc].e[i] = __float2bfloat16_rn(y[cc][i]);
+            for (int cc = 0; cc < QC; ++cc) {
+                o[cc].x = f2_to_bf2(y[cc][0]);
+                o[cc].y = f2_to_bf2(y[cc][1]);
+            }
         }
 #pragma unroll
         for (int cc = 0; cc < QC; ++cc) {
@@ -480,7 +502,7 @@ __device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bo
                 const int t = tt[cc];
                 bf16* dst = hq[cc] < p.Hq ? p.q_out + ((size_t)t * p.Hq + hq[cc]) * 128
                                           : p.k_out + ((size_t)t * p.Hkv + (hq[cc] - p.Hq)) * 128;
-                reinterpret_cast<uint2*>(dst)[lane] = o[cc].u;
+                reinterpret_cast<uint2*>(dst)[lane] = o[cc];
             }
         }
     }
@@ -634,8 +656,9 @@ __device__ void topk_rounds(const Smem& s, int t, int E, int K) {
 
 // D: exact top-K of every token; the same keys and tie rule as the router kernels: score =
 // logit + (bias + 0), ordered by okey (NaN highest), the lower expert first.
-//  1. Thread i keys experts i and i + kCT; each warp's largest key of token t is its group
-//     maximum (warp w's group: experts 32w.. and kCT + 32w..).
+//  1. (In the all-gather, as each record arrives.)  Thread i keys experts i and i + kCT; each
+//     warp's largest key of token t is its group maximum (warp w's group: experts 32w.. and
+//     kCT + 32w..), in wmax[t][w].
 //  2. tau = the K-th largest group maximum: the K groups with the largest maxima each hold a
 //     key >= tau, so every key of the top K is >= tau.  With fewer than K groups, tau = 0
 //     (every key is a candidate).
@@ -645,27 +668,13 @@ __device__ void topk_rounds(const Smem& s, int t, int E, int K) {
 //     More candidates (ties at tau) take the K rounds of topk_rounds.
 // Leaves sel (all tokens) complete for every thread; writes ids and weights (CTA 0).
 template <int TT>
-__device__ __forceinline__ void stage_route(const ChainParams& p, const Smem& s) {
+__device__ __forceinline__ void stage_route(const ChainParams& p, const Smem& s,
+                                            const uint32_t (&key)[TT][2]) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int T = TT;
     const int E = p.E, K = p.K;
     const int ng = min(kCW, (E + 31) >> 5);  // warps holding at least one expert
-    uint32_t key[TT][2];
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int e = tid + j * kCT;
-            key[t][j] = (t < T && e < E) ? okey(s.xrow[t * E_MAX + e] + (s.bias[e] + 0.0f)) : 0u;
-        }
-        const uint32_t m = __reduce_max_sync(FULL_MASK, max(key[t][0], key[t][1]));
-        if (lane == 0) s.wmax[t * 32 + warp] = m;
-    }
-    if (tid < TT) s.ncand[tid] = 0;
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < TT; ++t) {
-        if (t >= T) break;
         const uint32_t mj = lane < ng ? s.wmax[t * 32 + lane] : 0u;
         int above = 0;
 #pragma unroll
@@ -689,12 +698,13 @@ __device__ __forceinline__ void stage_route(const ChainParams& p, const Smem& s)
         }
     }
     __syncthreads();
-    if (warp < T) {
+    if (warp < TT) {
         const int t = warp;
         const int C = s.ncand[t];
         if (C <= 32) {
             const unsigned long long mine = lane < C ? s.cand[t * 32 + lane] : 0ull;
             int rank = 0;
+#pragma unroll 8
             for (int j = 0; j < C; ++j) rank += (s.cand[t * 32 + j] > mine) ? 1 : 0;
             if (lane < C && rank < K) s.sel[t * K + rank] = (int)(0xffffffffu - (unsigned)mine);
         } else {
@@ -724,10 +734,13 @@ __device__ __forceinline__ void stage_maps_expand(const ChainParams& p, const Sm
     const int E = p.E, K = p.K, n = T * K, nvec = p.H / 8;
     for (int e = c + tid * G; e <= E; e += kCT * G) {
         int below = 0, equal = 0;
-        for (int i = 0; i < n; ++i) {
-            const int v = s.sel[i];
-            below += (v < e) ? 1 : 0;
-            equal += (v == e) ? 1 : 0;
+#pragma unroll
+        for (int i = 0; i < kChainMaxK * TT; ++i) {
+            if (i < n) {
+                const int v = s.sel[i];
+                below += (v < e) ? 1 : 0;
+                equal += (v == e) ? 1 : 0;
+            }
         }
         p.offsets[e] = (int64_t)below;
         if (p.counts && e < E) p.counts[e] = equal;
@@ -736,9 +749,12 @@ __device__ __forceinline__ void stage_maps_expand(const ChainParams& p, const Sm
         if (warp == 0) {
             const int e = (lane < n) ? s.sel[lane] : 0x7fffffff;
             int rank = 0;
-            for (int i = 0; i < n; ++i) {
-                const int v = s.sel[i];
-                rank += (v < e || (v == e && i < lane)) ? 1 : 0;
+#pragma unroll
+            for (int i = 0; i < kChainMaxK * TT; ++i) {
+                if (i < n) {
+                    const int v = s.sel[i];
+                    rank += (v < e || (v == e && i < lane)) ? 1 : 0;
+                }
             }
             if (lane < n) {
                 const int tok = lane / K, slot = lane - tok * K;
@@ -850,6 +866,17 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
         for (int k = 0; k < 2; ++k)
             r[t][k].u = rs.ok[k] ? reinterpret_cast<const uint4*>(p.r_in + (size_t)t * H)[rs.v[k]]
                                  : make_uint4(0, 0, 0, 0);
+    f2_t rot[4] = {0ull, 0ull, 0ull, 0ull};  // TT == 1: this lane's rotation pairs
+    if (TT == 1 && p.pos) {
+        const int lane_ = tid & 31;
+        const float4 c4 = reinterpret_cast<const float4*>(s.cs)[lane_ & 15];
+        const float4 s4 = reinterpret_cast<const float4*>(s.sn)[lane_ & 15];
+        const float sg = lane_ < 16 ? -1.0f : 1.0f;
+        rot[0] = f2_pack(c4.x, c4.y);
+        rot[1] = f2_pack(c4.z, c4.w);
+        rot[2] = f2_pack(sg * s4.x, sg * s4.y);
+        rot[3] = f2_pack(sg * s4.z, sg * s4.w);
+    }
     int mine = 0;  // experts owned: c + m*G, m < mine
     for (int m = 0; m < p.nown; ++m)
         if (c + m * G < E) mine = m + 1;
@@ -865,9 +892,14 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
         const bool more = l + 1 < p.L;
 
         // ---- A: Q/K norm + RoPE ----
-        stage_qk<TT>(p, s, !Ly.rnope && p.pos != nullptr, par);
+        stage_qk<TT>(p, s, !Ly.rnope && p.pos != nullptr, par, rot);
         __syncthreads();
-        if (tid == 0 && more && !s.flag[0]) issue_weights(p, s, kBarQK, l + 1);
+        if (s.flag[0]) break;  // uniform: read after the barrier, written before it
+        // Every read of the previous layer's post-MoE gammas is behind the barrier above.
+        if (tid == 0) {
+            if (more) issue_weights(p, s, kBarQK, l + 1);
+            if (l > 0) issue_weights(p, s, kBarB, l);
+        }
 
         // ---- B: sandwich ----
         stage_pair<TT, true>(p, s, rs, p.attn_out, r, kBarA, par, s.ga, s.ga + H, hh, x, p.h, p.moe_in,
@@ -915,21 +947,25 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
                     acc[m * TT + t] = lo + hi;
                 }
         }
-        block_sum_n<kMaxOwn * TT>(acc, red0);
+        // Warp partials of every (expert, token) value; thread m*TT + t then replays the
+        // cross-warp butterfly of its own value only.
+#pragma unroll
+        for (int i = 0; i < kMaxOwn * TT; ++i) {
+            const float wsum = warp_sum(acc[i]);
+            if (lane == 0) red0[i * 33 + warp] = wsum;
+        }
+        __syncthreads();
         unsigned long long* bank = p.rec + (size_t)par * kChainMaxT * E_MAX;
-#pragma unroll
-        for (int m = 0; m < kMaxOwn; ++m)
-#pragma unroll
-            for (int t = 0; t < TT; ++t)
-                if (tid == m * TT + t && m < mine) {
-                    const float v = __bfloat162float(__float2bfloat16_rn(acc[m * TT + t]));
-                    const int e = c + m * G;
-                    st_rec(bank + (size_t)t * E_MAX + e, ((unsigned long long)tag << 32) | __float_as_uint(v));
-                    p.logits[(size_t)t * E + e] = v;
-                    if (p.trace_logits) p.trace_logits[((size_t)l * TT + t) * E + e] = v;
-                }
-        // Every read of ga and of the W rows is behind block_sum_n's barrier; the copies are
-        // issued by the last warp, after the records are out.
+        if (tid < mine * TT) {
+            const int m = tid / TT, t = tid - m * TT;
+            const float v = __bfloat162float(__float2bfloat16_rn(butterfly_of_partials(red0 + tid * 33)));
+            const int e = c + m * G;
+            st_rec(bank + (size_t)t * E_MAX + e, ((unsigned long long)tag << 32) | __float_as_uint(v));
+            p.logits[(size_t)t * E + e] = v;
+            if (p.trace_logits) p.trace_logits[((size_t)l * TT + t) * E + e] = v;
+        }
+        // Every read of ga and of the W rows is behind the barrier above; the copies are issued
+        // by the last warp, after the records are out.
         if (tid == kCT - 32 && more && !s.flag[0]) {
             issue_weights(p, s, kBarA, l + 1);
             issue_weights(p, s, kBarW, l + 1);
@@ -969,11 +1005,25 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
                 }
             }
         }
-        cp_wait_all();  // this thread's part of the bias row
+        // Router step 1 on the gathered logits: keys and the warp maxima (this thread's bias
+        // entries are its own 4-byte copies).
+        cp_wait_all();
+        uint32_t key[TT][2];
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int e = tid + j * kCT;
+                key[t][j] = e < E ? okey(s.xrow[t * E_MAX + e] + (s.bias[e] + 0.0f)) : 0u;
+            }
+            const uint32_t m = __reduce_max_sync(FULL_MASK, max(key[t][0], key[t][1]));
+            if (lane == 0) s.wmax[t * 32 + warp] = m;
+        }
+        if (tid < TT) s.ncand[tid] = 0;
         __syncthreads();
 
         // ---- D: router, maps; E: expansion ----
-        stage_route<TT>(p, s);
+        stage_route<TT>(p, s, key);
         if (more) issue_bias(p, s, l + 1);  // every bias read is behind stage_route's barrier
         stage_maps_expand<TT>(p, s, x, own_perm);
 
@@ -981,10 +1031,9 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
         V8 unused[TT][2];
         stage_pair<TT, false>(p, s, rs, p.moe_out, hh, kBarB, par, s.gb, s.gb + H, r, unused, p.r_out,
                               p.nxt, own, red1, red0);
-        __syncthreads();
-        if (tid == 0 && more && !s.flag[0]) issue_weights(p, s, kBarB, l + 1);
-        if (s.flag[0]) break;  // uniform: read after the barrier, written before it
     }
+    __syncthreads();
+    if (s.flag[0] && l == p.L) l = p.L - 1;  // a wait of the last layer gave up
     if (l < p.L) {  // left early: no copy may still be writing when the CTA exits
         if (tid == 0) {
             // The last phase issued on each buffer (every earlier one completed) is the current
