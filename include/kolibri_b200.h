@@ -57,6 +57,29 @@ enum {
 
 KB_API const char *kb_status_str(int status);
 KB_API int kb_version(void);
+
+/* ---------------------------------------------------------------------------------
+ * Failure detection.  Every wait inside the multi-CTA kernels (grid barriers, bulk-copy
+ * barriers, the decode chain's logit all-gather) is bounded.  A wait that gives up sets its
+ * workspace's error word and the call returns early with invalid outputs; every later call on
+ * that workspace writes offsets[0..E] = -1 and nothing else until the workspace is zero-filled
+ * again (kb_expert_maps_noalloc: flags = KB_NOALLOC_REZERO).
+ * kb_workspace_status reads the error word (it waits for `stream` first):
+ *   kind   KB_WS_MAPS (kb_expert_maps / kb_router_maps workspace), KB_WS_CHAIN
+ *          (kb_decode_chain workspace), KB_WS_NOALLOC (the static scratch of
+ *          kb_expert_maps_noalloc on the current device; workspace is ignored)
+ *   status KB_WS_CLEAN (0), KB_WS_TIMEOUT (1: a bounded wait gave up),
+ *          KB_WS_MISALIGNED (2: kb_decode_chain found a layer weight pointer that is not
+ *          16-byte aligned)
+ * kb_set_wait_limit sets the number of polls after which every later launch's waits give up
+ * (0 restores the defaults, about a second of polling); it returns the previous setting.  A
+ * short limit makes waits give up early on purpose, so that the error path can be exercised.
+ * No counterpart in the reference (its kernels report launch errors only,
+ * kernels/cuda/customKolibriBuildExpertMapsKernel.cu:78-88). */
+enum { KB_WS_MAPS = 0, KB_WS_CHAIN = 1, KB_WS_NOALLOC = 2 };
+enum { KB_WS_CLEAN = 0, KB_WS_TIMEOUT = 1, KB_WS_MISALIGNED = 2 };
+KB_API int kb_workspace_status(const void *workspace, int kind, int *status, kb_stream_t stream);
+KB_API long long kb_set_wait_limit(long long polls);
 /* Programmatic dependent launch on (1, default) or off (0) for every later launch
  * made by this library in this process.  Returns the previous value. */
 KB_API int kb_set_pdl(int enable);

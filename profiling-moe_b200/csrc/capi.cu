@@ -15,7 +15,13 @@ int initial_pdl() {
     return 1;
 }
 std::atomic<int> g_pdl{initial_pdl()};
+std::atomic<long long> g_wait_limit{0};
 }  // namespace
+
+long long wait_limit(long long dflt) {
+    const long long v = g_wait_limit.load(std::memory_order_relaxed);
+    return v > 0 ? v : dflt;
+}
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
@@ -56,4 +62,33 @@ extern "C" int kb_version(void) { return 10000; }  // 1.0.0
 
 extern "C" int kb_set_pdl(int enable) {
     return kb::g_pdl.exchange(enable ? 1 : 0);
+}
+
+extern "C" long long kb_set_wait_limit(long long polls) {
+    return kb::g_wait_limit.exchange(polls > 0 ? polls : 0);
+}
+
+extern "C" int kb_workspace_status(const void* workspace, int kind, int* status,
+                                   kb_stream_t stream) {
+    if (!status) return KB_ERR_INVALID_ARG;
+    const unsigned char* word = nullptr;
+    if (kind == KB_WS_NOALLOC) {
+        void* p = nullptr;
+        const int st = kb::noalloc_scratch_address(&p);
+        if (st) return st;
+        word = static_cast<const unsigned char*>(p) + kb::maps_err_offset();
+    } else if (kind == KB_WS_MAPS || kind == KB_WS_CHAIN) {
+        if (!workspace) return KB_ERR_INVALID_ARG;
+        word = static_cast<const unsigned char*>(workspace) +
+               (kind == KB_WS_MAPS ? kb::maps_err_offset() : kb::chain_err_offset());
+    } else {
+        return KB_ERR_INVALID_ARG;
+    }
+    int v = 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    *status = v;
+    return KB_OK;
 }

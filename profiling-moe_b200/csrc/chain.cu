@@ -104,6 +104,7 @@ struct ChainParams {
     unsigned* done;
     int* err;
     unsigned long long* rec;
+    long long spin;  // poll limit of the bounded waits (kb_set_wait_limit)
 };
 
 // ------------------------------------------------------------------------------------
@@ -306,7 +307,7 @@ __device__ __forceinline__ bool leaving(const ChainParams& p, const Smem& s) {
 __device__ __forceinline__ void wait_weights(const ChainParams& p, const Smem& s, int b, unsigned par) {
     long long it = 0;
     while (!mb_try(s.bar + b, par)) {
-        if (++it > kChainSpin || ((it & 255) == 0 && leaving(p, s))) {
+        if (++it > p.spin || ((it & 255) == 0 && leaving(p, s))) {
             give_up(p, s, kErrTimeout);
             return;
         }
@@ -997,7 +998,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
                             pending &= ~(1u << (j * TT + t));
                         }
                 if (pending) {
-                    if (++it > kChainSpin || ((it & 1023) == 0 && leaving(p, s))) {
+                    if (++it > p.spin || ((it & 1023) == 0 && leaving(p, s))) {
                         give_up(p, s, kErrTimeout);
                         break;
                     }
@@ -1098,6 +1099,10 @@ bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
 }  // namespace
 }  // namespace kb
 
+namespace kb {
+size_t chain_err_offset() { return kWsErr; }
+}  // namespace kb
+
 using namespace kb;
 
 extern "C" size_t kb_decode_chain_workspace_bytes(void) { return kWsBytes; }
@@ -1186,6 +1191,7 @@ extern "C" int kb_decode_chain(const kb_chain_layer_t* layers, int n_layers, con
     prm.done = reinterpret_cast<unsigned*>(wsb + kWsDone);
     prm.err = reinterpret_cast<int*>(wsb + kWsErr);
     prm.rec = reinterpret_cast<unsigned long long*>(wsb + kWsRec);
+    prm.spin = wait_limit(kChainSpin);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     switch (T) {
         case 1: return run_chain<1>(prm, smem, G, st);

@@ -33,6 +33,16 @@ bool pdl_enabled();
 // Host: multiprocessor count of the current device (cached per device; 148 on B200).
 int device_sm_count();
 
+// Host: the poll limit of the kernels' bounded waits (kb_set_wait_limit), or dflt when none
+// was set.
+long long wait_limit(long long dflt);
+
+// Host: byte offsets of the error words in the workspaces, and the device address of the
+// static scratch of kb_expert_maps_noalloc on the current device (resolved on first use).
+size_t maps_err_offset();
+size_t chain_err_offset();
+int noalloc_scratch_address(void** out);
+
 template <typename... KArgs, typename... Args>
 inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                   cudaStream_t stream, Args&&... args) {

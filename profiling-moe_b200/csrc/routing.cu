@@ -527,6 +527,7 @@ struct PersistWs {
     int* err;        // non-zero after a barrier wait gave up; the workspace must be re-zeroed
     int* rowhist;    // [grid][E] per-CTA histograms, CTA-major
     int* gsum;       // [ceil(grid/kGS)][E] histogram sums of kGS-CTA groups; zero between calls
+    long long spin;  // poll limit of the bounded waits (kb_set_wait_limit)
 };
 
 constexpr int kPW = 8;                      // warps per persistent CTA
@@ -549,7 +550,7 @@ __device__ bool grid_barrier(const PersistWs& ws, unsigned target) {
         atomicAdd(ws.bar, 1u);
         unsigned v = ld_acquire_gpu(ws.bar);
         long long it = 0;
-        while (v < target && it < kSpinLimit) {
+        while (v < target && it < ws.spin) {
             __nanosleep(64);
             v = ld_acquire_gpu(ws.bar);
             ++it;
@@ -644,7 +645,7 @@ __device__ bool grid_wait(const PersistWs& ws, unsigned target) {
     if (threadIdx.x == 0) {
         unsigned v = ld_acquire_gpu(ws.bar);
         long long it = 0;
-        while (v < target && it < kSpinLimit) {
+        while (v < target && it < ws.spin) {
             __nanosleep(32);
             v = ld_acquire_gpu(ws.bar);
             ++it;
@@ -657,87 +658,82 @@ __device__ bool grid_wait(const PersistWs& ws, unsigned target) {
     return ok != 0;
 }
 
-// Per-warp counts and ranks in one pass over each warp's chunk range: whist[w][e] (zeroed
-// here) ends as warp w's count of expert e, and lrk[i] is the count of sel[i]'s expert in
-// the warp's earlier chunk groups plus a position among the group's selections of that
-// expert.  A shared-memory atomic hands these out, kCountGroup chunks (32 selections each)
-// at a time, so the selections of one group sharing an expert may come out in any order;
-// fix_order restores selection order.
-constexpr int kCountGroup = 4;
-__device__ void count_rank_warp(const uint16_t* sel, int n, int E, int* whist, uint16_t* lrk) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int* h = whist + warp * E;
-    for (int e = lane; e < E; e += 32) h[e] = 0;
-    __syncwarp();
-    int c0, c1;
-    warp_ranges(n, c0, c1);
-    for (int c = c0; c < c1; c += kCountGroup) {  // every lane runs every group: converged
-#pragma unroll
-        for (int u = 0; u < kCountGroup; ++u) {
-            const int i = (c + u) * 32 + lane;
-            if (c + u < c1 && i < n) {
-                const int e = (int)sel[i];
-                if (e < E) lrk[i] = (uint16_t)atomicAdd(h + e, 1);
-            }
-        }
-        __syncwarp();  // this group's ranks are taken before the next group's
-    }
-}
-
-// CTA-sorted position of every selection of this warp's chunk range: loc[e] (the CTA's
-// offset of expert e) + whist[w][e] (warp w's offset inside it) + lrk[i].
-__device__ void place_sorted(const uint16_t* sel, int n, int E, const int* loc, const int* whist,
-                             const uint16_t* lrk, int* stage_sel) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int* h = whist + warp * E;
-    int c0, c1;
-    warp_ranges(n, c0, c1);
-    for (int i = c0 * 32 + lane; i < min(n, c1 * 32); i += 32) {
-        const int e = (int)sel[i];
-        if (e < E) stage_sel[loc[e] + h[e] + lrk[i]] = i;
-    }
-}
-
-// Odd-even transposition over stage_sel[0..nvalid) (sorted by expert): swaps neighbours of
-// one expert whose selection indices are out of order.  Out-of-order entries only span the
-// selections of one group of count_rank_warp (kCountGroup * 32), so kCountGroup * 16 double
-// rounds sort them; the loop stops at the first round without a swap.  Block-wide (barriers
-// inside).
-__device__ void fix_order(const uint16_t* sel, int nvalid, int* stage_sel) {
-    const int tid = threadIdx.x, nthr = blockDim.x;
-    for (int round = 0; round < kCountGroup * 16 + 1; ++round) {
-        int swapped = 0;
-#pragma unroll 1
-        for (int ph = 0; ph < 2; ++ph) {
-            for (int j = 2 * tid + ph; j + 1 < nvalid; j += 2 * nthr) {
-                const int a = stage_sel[j], b = stage_sel[j + 1];
-                if (a > b && sel[a] == sel[b]) {
-                    stage_sel[j] = b;
-                    stage_sel[j + 1] = a;
-                    swapped = 1;
-                }
-            }
-            __syncthreads();
-        }
-        if (!__syncthreads_or(swapped)) break;
-    }
-}
-
 // Shared-memory ints the tile kernel's map phases need beyond the selections: whist, local
-// offsets, prefix partial sums, and (staged writes) the three rank arrays.
-__host__ __device__ constexpr size_t tile_maps_ints(int nthreads, int E, int n, bool staged) {
+// offsets, prefix partial sums, and (staged writes) the two staging arrays and the token
+// masks and prefixes of the CTA's 32-token tiles.
+__host__ __device__ constexpr size_t tile_maps_ints(int nthreads, int E, int n, int K, bool staged) {
     return (size_t)(nthreads / 32) * E + tile_align_c(E + 1, 4) +
-           (size_t)2 * (nthreads / (E / 4)) * E + (staged ? (size_t)2 * n + (n + 1) / 2 : 0);
+           (size_t)2 * (nthreads / (E / 4)) * E +
+           (staged ? (size_t)2 * n + (size_t)2 * ((n / (K > 0 ? K : 1) + 31) / 32) * E : 0);
+}
+
+// Token masks of the CTA's 32-token tiles: mask[tile][e] bit l is set when token l of the tile
+// selected expert e.  A warp takes tiles w, w + nwarps, ...; per slot k one match.any groups
+// the lanes whose slot-k expert is equal, and the group's lowest lane ORs the group into the
+// mask (one writer per expert per slot; slots in turn).  A token's experts are distinct, so
+// every bit is set once.  mask: [ntiles][E], zero on entry.
+__device__ void build_tile_masks(const uint16_t* sel, int ntok, int K, int E, unsigned* mask) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int ntiles = (ntok + 31) >> 5;
+    for (int tile = warp; tile < ntiles; tile += nw) {
+        const int tok = tile * 32 + lane;
+        unsigned* m = mask + (size_t)tile * E;
+        for (int k = 0; k < K; ++k) {  // uniform trip count over the warp
+            int e = tok < ntok ? (int)sel[tok * K + k] : -1;
+            if (e >= E) e = -1;
+            const unsigned peers = __match_any_sync(FULL_MASK, e);
+            if (e >= 0 && lane == __ffs(peers) - 1) m[e] |= peers;
+            __syncwarp();
+        }
+    }
+}
+
+// Per expert e: tbase[tile][e] = selections of e in the tiles before `tile`; returns the
+// CTA total of e (thread e, e + blockDim, ...).
+__device__ void tile_prefix(const unsigned* mask, int ntiles, int E, unsigned* tbase, int* hist) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        unsigned run = 0;
+        for (int t = 0; t < ntiles; ++t) {
+            const unsigned m = mask[(size_t)t * E + e];
+            tbase[(size_t)t * E + e] = run;
+            run += (unsigned)__popc(m);
+        }
+        hist[e] = (int)run;
+    }
+}
+
+// CTA-sorted position of every selection: loc[e] (the CTA's offset of expert e) + the
+// selections of e in earlier tiles + the tile's earlier tokens that selected e.  The order
+// inside each expert is token order, which is selection order.
+__device__ void place_by_masks(const uint16_t* sel, int ntok, int K, int E, const int* loc,
+                               const unsigned* mask, const unsigned* tbase, int* stage_sel) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int ntiles = (ntok + 31) >> 5;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int tile = warp; tile < ntiles; tile += nw) {
+        const int tok = tile * 32 + lane;
+        if (tok >= ntok) continue;
+        for (int k = 0; k < K; ++k) {
+            const int e = (int)sel[tok * K + k];
+            if (e >= E) continue;
+            const size_t te = (size_t)tile * E + e;
+            stage_sel[loc[e] + (int)tbase[te] + __popc(mask[te] & lt)] = tok * K + k;
+        }
+    }
 }
 
 // Maps phases of the tile kernel (E % 4 == 0, blockDim >= E/4), after the CTA's selections
 // sel[0..n) (16-bit experts, tokens t0..) are in shared memory.  free_sm: the ring, free now.
 // As maps_finish, with:
-//   count + rank   one pass of shared-memory atomics gives the per-warp counts and each
-//                  selection's rank inside its warp (count_rank_warp)
-//   arrive early   the grid barrier is entered right after the CTA histogram is published;
-//                  the CTA-local expert offsets and (staged) the CTA-sorted positions of all
-//                  selections (place_sorted + fix_order) are computed while others arrive
+//   tile masks     (staged) per 32-token tile and expert, the mask of tokens that selected it
+//                  (build_tile_masks: one match.any per slot per tile, no shared-memory
+//                  atomics and no per-selection warp votes, which serialise on this GPU), and
+//                  per expert the counts of the earlier tiles (tile_prefix), which give the
+//                  CTA histogram
+//   arrive early   the CTA histogram is published and the grid barrier entered; the
+//                  CTA-local expert offsets and the CTA-sorted position of every selection
+//                  (place_by_masks: token order inside each expert) are computed while the
+//                  other CTAs arrive
 //   prefix         every thread issues its 128-bit loads of group sums and earlier rows of
 //                  its group before summing; partial sums meet in shared memory
 //   staged writes  p2u in CTA-sorted order (one run of consecutive rows per expert) and u2p
@@ -760,29 +756,36 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     int* part_t = part_b + R * E;
     int* stage_sel = part_t + R * E;
     int* stage_r = stage_sel + n;
-    uint16_t* lrk = reinterpret_cast<uint16_t*>(stage_r + n);
-
+    // Tile masks (staged path): [ntiles][E] masks and tile prefixes after the staging arrays.
+    const int ntok = n / K, ntiles = (ntok + 31) >> 5;
+    unsigned* tmask = reinterpret_cast<unsigned*>(stage_r + n);
+    unsigned* tbase = tmask + (size_t)ntiles * E;
     __syncthreads();  // selections complete; the ring is free
-    if (staged)
-        count_rank_warp(sel, n, E, whist, lrk);
-    else
+    if (staged) {
+        for (int i = tid; i < ntiles * E; i += nthr) tmask[i] = 0u;
+        __syncthreads();
+        build_tile_masks(sel, ntok, K, E, tmask);
+        __syncthreads();
+        tile_prefix(tmask, ntiles, E, tbase, hist);  // hist = CTA histogram
+    } else {
         count_per_warp(sel, n, E, whist);
-    __syncthreads();
-    scan_over_warps(E, whist, hist);  // hist = CTA histogram, whist exclusive over warps
+        __syncthreads();
+        scan_over_warps(E, whist, hist);  // hist = CTA histogram, whist exclusive over warps
+    }
+    // Atomics reach L2 at once, so the release of grid_arrive does not wait behind stores
+    // that are still buffered.
     for (int e = tid; e < E; e += nthr) {
         const int v = hist[e];
-        __stcg(ws.rowhist + (size_t)c * E + e, v);
+        atomicExch(ws.rowhist + (size_t)c * E + e, v);
         if (v) atomicAdd(ws.gsum + (size_t)g * E + e, v);
     }
     grid_arrive(ws);
-    // While the other CTAs arrive: CTA-local expert offsets and CTA-sorted positions.
+    // While the other CTAs arrive: CTA-local expert offsets, CTA-sorted positions.
     scan_experts(hist, E, loc, scratch);  // barriers inside
     __syncthreads();
     const int nvalid = loc[E];
     if (staged) {
-        place_sorted(sel, n, E, loc, whist, lrk, stage_sel);
-        __syncthreads();
-        fix_order(sel, nvalid, stage_sel);
+        place_by_masks(sel, ntok, K, E, loc, tmask, tbase, stage_sel);
     } else {
         for (int e = tid; e < E; e += nthr) {
             const int l = loc[e];
@@ -1007,8 +1010,28 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // Waits for the phase of parity `parity` to complete; false (and the error word set) if it
-// did not within kMbarSpin polls, or as soon as another wait gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* err) {
+// did not within `limit` polls (kMbarSpin when limit <= 0), or as soon as another wait gave
+// up.  err may be null (the router-only launches have no workspace): nothing is read or set.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* err,
+                                          long long limit = kMbarSpin) {
+    const unsigned a = smem_u32(bar);
+    if (limit <= 0) limit = kMbarSpin;
+    for (long long it = 0; it < limit; ++it) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+        if ((it & 255) == 255 && err && *(volatile int*)err) return false;
+        __nanosleep(40);  // a waiting warp leaves the issue slots to the working ones
+    }
+    if (err) atomicExch(err, 1);
+    return false;
+}
+// The drain after a wait gave up: waits for a copy this CTA issued to land whatever the error
+// word says (a CTA must not leave with a copy still writing its shared memory); bounded.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, unsigned parity) {
     const unsigned a = smem_u32(bar);
     for (long long it = 0; it < kMbarSpin; ++it) {
         unsigned done;
@@ -1016,12 +1039,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* e
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
             " selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done) : "r"(a), "r"(parity) : "memory");
-        if (done) return true;
-        if ((it & 255) == 255 && *(volatile int*)err) return false;
-        __nanosleep(40);  // a waiting warp leaves the issue slots to the working ones
+        if (done) return;
+        __nanosleep(40);
     }
-    atomicExch(err, 1);
-    return false;
 }
 // One bulk copy global -> this CTA's own shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
@@ -1099,7 +1119,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) maps_tma_kernel(
         int issued = 0;
         for (int bi = 0; bi < nbat && ok; ++bi) {
             const int st = bi % kTmaStages, k = bi / kTmaStages;
-            if (lane == 0 && k > 0) ok = mbar_wait(empty + st, (unsigned)((k - 1) & 1), ws.err);
+            if (lane == 0 && k > 0) ok = mbar_wait(empty + st, (unsigned)((k - 1) & 1), ws.err, ws.spin);
             ok = __shfl_sync(FULL_MASK, ok, 0);
             if (!ok) break;
             const int64_t tb = t0 + (int64_t)bi * kTmaRows;
@@ -1111,9 +1131,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) maps_tma_kernel(
             }
             issued = bi + 1;
         }
-        if (!ok && lane == 0) {  // drain: no bulk copy may still be writing when the CTA moves on
+        // Drain: no bulk copy may still be writing when the CTA moves on, also when a consumer
+        // gave up on a tile (the last phase of each slot is complete or current, so its
+        // parity waits only for a copy still in flight).
+        if (lane == 0) {
             for (int bi = max(0, issued - kTmaStages); bi < issued; ++bi)
-                mbar_wait(full + bi % kTmaStages, (unsigned)((bi / kTmaStages) & 1), ws.err);
+                mbar_drain(full + bi % kTmaStages, (unsigned)((bi / kTmaStages) & 1));
         }
         __syncwarp();
     } else {
@@ -1131,7 +1154,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) maps_tma_kernel(
             // the decision reaches the others through the group barrier, so every warp of the
             // group takes the same branch and no named barrier can miss a participant.
             if (gw == 0) {
-                const bool ok = mbar_wait(full + st, (unsigned)(k & 1), ws.err);
+                const bool ok = mbar_wait(full + st, (unsigned)(k & 1), ws.err, ws.spin);
                 if (lane == 0) group_ok[cw] = ok ? 1 : 0;
             }
             group_sync<kTmaGroup>(cw);
@@ -1240,7 +1263,8 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 __device__ __forceinline__ void pair_sync(int p) {
     asm volatile("bar.sync %0, 64;" ::"r"(1 + p) : "memory");
 }
-static_assert(kTileMaxSlots < 16, "named barriers 1..kTileMaxSlots must exist");
+static_assert(kTileMaxSlots < 15, "named barriers 1..kTileMaxSlots must exist");
+constexpr int kTileSetupBar = 15;  // the tile kernel's set-up barrier (the pairs use 1..nslot)
 
 // Insert (kk, jj) into a top-KM list sorted by key descending; candidates arrive in ascending
 // index order, so a strict comparison keeps the earlier (lower) index first among equal keys.
@@ -1316,14 +1340,25 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
     const int64_t t1 = min(T, t0 + tpc);
     const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
     const int nbat = (t1 > t0) ? (int)((t1 - t0 + kTileRows - 1) / kTileRows) : 0;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < nslot; ++st) {
-            mbar_init(full + st, 1);
-            mbar_init(empty + st, 2);
+    // Set-up: the producer warp initialises the mbarriers and only arrives on the set-up
+    // barrier (named barrier kTileSetupBar), so its first copies are issued while the other
+    // warps zero the CTA histogram and load the bias; they wait on the barrier, which also
+    // publishes the mbarriers' initialisation to them.
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int st = 0; st < nslot; ++st) {
+                mbar_init(full + st, 1);
+                mbar_init(empty + st, 2);
+            }
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        __syncwarp();
+        asm volatile("bar.arrive %0, %1;" ::"r"(kTileSetupBar), "r"((int)blockDim.x) : "memory");
+    } else {
+        const int nt = blockDim.x - 32, t = threadIdx.x - 32;
+        for (int e = t; e < E_; e += nt) bias_sm[e] = bias ? __ldg(bias + e) + 0.0f : 0.0f;
+        asm volatile("bar.sync %0, %1;" ::"r"(kTileSetupBar), "r"((int)blockDim.x) : "memory");
     }
-    troute_setup<E_>(bias, bias_sm);  // includes the barrier that publishes the mbarriers
 
     if (warp == 0) {
         // Producer: every tile of this CTA in order; lane 0 waits for the slot, posts the
@@ -1333,7 +1368,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
         int issued = 0;
         for (int bi = 0; bi < nbat && ok; ++bi) {
             const int st = bi % nslot, k = bi / nslot;
-            if (lane == 0 && k > 0) ok = mbar_wait(empty + st, (unsigned)((k - 1) & 1), ws.err);
+            if (lane == 0 && k > 0) ok = mbar_wait(empty + st, (unsigned)((k - 1) & 1), ws.err, ws.spin);
             ok = __shfl_sync(FULL_MASK, ok, 0);
             if (!ok) break;
             const int y = (int)(t0 + (int64_t)bi * kTileRows);
@@ -1346,9 +1381,12 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
             }
             issued = bi + 1;
         }
-        if (!ok && lane == 0) {  // drain: no copy may still be writing when the CTA moves on
+        // Drain: no copy may still be writing when the CTA moves on, also when a consumer gave
+        // up on a tile (the last phase of each slot is complete or current, so its parity
+        // waits only for a copy still in flight).
+        if (lane == 0) {
             for (int bi = max(0, issued - nslot); bi < issued; ++bi)
-                mbar_wait(full + bi % nslot, (unsigned)((bi / nslot) & 1), ws.err);
+                mbar_drain(full + bi % nslot, (unsigned)((bi / nslot) & 1));
         }
         __syncwarp();
     } else if (warp <= 2 * nslot) {
@@ -1366,7 +1404,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
             // The pair's first warp decides whether the tile arrived (bounded wait); the
             // decision reaches the second through the pair barrier, so both take one branch.
             if (h == 0) {
-                const bool ok = mbar_wait(full + p, par, ws.err);
+                const bool ok = mbar_wait(full + p, par, ws.err, ws.spin);
                 if (lane == 0) pair_ok[p] = ok ? 1 : 0;
             }
             pair_sync(p);
@@ -1565,7 +1603,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
     }
     if constexpr (MAPS) {
         const bool staged =
-            tile_maps_ints(blockDim.x, E_, n, true) <= (size_t)nslot * C::SLOT_FLOATS;
+            tile_maps_ints(blockDim.x, E_, n, K, true) <= (size_t)nslot * C::SLOT_FLOATS;
         maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, whist, staged,
                              counts, offsets, p2u, u2p);
     }
@@ -1816,6 +1854,7 @@ PersistWs carve_persist(void* ws, int grid, int E) {
     w.err = reinterpret_cast<int*>(b + sizeof(int));
     w.gsum = reinterpret_cast<int*>(b + kGsumOff);
     w.rowhist = reinterpret_cast<int*>(b + kScratchOff);
+    w.spin = wait_limit(kSpinLimit);
     return w;
 }
 
@@ -2434,10 +2473,12 @@ int tile_router(const float* logits, const float* bias, int32_t* ids, WT* w, int
         auto* kern = (K == 6) ? maps_tile_kernel<E_, 6, false, WT> : maps_tile_kernel<E_, 0, false, WT>;
         int err = allow_smem(kern, p.smem_persist);
         if (err) return err;
+        PersistWs nows{};  // no workspace: no error word, only the wait limit
+        nows.spin = wait_limit(kMbarSpin);
         return launch(kern, dim3(p.grid), dim3(32 * (1 + 2 * p.tnw)), p.smem_persist, st, p.tmap,
                       logits, bias, ids, w, T, K, renorm, p.tpc, p.tnw,
                       static_cast<int32_t*>(nullptr), static_cast<int64_t*>(nullptr),
-                      static_cast<int32_t*>(nullptr), static_cast<int32_t*>(nullptr), PersistWs{});
+                      static_cast<int32_t*>(nullptr), static_cast<int32_t*>(nullptr), nows);
     }
 }
 template <typename WT>
@@ -2594,7 +2635,16 @@ int noalloc_scratch(cudaStream_t st, int flags, void** out) {
     return KB_OK;
 }
 
+
 }  // namespace
+
+size_t maps_err_offset() { return sizeof(unsigned); }
+
+// The scratch address of the current device for kb_workspace_status (no zero fill: a scratch
+// that no call has used yet holds zeros).
+int noalloc_scratch_address(void** out) {
+    return static_cast<int>(cudaGetSymbolAddress(out, g_noalloc_scratch));
+}
 }  // namespace kb
 
 extern "C" int kb_expert_maps_noalloc(const int32_t* ids, int32_t* counts, int64_t* offsets,

@@ -19,6 +19,8 @@ KB_ERR_WORKSPACE = -4
 KB_ERR_TOO_LARGE = -5
 KB_ERR_SCRATCH_LIMIT = -6
 KB_NOALLOC_REZERO = 1
+KB_WS_MAPS, KB_WS_CHAIN, KB_WS_NOALLOC = 0, 1, 2
+KB_WS_CLEAN, KB_WS_TIMEOUT, KB_WS_MISALIGNED = 0, 1, 2
 
 KB_BF16, KB_F16, KB_F32 = 0, 1, 2
 KB_MAPS_AUTO, KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA, KB_MAPS_TWO_KERNEL = 0, 1, 2, 3
@@ -28,6 +30,8 @@ SIGNATURES = {
     "kb_status_str": (c_char_p, [c_int]),
     "kb_version": (c_int, []),
     "kb_set_pdl": (c_int, [c_int]),
+    "kb_workspace_status": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "kb_set_wait_limit": (c_int64, [c_int64]),
     "kb_router": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                           c_int, c_void_p]),
     "kb_expert_maps_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),

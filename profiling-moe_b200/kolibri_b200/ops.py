@@ -17,6 +17,7 @@ from ._lib import (KB_BF16, KB_F16, KB_F32, KB_MAPS_AUTO, KB_MAPS_MULTI_CTA, KB_
 __all__ = [
     "router", "expert_maps", "router_maps", "expand_rows", "qk_norm_rope", "rope_inv_freq",
     "residual_norm_pair", "add_rms_norm", "reserve_workspace", "set_pdl", "expert_maps_noalloc",
+    "set_wait_limit", "workspace_status",
     "moe_finalize",
     "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA", "KB_MAPS_TWO_KERNEL",
 ]
@@ -45,6 +46,26 @@ def _contig(t: torch.Tensor, name: str) -> None:
 def set_pdl(enable: bool) -> bool:
     """Turn programmatic dependent launch on or off for later launches; returns the old value."""
     return bool(load().kb_set_pdl(int(bool(enable))))
+
+
+def set_wait_limit(polls: int) -> int:
+    """Poll limit of the kernels' bounded waits for later launches (0 = the defaults);
+    returns the previous setting."""
+    return int(load().kb_set_wait_limit(int(polls)))
+
+
+def workspace_status(workspace: Optional[torch.Tensor], kind: int = 0,
+                     device: Optional[torch.device] = None) -> int:
+    """The error word of a workspace (kind 0: maps / router+maps, 1: decode chain, 2: the
+    static scratch of expert_maps_noalloc on `device`): 0 clean, 1 a bounded wait gave up,
+    2 misaligned decode-chain weights.  Waits for the current stream."""
+    import ctypes
+    dev = workspace.device if workspace is not None else (device or torch.device("cuda"))
+    out = ctypes.c_int(-1)
+    with torch.cuda.device(dev):
+        check(load().kb_workspace_status(_p(workspace), int(kind), ctypes.byref(out),
+                                         _stream(dev)), "kb_workspace_status")
+    return out.value
 
 
 # ----------------------------------------------------------------------------------------
