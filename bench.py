@@ -476,7 +476,8 @@ def main():
                                     ctypes.byref(launch_c), ctypes.byref(grid_c)),
                "kb_maps_describe")
     launches_per_step = launch_c.value
-    path_name = {1: "single-CTA", 2: "persistent multi-CTA", 3: "two-kernel"}[path_c.value]
+    path_name = {1: "single-CTA", 2: "persistent multi-CTA", 3: "two-kernel",
+                 4: "hybrid-router persistent", 5: "warp-router persistent"}[path_c.value]
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):

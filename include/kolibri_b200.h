@@ -52,7 +52,11 @@ enum {
     KB_MAPS_AUTO = 0,        /* single CTA at small T, persistent multi-CTA kernel above   */
     KB_MAPS_SINGLE_CTA = 1,  /* one CTA, everything in shared memory (T*K <= 12288)         */
     KB_MAPS_MULTI_CTA = 2,   /* persistent cooperative kernel (two-kernel path if it cannot hold T) */
-    KB_MAPS_TWO_KERNEL = 3   /* tile histograms + per-super-tile scatter, two launches      */
+    KB_MAPS_TWO_KERNEL = 3,  /* tile histograms + per-super-tile scatter, two launches      */
+    /* Forced multi-CTA routing paths of kb_router_maps (kb_expert_maps treats them as
+     * KB_MAPS_MULTI_CTA): the fallbacks AUTO takes when the tile kernel does not apply. */
+    KB_MAPS_HYBRID_ROUTER = 4,  /* lane-per-token hybrid router kernel (E in {128..512})    */
+    KB_MAPS_WARP_ROUTER = 5     /* warp-per-token router kernel (any E <= 512, K <= 32)       */
 };
 
 KB_API const char *kb_status_str(int status);
@@ -132,7 +136,9 @@ KB_API int kb_router_maps(const float *logits, const float *bias, int32_t *ids, 
                    int renorm, int mode, kb_stream_t stream);
 
 /* The path kb_expert_maps (route = 0) or kb_router_maps (route = 1) takes for this shape:
- * *path = KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA (persistent kernel) or KB_MAPS_TWO_KERNEL,
+ * *path = KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA (persistent kernel; with route = 1 the tile
+ * kernel), KB_MAPS_HYBRID_ROUTER / KB_MAPS_WARP_ROUTER (route = 1: those router kernels) or
+ * KB_MAPS_TWO_KERNEL,
  * *launches = kernel launches per call, *grid = CTAs of the (first) launch.  Any output
  * pointer may be NULL.  Library introspection; no counterpart in the reference. */
 KB_API int kb_maps_describe(int64_t T, int E, int K, int route, int mode, int *path,

@@ -978,22 +978,8 @@ __global__ void __launch_bounds__(256) maps_tpersist_kernel(
 }
 
 // ------------------------------------------------------------------------------------
-// Warp-specialised TMA maps kernel (routing, E = 32*VPL <= 384, K <= 8): one CTA per SM.
-// Warp 0 streams the CTA's tokens in batches of kTmaRows rows, one bulk copy per batch
-// (cp.async.bulk, completion on an mbarrier per slot), through a kTmaStages-deep ring; consumer group c
-// (kTmaGroup warps) owns slot c and routes batches c, c + kTmaStages, ... from shared memory
-// (troute_stage1_sm and troute_stage2_sm, both split over the group's warps), releasing the
-// slot after each.  Then the maps phases of maps_finish.  Every mbarrier wait is bounded; a wait
-// that gives up sets the workspace error word.
-// smem: ring[S][R][E] | gm[S][R][G+1] | bias[E] | sel_tmp[nw][32] | sel[tpc*K] | hist[E]
-//       | totsm[E] | offs[E+1] | scratch[64] | full[S], empty[S] (u64); whist aliases ring.
+// mbarrier helpers of the tile kernel (bounded waits).
 // ------------------------------------------------------------------------------------
-constexpr int kTmaStages = 16;
-constexpr int kTmaRows = 8;
-constexpr int kTmaGroup = 1;  // consumer warps per ring slot
-template <int E_>
-constexpr int tma_row_stride() { return E_; }  // rows back to back: one bulk copy per batch
-constexpr int kTmaThreads = 32 * (1 + kTmaStages * kTmaGroup);  // producer + consumer groups
 constexpr long long kMbarSpin = 1LL << 20;
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
@@ -1043,146 +1029,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, unsigned parity) {
         __nanosleep(40);
     }
 }
-// One bulk copy global -> this CTA's own shared memory, completing on `bar`.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-
-// Barrier over the G warps of consumer group cw (named barrier 1 + cw; a warp alone needs
-// only __syncwarp).
-template <int G>
-__device__ __forceinline__ void group_sync(int cw) {
-    if constexpr (G == 1) {
-        __syncwarp();
-    } else {
-        asm volatile("bar.sync %0, %1;" ::"r"(1 + cw), "r"(32 * G) : "memory");
-    }
-}
-static_assert(kTmaGroup == 1 || kTmaStages < 16, "named barriers 1..kTmaStages must exist");
-
-template <int E_>
-__host__ __device__ constexpr size_t tma_ring_floats() {
-    return (size_t)kTmaStages * kTmaRows * tma_row_stride<E_>();
-}
-template <int E_>
-__host__ __device__ constexpr size_t tma_gm_floats() {
-    return (size_t)kTmaStages * kTmaRows * (E_ / 16 + 1);
-}
-
-template <int E_, int KT>
-__global__ void __launch_bounds__(kTmaThreads, 1) maps_tma_kernel(
-    const float* __restrict__ logits, const float* __restrict__ bias, int32_t* __restrict__ ids_out,
-    float* __restrict__ w, int64_t T, int K, int renorm, int tpc, int32_t* __restrict__ counts,
-    int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p,
-    PersistWs ws) {
-    pdl_wait();
-    extern __shared__ __align__(128) float qsm[];
-    constexpr int GP = E_ / 16 + 1;
-    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* ring = qsm;
-    float* gm = ring + tma_ring_floats<E_>();
-    float* bias_sm = gm + tma_gm_floats<E_>();
-    int* sel_tmp = reinterpret_cast<int*>(bias_sm + E_);
-    int* sel = sel_tmp + nw * 32;
-    const int selcap = (tpc * K + 3) & ~3;
-    int* hist = sel + selcap;
-    int* totsm = hist + E_;
-    int* offs = totsm + E_;
-    int* scratch = offs + ((E_ + 1 + 3) & ~3);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(scratch + 64);  // 8-byte aligned: even ints
-    uint64_t* full = bars;
-    uint64_t* empty = bars + kTmaStages;
-    int* whist = reinterpret_cast<int*>(ring);
-    if (ws_poisoned(ws, E_, offsets)) return;
-    const int c = blockIdx.x;
-    const int64_t t0 = (int64_t)c * tpc;
-    const int64_t t1 = min(T, t0 + tpc);
-    const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
-    const int nbat = (t1 > t0) ? (int)((t1 - t0 + kTmaRows - 1) / kTmaRows) : 0;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < kTmaStages; ++st) {
-            mbar_init(full + st, 1);
-            mbar_init(empty + st, kTmaGroup);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    troute_setup<E_>(bias, bias_sm);  // includes the barrier that publishes the mbarriers
-
-    if (warp == 0) {
-        // Producer warp: every batch of this CTA in order, one bulk copy per batch (issuing is
-        // the producer's cost, so a batch is one copy); lane 0 waits for the slot, posts the
-        // byte count and issues the copy.
-        constexpr int RS = tma_row_stride<E_>();
-        bool ok = true;
-        int issued = 0;
-        for (int bi = 0; bi < nbat && ok; ++bi) {
-            const int st = bi % kTmaStages, k = bi / kTmaStages;
-            if (lane == 0 && k > 0) ok = mbar_wait(empty + st, (unsigned)((k - 1) & 1), ws.err, ws.spin);
-            ok = __shfl_sync(FULL_MASK, ok, 0);
-            if (!ok) break;
-            const int64_t tb = t0 + (int64_t)bi * kTmaRows;
-            const int rows = (int)min((int64_t)kTmaRows, t1 - tb);
-            if (lane == 0) {
-                const unsigned bytes = (unsigned)(rows * E_ * sizeof(float));
-                mbar_expect_tx(full + st, bytes);
-                bulk_g2s(ring + (size_t)st * kTmaRows * RS, logits + tb * E_, bytes, full + st);
-            }
-            issued = bi + 1;
-        }
-        // Drain: no bulk copy may still be writing when the CTA moves on, also when a consumer
-        // gave up on a tile (the last phase of each slot is complete or current, so its
-        // parity waits only for a copy still in flight).
-        if (lane == 0) {
-            for (int bi = max(0, issued - kTmaStages); bi < issued; ++bi)
-                mbar_drain(full + bi % kTmaStages, (unsigned)((bi / kTmaStages) & 1));
-        }
-        __syncwarp();
-    } else {
-        // Consumer group cw (kTmaGroup warps) owns ring slot cw and takes its batches in order,
-        // so that none of its warps is ever more than one phase ahead of the slot's barriers.
-        // Stage 1 and stage 2 are both split over the group's warps; every warp releases the
-        // slot after its stage 2.
-        const int cw = (warp - 1) / kTmaGroup, gw = (warp - 1) % kTmaGroup;
-        float b[E_ / 32];
-        load_bias<E_ / 32, true>(bias, E_, lane, b);
-        __shared__ int group_ok[kTmaStages];
-        for (int bi = cw; bi < nbat; bi += kTmaStages) {
-            const int st = bi % kTmaStages, k = bi / kTmaStages;
-            // The group's first warp alone decides whether the batch arrived (bounded wait);
-            // the decision reaches the others through the group barrier, so every warp of the
-            // group takes the same branch and no named barrier can miss a participant.
-            if (gw == 0) {
-                const bool ok = mbar_wait(full + st, (unsigned)(k & 1), ws.err, ws.spin);
-                if (lane == 0) group_ok[cw] = ok ? 1 : 0;
-            }
-            group_sync<kTmaGroup>(cw);
-            if (!group_ok[cw]) break;
-            if (gw != 0) mbar_wait(full + st, (unsigned)(k & 1), ws.err);  // completed: returns at once
-            const int64_t tb = t0 + (int64_t)bi * kTmaRows;
-            const int rows = (int)min((int64_t)kTmaRows, t1 - tb);
-            constexpr int RS = tma_row_stride<E_>();
-            const float* slot = ring + (size_t)st * kTmaRows * RS;
-            float* gms = gm + (size_t)st * kTmaRows * GP;
-            troute_stage1_sm<E_, RS>(slot, rows, gw, kTmaGroup, b, gms);
-            group_sync<kTmaGroup>(cw);
-            // Stage 2: warp gw ranks tokens [gw*R, gw*R + R) of the batch, R = kTmaRows/kTmaGroup,
-            // re-reading their qualifying groups from the slot; then the slot is released.
-            constexpr int R = kTmaRows / kTmaGroup;
-            const int mine = min(R, rows - gw * R);
-            if (mine > 0)
-                troute_stage2_sm<E_, RS, KT, float>(slot + (size_t)gw * R * RS, mine, tb + gw * R,
-                                                    logits, bias_sm, K, renorm,
-                                                    gms + (size_t)gw * R * GP, sel_tmp + warp * 32,
-                                                    ids_out, w, sel, t0);
-            if (lane == 0) mbar_arrive(empty + st);  // every warp of the group: count kTmaGroup
-        }
-    }
-    maps_finish(ws, T, E_, K, t0, n, sel, hist, totsm, offs, scratch, whist, counts, offsets, p2u,
-                u2p);
-}
-
 // ------------------------------------------------------------------------------------
 // Tile maps kernel (routing, E = 32*VPL in {128, 256, 384}, K <= 8): one CTA per SM.
 //
@@ -1783,7 +1629,7 @@ DevInfo dev_info() {
     return d;
 }
 
-enum class Path { Single, Persistent, TPersistent, Tma, Tile, TwoKernel };
+enum class Path { Single, Persistent, TPersistent, Tile, TwoKernel };
 
 struct MapsPlan {
     Path path;
@@ -2117,66 +1963,6 @@ struct MapsLaunchT {
             }
         }
 
-        // Warp-specialised TMA kernel (routing, E = 32*VPL in {128, 256, 384}, K <= 8): one CTA
-        // per SM, when the ring, the selections and the map buffers fit in shared memory.
-        static size_t tma_smem(int tpc, int K) {
-            constexpr int E_ = 32 * VPL;
-            const size_t ints = (size_t)(kTmaThreads / 32) * 32 + (((size_t)tpc * K + 3) & ~size_t(3)) +
-                                2 * (size_t)E_ + ((E_ + 1 + 3) & ~3) + 64;
-            return (tma_ring_floats<E_>() + tma_gm_floats<E_>() + E_) * sizeof(float) +
-                   ints * sizeof(int) + 2 * kTmaStages * sizeof(uint64_t);
-        }
-        static bool plan_tma(MapsPlan& p, int64_t T, int E, int K) {
-            if constexpr (!(ROUTE && VEC)) {
-                return false;
-            } else {
-                constexpr int E_ = 32 * VPL;
-                if (E_ > 384 || E != E_ || K > 8) return false;
-                const int sms = dev_info().sms;
-                int grid = (int)std::min<int64_t>(std::min(kMaxPersistGrid, sms),
-                                                  (T + kTmaRows - 1) / kTmaRows);
-                grid = std::max(grid, 1);
-                const int64_t tpc = (T + grid - 1) / grid;
-                if (tpc * K > kMaxPersistSel) return false;
-                const size_t smem = tma_smem((int)tpc, K);
-                if (smem > kMaxSmem) return false;
-                if (tma_blocks_per_sm(K, smem) < 1) return false;
-                p.grid = (int)((T + tpc - 1) / tpc);
-                p.tpc = (int)tpc;
-                p.smem_persist = smem;
-                return true;
-            }
-        }
-        static int tma_blocks_per_sm(int K, size_t smem) {
-            if constexpr (!(ROUTE && VEC)) {
-                return 0;
-            } else {
-                constexpr int E_ = 32 * VPL;
-                static std::mutex mu;
-                static std::map<std::tuple<int, int, size_t>, int> cache;
-                int dev = 0;
-                cudaGetDevice(&dev);
-                std::lock_guard<std::mutex> lk(mu);
-                int& v = cache[std::make_tuple(dev, K == 6 ? 6 : 0, smem)];
-                if (v == 0) {
-                    int occ = 0;
-                    if constexpr (E_ <= 384) {
-                        if (K == 6) {
-                            auto* kern = maps_tma_kernel<E_, 6>;
-                            allow_smem(kern, smem);
-                            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTmaThreads, smem) != cudaSuccess) occ = 0;
-                        } else {
-                            auto* kern = maps_tma_kernel<E_, 0>;
-                            allow_smem(kern, smem);
-                            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTmaThreads, smem) != cudaSuccess) occ = 0;
-                        }
-                    }
-                    v = occ > 0 ? occ : -1;
-                }
-                return v;
-            }
-        }
-
         // Co-resident CTAs per SM of the transposed persistent kernel.
         static int tblocks_per_sm(int K, size_t smem) {
             if constexpr (!(ROUTE && VEC)) {
@@ -2272,16 +2058,18 @@ struct MapsLaunchT {
                 return p;
             }
             plan_two_kernel(p, T, E, K, ROUTE, VEC);
-            if (mode != KB_MAPS_TWO_KERNEL && allow_tile && plan_tile(p, T, E, K)) {
+            // Forced routing paths: KB_MAPS_HYBRID_ROUTER skips the tile kernel,
+            // KB_MAPS_WARP_ROUTER skips both the tile and the hybrid-router kernels.
+            const bool multi = mode != KB_MAPS_TWO_KERNEL;
+            const bool tile_ok = multi && mode != KB_MAPS_HYBRID_ROUTER && mode != KB_MAPS_WARP_ROUTER;
+            const bool hybrid_ok = multi && mode != KB_MAPS_WARP_ROUTER;
+            if (tile_ok && allow_tile && plan_tile(p, T, E, K)) {
                 p.path = Path::Tile;
                 p.ws_bytes = persist_ws_bytes(p.grid, E);
-            } else if (mode != KB_MAPS_TWO_KERNEL && plan_tma(p, T, E, K)) {
-                p.path = Path::Tma;
-                p.ws_bytes = persist_ws_bytes(p.grid, E);
-            } else if (mode != KB_MAPS_TWO_KERNEL && plan_tpersist(p, T, E, K)) {
+            } else if (hybrid_ok && plan_tpersist(p, T, E, K)) {
                 p.path = Path::TPersistent;
                 p.ws_bytes = persist_ws_bytes(p.grid, E);
-            } else if (mode != KB_MAPS_TWO_KERNEL && plan_persist(p, T, E, K)) {
+            } else if (multi && plan_persist(p, T, E, K)) {
                 p.path = Path::Persistent;
                 p.ws_bytes = persist_ws_bytes(p.grid, E);
             } else {
@@ -2314,17 +2102,6 @@ struct MapsLaunchT {
                                        renorm, p.tpc, p.tnw, counts, offsets, p2u, u2p,
                                        carve_persist(ws, p.grid, E));
                 }
-                if (p.path == Path::Tma) {
-                    constexpr int E_ = 32 * VPL;
-                    auto* kern = maps_tma_kernel<E_, (KT == 6 ? 6 : 0)>;
-                    int err = allow_smem(kern, p.smem_persist);
-                    if (err) return err;
-                    return launch_coop(kern, dim3(p.grid), dim3(kTmaThreads), p.smem_persist, st,
-                                       logits, bias, ids_out, w, T, K, renorm, p.tpc, counts,
-                                       offsets, p2u, u2p, carve_persist(ws, p.grid, E));
-                }
-            }
-            if constexpr (ROUTE && VEC) {
                 if (p.path == Path::TPersistent) {
                     constexpr int E_ = 32 * VPL;
                     auto* kern = maps_tpersist_kernel<E_, (KT == 6 ? 6 : 0)>;
@@ -2377,7 +2154,7 @@ struct MapsLaunchT {
             if (VEC && ROUTE && K == 6)
                 return run_kt<6>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
                                  ws, T, E, K, renorm, st);
-            if (p.path == Path::TPersistent || p.path == Path::Tma ||
+            if (p.path == Path::TPersistent ||
                 p.path == Path::Tile)  // runtime-K (K <= 8)
                 return run_kt<0>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
                                  ws, T, E, K, renorm, st);
@@ -2394,8 +2171,6 @@ struct MapsLaunchT {
             if (plan_persist(q, T, E, K)) b = std::max(b, persist_ws_bytes(q.grid, E));
             MapsPlan r{};
             if (plan_tpersist(r, T, E, K)) b = std::max(b, persist_ws_bytes(r.grid, E));
-            MapsPlan u{};
-            if (plan_tma(u, T, E, K)) b = std::max(b, persist_ws_bytes(u.grid, E));
             MapsPlan v{};
             if (plan_tile(v, T, E, K)) b = std::max(b, persist_ws_bytes(v.grid, E));
             return b;
@@ -2406,8 +2181,11 @@ struct MapsLaunchT {
                              int* grid) {
             const MapsPlan p = plan(T, E, K, mode);
             const bool pers = p.path == Path::Persistent || p.path == Path::TPersistent ||
-                              p.path == Path::Tma || p.path == Path::Tile;
+                              p.path == Path::Tile;
+            // Routing paths name their router kernel: the hybrid and the warp-per-token router.
             const int pk = p.path == Path::Single ? KB_MAPS_SINGLE_CTA
+                         : (ROUTE && p.path == Path::TPersistent) ? KB_MAPS_HYBRID_ROUTER
+                         : (ROUTE && p.path == Path::Persistent) ? KB_MAPS_WARP_ROUTER
                          : pers ? KB_MAPS_MULTI_CTA : KB_MAPS_TWO_KERNEL;
             if (path) *path = pk;
             if (launches) *launches = (p.path == Path::TwoKernel) ? 2 : 1;
@@ -2529,7 +2307,7 @@ extern "C" int kb_expert_maps(const int32_t* ids, int32_t* counts, int64_t* offs
                               int E, int K, int mode, kb_stream_t stream) {
     int st = check_common(T, E, K);
     if (st) return st;
-    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_TWO_KERNEL) return KB_ERR_INVALID_ARG;
+    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_WARP_ROUTER) return KB_ERR_INVALID_ARG;
     if (!offsets) return KB_ERR_INVALID_ARG;
     if (T == 0)
         return launch(zero_offsets_kernel, dim3(1), dim3(512), 0, (cudaStream_t)stream, offsets,
@@ -2547,7 +2325,7 @@ extern "C" int kb_router_maps(const float* logits, const float* bias, int32_t* i
                               int renorm, int mode, kb_stream_t stream) {
     int st = check_common(T, E, K);
     if (st) return st;
-    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_TWO_KERNEL) return KB_ERR_INVALID_ARG;
+    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_WARP_ROUTER) return KB_ERR_INVALID_ARG;
     if (!offsets) return KB_ERR_INVALID_ARG;
     if (T == 0)
         return launch(zero_offsets_kernel, dim3(1), dim3(512), 0, (cudaStream_t)stream, offsets,
@@ -2564,7 +2342,7 @@ extern "C" int kb_maps_describe(int64_t T, int E, int K, int route, int mode, in
                                 int* launches, int* grid) {
     int st = check_common(T, E, K);
     if (st) return st;
-    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_TWO_KERNEL) return KB_ERR_INVALID_ARG;
+    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_WARP_ROUTER) return KB_ERR_INVALID_ARG;
     if (T == 0) {
         if (path) *path = KB_MAPS_SINGLE_CTA;
         if (launches) *launches = 1;

@@ -24,6 +24,7 @@ KB_WS_CLEAN, KB_WS_TIMEOUT, KB_WS_MISALIGNED = 0, 1, 2
 
 KB_BF16, KB_F16, KB_F32 = 0, 1, 2
 KB_MAPS_AUTO, KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA, KB_MAPS_TWO_KERNEL = 0, 1, 2, 3
+KB_MAPS_HYBRID_ROUTER, KB_MAPS_WARP_ROUTER = 4, 5
 
 # name -> (restype, argtypes); must match include/kolibri_b200.h one for one.
 SIGNATURES = {

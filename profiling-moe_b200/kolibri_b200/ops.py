@@ -11,8 +11,9 @@ from typing import Optional, Tuple
 
 import torch
 
-from ._lib import (KB_BF16, KB_F16, KB_F32, KB_MAPS_AUTO, KB_MAPS_MULTI_CTA, KB_MAPS_SINGLE_CTA,
-                   KB_MAPS_TWO_KERNEL, KB_NOALLOC_REZERO, check, load)
+from ._lib import (KB_BF16, KB_F16, KB_F32, KB_MAPS_AUTO, KB_MAPS_HYBRID_ROUTER,
+                   KB_MAPS_MULTI_CTA, KB_MAPS_SINGLE_CTA, KB_MAPS_TWO_KERNEL, KB_MAPS_WARP_ROUTER,
+                   KB_NOALLOC_REZERO, check, load)
 
 __all__ = [
     "router", "expert_maps", "router_maps", "expand_rows", "qk_norm_rope", "rope_inv_freq",
@@ -20,6 +21,7 @@ __all__ = [
     "set_wait_limit", "workspace_status",
     "moe_finalize",
     "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA", "KB_MAPS_TWO_KERNEL",
+    "KB_MAPS_HYBRID_ROUTER", "KB_MAPS_WARP_ROUTER",
 ]
 
 _DTYPE_CODE = {torch.bfloat16: KB_BF16, torch.float16: KB_F16, torch.float32: KB_F32}

@@ -8,7 +8,7 @@ import torch
 
 from conftest import GOLDEN
 from kb_testutil import np_of
-from kolibri_b200 import ops
+from kolibri_b200 import _lib, ops
 from kolibri_b200 import workloads as wl
 from oracle import kolibri_oracle as orc
 
@@ -123,6 +123,28 @@ def test_router_maps_fused(T, mode):
         assert torch.equal(ids.cpu(), rid)
         torch.testing.assert_close(w.cpu(), rw, rtol=1e-6, atol=0)
         check_maps(rid, (c, off, p2u, u2p))
+
+
+@pytest.mark.parametrize("E,k", [(384, 6), (256, 8), (128, 6), (512, 6)])
+@pytest.mark.parametrize("T", [33, 4096, 65536])
+@pytest.mark.parametrize("mode", [ops.KB_MAPS_HYBRID_ROUTER, ops.KB_MAPS_WARP_ROUTER])
+def test_router_maps_forced_fallback_paths(mode, T, E, k):
+    """The routing paths AUTO takes only when the tile kernel does not apply, forced: the
+    hybrid-router and the warp-per-token-router persistent kernels, bit-exact against the
+    oracle (ids, maps) and within 1e-6 (weights), the path confirmed by kb_maps_describe."""
+    import ctypes
+    path = ctypes.c_int(-1)
+    _lib.check(_lib.load().kb_maps_describe(T, E, k, 1, mode, ctypes.byref(path), None, None),
+               "kb_maps_describe")
+    assert path.value in (mode, ops.KB_MAPS_WARP_ROUTER, ops.KB_MAPS_TWO_KERNEL)
+    if mode == ops.KB_MAPS_HYBRID_ROUTER and E in (128, 256, 384, 512):
+        assert path.value == ops.KB_MAPS_HYBRID_ROUTER
+    logits, bias = wl.router_inputs(T, seed=3, E=E)
+    ids, w, c, off, p2u, u2p = ops.router_maps(logits.cuda(), bias.cuda(), k=k, mode=mode)
+    rid, rw = orc.router_ref(logits, bias, k=k)
+    assert torch.equal(ids.cpu(), rid)
+    torch.testing.assert_close(w.cpu(), rw, rtol=1e-6, atol=0)
+    check_maps(rid, (c, off, p2u, u2p), E)
 
 
 def test_expansion_and_prologue(api):
