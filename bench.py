@@ -402,6 +402,15 @@ def main():
     from kolibri_b200 import _lib, ops
     from kolibri_b200 import workloads as wl
 
+    if args.only_kernel == "decode_chain":  # the one-launch chain alone (profiling runs)
+        from kolibri_b200 import decode_chain as dc
+        ch = dc.DecodeChain(args.only_T or 1, dc.make_layers(args.chain_layers, dev), dev)
+        for _ in range(4):
+            ch.run_mega(torch.cuda.current_stream(dev))
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            print(json.dumps({"decode_chain_calls": 4, "T": args.only_T or 1}), flush=True)
+        return
     if args.only_kernel:  # one kernel of the per-kernel table alone (profiling runs)
         peak, _ = measured_peak()
         tab = kernel_table(dev, torch.cuda.Stream(dev), peak, args.only_kernel, args.only_T)
