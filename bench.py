@@ -4,8 +4,9 @@
 Step = one pass of the fused router + expert-map build (kb_router_maps) over one batch of
 T tokens of synthetic router logits (fp32 [T, 384] ~ N(0,1), bias ~ N(0, 0.1)); T = 65536
 per GPU (the large-T configuration of the metric).  With N GPUs every rank routes its own
-T tokens and the ranks exchange their per-expert counts (all-gather, the expert-parallel
-exchange step), so the work per GPU is fixed ("weak" scaling) and value = N*T / step time.
+T tokens and the ranks all-gather their per-expert counts (the expert-parallel exchange
+step) with kb_ep_counts_allgather, a kernel that stores into the peers' memory over
+NVLink; the work per GPU is fixed ("weak" scaling) and value = N*T / step time.
 
   value     device-resident throughput: inputs already in HBM, steps replayed from CUDA
             graphs, four rotating 100 MB input sets (together > the 126 MB L2)
@@ -14,6 +15,12 @@ exchange step), so the work per GPU is fixed ("weak" scaling) and value = N*T / 
   roofline  algorithmic bytes of the router+map pass (1632 B/token + 6164 B/call) over its
             measured device time, against MEASURED_PEAKS.json hbm_gbs
   cpu_baseline  the reference's eager router + map path on the host cores (rank 0, N=1)
+  kernels   (N=1) every kernel of the path at every benchmark T: us/call, GB/s, roofline
+            fraction, and the reference's eager CPU time of the same call
+  decode_chain  the 50-layer chain at T in {1, 32, 256, 8192}; with N GPUs the batch is
+            token-sharded T/N per rank with the expert-parallel exchange in every layer
+  ep_dispatch   one layer's expert-parallel round trip at 4096 tokens per GPU, checked bit
+            for bit (ep_parity) before it is timed
 
 --impl reference times the reference's eager CPU path alone (rank 0; other ranks exit).
 """
@@ -37,6 +44,7 @@ sys.path.insert(0, str(REPO / "profiling-moe_b200"))
 METRIC = "router+expert-map Mtok/s (50-layer non-GEMM decode us/token reported alongside)"
 UNIT = "Mtok/s"
 E, K = 384, 6
+HIDDEN = 6144
 BYTES_PER_TOKEN = 1536 + 24 + 24 + 24 + 24      # logits, ids, w, p2u, u2p
 BYTES_PER_CALL = 384 * 4 + 385 * 8 + 384 * 4    # bias, offsets, counts
 
@@ -58,6 +66,8 @@ def parse():
     p.add_argument("--only-kernel", default="",
                    help="time one kernel of the per-kernel table alone (profiling runs)")
     p.add_argument("--only-T", type=int, default=0)
+    p.add_argument("--no-ep", action="store_true",
+                   help="skip the expert-parallel round trip")
     return p.parse_args()
 
 
@@ -273,60 +283,105 @@ def run_reference(args):
 # ------------------------------------------------------------------------------------
 # 50-layer decode chain (replicas only: every rank times its own copy at N>1)
 # ------------------------------------------------------------------------------------
-def decode_chain_times(dev, tokens, n_layers, stream, steps=20, warmup=3):
+def _time_graph(g, stream, dev, steps, warmup, world):
+    """Device time of one replay of g (CUDA events on `stream`, max over ranks), in ms."""
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(steps):
+            g.replay()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def decode_chain_times(dev, tokens, n_layers, stream, world=1, steps=20, warmup=3):
+    """The 50-layer chain at every batch size.  One GPU: the per-stage graph with and without
+    the gate GEMM, the one-launch kernel (T <= 4), and the token-sharded expert-parallel
+    layer (self exchange).  N GPUs: batch T is sharded T/N tokens per rank and every layer
+    runs the expert-parallel exchange over peer memory (config 4); a batch smaller than N
+    (T = 1) runs as replicas (the one-launch kernel on every rank)."""
     from kolibri_b200 import decode_chain as dc
+    from kolibri_b200.ep import PeerExpertParallel
     layers = dc.make_layers(n_layers, dev)
     out = {"layers": n_layers, "rnope_layers": sum(L.rnope for L in layers),
-           "stages": "qk_norm_rope, sandwich, gate GEMM/GEMV, router+maps, expansion, "
-                     "post-MoE+pre-attn norm",
+           "stages": "qk_norm_rope, sandwich, gate GEMM/GEMV, router+maps, expansion or the "
+                     "expert-parallel exchange, post-MoE+pre-attn norm",
            "paths": {"with_gate_gemm": "CUDA graph of per-stage kernels + cuBLAS gate GEMM",
                      "non_gemm_only": "the same graph without the gate GEMM",
                      "one_launch_with_gate_gemv": "kb_decode_chain: all layers in one "
-                                                  "persistent launch (T <= 4)"},
-           "graph": True, "by_T": {}}
-    for T in tokens:
-        rec = {}
-        for gemm in (True, False):
-            ch = dc.DecodeChain(T, layers, dev, gate_gemm=gemm, expansion=True)
-            g = ch.capture(stream)
-            with torch.cuda.stream(stream):
+                                                  "persistent launch (T <= 4)",
+                     "ep_sharded": "T/N tokens per rank; per layer the per-stage kernels, "
+                                   "cuBLAS gate GEMM, then the peer-memory count all-gather, "
+                                   "dispatch to the 384/N expert owners, identity experts, "
+                                   "combine back + finalize as the layer's MoE output"},
+           "graph": True, "n_gpus": world, "by_T": {}}
+    sharded = [T for T in tokens if T >= world and T % world == 0]
+    ep = None
+    if sharded:
+        ep = PeerExpertParallel(E, K, HIDDEN, max_tokens=max(sharded) // world, device=dev)
+    try:
+        for T in tokens:
+            rec = {}
+            if world == 1:
+                for gemm in (True, False):
+                    ch = dc.DecodeChain(T, layers, dev, gate_gemm=gemm, expansion=True)
+                    g = ch.capture(stream)
+                    ms = _time_graph(g, stream, dev, steps, warmup, world)
+                    key = "with_gate_gemm" if gemm else "non_gemm_only"
+                    rec[key] = {"us_per_step": round(ms * 1e3, 2),
+                                "us_per_token": round(ms * 1e3 / T, 4),
+                                "kb_launches_per_step": ch.launches_per_layer() * n_layers}
+                    del g, ch
+            if T <= dc.DecodeChain.MEGA_MAX_T and (world == 1 or T not in sharded):
+                ch = dc.DecodeChain(T, layers, dev, gate_gemm=True, expansion=True)
                 for _ in range(warmup):
-                    g.replay()
-            torch.cuda.synchronize(dev)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                a.record(stream)
-                for _ in range(steps):
-                    g.replay()
-                b.record(stream)
-            torch.cuda.synchronize(dev)
-            ms = a.elapsed_time(b) / steps
-            key = "with_gate_gemm" if gemm else "non_gemm_only"
-            rec[key] = {"us_per_step": round(ms * 1e3, 2),
-                        "us_per_token": round(ms * 1e3 / T, 4),
-                        "kb_launches_per_step": ch.launches_per_layer() * n_layers}
-            del g, ch
-        if T <= dc.DecodeChain.MEGA_MAX_T:  # the whole chain as one kb_decode_chain launch
-            ch = dc.DecodeChain(T, layers, dev, gate_gemm=True, expansion=True)
-            for _ in range(warmup):
-                ch.run_mega(stream)
-            torch.cuda.synchronize(dev)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                a.record(stream)
-                for _ in range(steps):
                     ch.run_mega(stream)
-                b.record(stream)
-            torch.cuda.synchronize(dev)
-            ms = a.elapsed_time(b) / steps
-            rec["one_launch_with_gate_gemv"] = {"us_per_step": round(ms * 1e3, 2),
-                                                "us_per_token": round(ms * 1e3 / T, 4),
-                                                "kb_launches_per_step": 1}
-            del ch
-        out["by_T"][str(T)] = rec
+                torch.cuda.synchronize(dev)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    a.record(stream)
+                    for _ in range(steps):
+                        ch.run_mega(stream)
+                    b.record(stream)
+                torch.cuda.synchronize(dev)
+                ms = a.elapsed_time(b) / steps
+                key = "one_launch_with_gate_gemv" if world == 1 else "replicas_one_launch"
+                rec[key] = {"us_per_step": round(ms * 1e3, 2), "us_per_token": round(ms * 1e3 / T, 4),
+                            "kb_launches_per_step": 1}
+                del ch
+            if T in sharded:
+                ch = dc.DecodeChain(T // world, layers, dev, gate_gemm=True, ep=ep)
+                g = ch.capture(stream)
+                ms = _time_graph(g, stream, dev, max(3, steps // 2), warmup, world)
+                rec["ep_sharded"] = {"us_per_step": round(ms * 1e3, 2),
+                                     "us_per_token": round(ms * 1e3 / T, 4),
+                                     "tokens_per_rank": T // world,
+                                     "kb_launches_per_step": ch.launches_per_layer() * n_layers,
+                                     "exchange_status": ep.pg.status()}
+                del g, ch
+            out["by_T"][str(T)] = rec
+    finally:
+        if ep is not None:
+            ep.close()
     t1 = out["by_T"].get("1")
     if t1:
-        best = t1.get("one_launch_with_gate_gemv", t1["with_gate_gemm"])
+        best = t1.get("one_launch_with_gate_gemv") or t1.get("replicas_one_launch") or \
+            t1.get("with_gate_gemm")
         out["us_per_token_bs1"] = best["us_per_token"]
     return out
 
@@ -334,52 +389,92 @@ def decode_chain_times(dev, tokens, n_layers, stream, steps=20, warmup=3):
 # ------------------------------------------------------------------------------------
 # Expert-parallel dispatch + combine (N > 1): count all-gather and token all-to-all
 # ------------------------------------------------------------------------------------
-def ep_round_trip(dev, world, rank, T=4096, H=6144, steps=10, warmup=3):
+def ep_round_trip(dev, world, rank, T=4096, H=HIDDEN, steps=10, warmup=3):
+    """One MoE layer's expert-parallel round trip at T tokens per GPU: router + maps, count
+    all-gather, dispatch to the owners, identity experts, combine back + finalize.  The timed
+    path is the peer-memory exchange (kb_ep_*), replayed from a CUDA graph; before timing it
+    is checked bit for bit against the one-GPU finalize(expand(x)) of the same routing and,
+    with N > 1, against the collective exchange (ExpertParallel over NCCL), whose eager time
+    is reported beside it."""
     import torch.distributed as dist
+    from kolibri_b200 import ops
     from kolibri_b200 import workloads as wl
-    from kolibri_b200.ep import ExpertParallel
+    from kolibri_b200.ep import ExpertParallel, PeerExpertParallel
     g = torch.Generator().manual_seed(31 + rank)
     x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
     logits, bias = wl.router_inputs(T, seed=41 + rank)
     logits, bias = logits.to(dev), bias.to(dev)
-    ep = ExpertParallel(E, K)
-    # Parity: with identity experts, combine(dispatch(x)) equals the one-GPU path
-    # finalize(expand(x)) of the same routing, bit for bit, on every rank.
-    from kolibri_b200 import ops
-    d0 = ep.dispatch(x, logits, bias)
-    out0 = ep.combine(d0, d0.rows)
-    _, w0, _, _, p2u0, u2p0 = ops.router_maps(logits, bias)
-    ref0 = ops.moe_finalize(ops.expand_rows(x, p2u0), u2p0, w0)
-    Er = E // world
-    owned = bool(((d0.meta[:, 0] >= rank * Er) & (d0.meta[:, 0] < (rank + 1) * Er)).all())
-    ok = torch.tensor([1 if (torch.equal(out0, ref0) and owned) else 0], device=dev)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    parity = bool(ok.item())
-    del d0, out0, ref0
-    sent = 0
-    for i in range(warmup + steps):
-        if i == warmup:
+    pep = PeerExpertParallel(E, K, H, max_tokens=T, device=dev)
+    graph = None
+    try:
+        d = pep.dispatch(x, logits, bias)
+        out = pep.combine(d, d.rows)
+        _, w0, _, _, p2u0, u2p0 = ops.router_maps(logits, bias)
+        local = ops.moe_finalize(ops.expand_rows(x, p2u0), u2p0, w0)
+        torch.cuda.synchronize(dev)
+        R = d.num_rows()
+        ok = torch.equal(out, local) and pep.pg.status() == 0
+        nccl_ms = None
+        if world > 1:
+            ref_ep = ExpertParallel(E, K)
+            r = ref_ep.dispatch(x, logits, bias)
+            rout = ref_ep.combine(r, r.rows)
+            ok = ok and torch.equal(rout, local) and R == r.rows.shape[0] and \
+                torch.equal(d.rows[:R], r.rows) and torch.equal(d.expert_offsets, r.expert_offsets)
+            del r, rout
+            for i in range(warmup + steps):     # the collective path, eager (host splits)
+                if i == warmup:
+                    torch.cuda.synchronize(dev)
+                    dist.barrier()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                rr = ref_ep.dispatch(x, logits, bias)
+                ref_ep.combine(rr, rr.rows)
+            b.record()
             torch.cuda.synchronize(dev)
-            dist.barrier()
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-        d = ep.dispatch(x, logits, bias)
-        ep.combine(d, d.rows)  # identity experts
-        sent = sum(d.send_splits) - d.send_splits[rank]
-    b.record()
-    torch.cuda.synchronize(dev)
-    ms = torch.tensor([a.elapsed_time(b) / steps], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
-    nvlink_bytes = 2 * sent * (H * 2 + 12)  # rows and metadata out, rows back
-    return {"tokens_per_gpu": T, "hidden": H, "experts_per_gpu": E // world,
-            "ep_parity": parity,
-            "us_per_step": round(ms * 1e3, 2),
-            "stages": "router+maps, expansion, count all-gather, row+meta all-to-all, "
-                      "grouping by local expert, reverse all-to-all, finalize",
-            "remote_bytes_per_gpu": nvlink_bytes,
-            "remote_GBps_per_gpu": round(nvlink_bytes / (ms * 1e-3) / 1e9, 1)}
+            t = torch.tensor([a.elapsed_time(b) / steps], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            nccl_ms = float(t.item())
+            flag = torch.tensor([1 if ok else 0], device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            ok = bool(flag.item())
+        # rows this rank sends to other ranks (dispatch) and gets back (combine)
+        Er = E // world
+        mine = d.gathered[rank].view(world, Er).sum(-1)
+        sent = int(mine.sum().item()) - int(mine[rank].item())
+        ops.reserve_workspace(T)
+        s = torch.cuda.Stream(dev)
+        obuf = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        with torch.cuda.stream(s):
+            dd = pep.dispatch(x, logits, bias)
+            pep.combine(dd, dd.rows, obuf)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            dd = pep.dispatch(x, logits, bias)
+            pep.combine(dd, dd.rows, obuf)
+        ms = _time_graph(graph, s, dev, steps, warmup, world)
+        ok = ok and torch.equal(obuf, local) and pep.pg.status() == 0
+        if world > 1:
+            flag = torch.tensor([1 if ok else 0], device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            ok = bool(flag.item())
+    finally:
+        graph = None
+        pep.close()
+    remote = 2 * sent * H * 2      # rows out to the owners and back; no metadata travels
+    res = {"tokens_per_gpu": T, "hidden": H, "experts_per_gpu": E // world, "ep_parity": ok,
+           "us_per_step": round(ms * 1e3, 2),
+           "stages": "router+maps, peer count all-gather, dispatch (expansion + pack + "
+                     "all-to-all in one kernel), identity experts, combine back + finalize",
+           "kb_launches_per_step": 5,
+           "remote_bytes_per_gpu": remote,
+           "remote_GBps_per_gpu": round(remote / (ms * 1e-3) / 1e9, 1) if world > 1 else None,
+           "parity": "combine(dispatch(x)) == finalize(expand(x)) bit for bit"
+                     + (", rows/segments == the NCCL collective path" if world > 1 else "")}
+    if nccl_ms is not None:
+        res["nccl_collective_path_us_per_step"] = round(nccl_ms * 1e3, 2)
+    return res
 
 
 # ------------------------------------------------------------------------------------
@@ -434,6 +529,12 @@ def main():
     u2p = torch.empty(T * K, dtype=torch.int32, device=dev)
     gathered = torch.empty(world, E, dtype=torch.int32, device=dev)
     lib = _lib.load()
+    # N > 1: the per-expert counts are all-gathered by a kernel over peer memory (no NCCL in
+    # the step), so the whole step is captured in CUDA graphs at every N.
+    counts_pg = None
+    if world > 1:
+        from kolibri_b200.ep import PeerGroup
+        counts_pg = PeerGroup(E, K, 0, 16, device=dev)
     ws_bytes = lib.kb_router_maps_workspace_bytes(T, E, K)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream(dev)
@@ -447,7 +548,10 @@ def main():
                                       torch.cuda.current_stream(dev).cuda_stream),
                    "kb_router_maps")
         if world > 1:
-            dist.all_gather_into_tensor(gathered, counts)
+            _lib.check(lib.kb_ep_counts_allgather(counts_pg.addr, counts.data_ptr(),
+                                                  gathered.data_ptr(),
+                                                  torch.cuda.current_stream(dev).cuda_stream),
+                       "kb_ep_counts_allgather")
 
     # Graphs: one per input set (router+maps, and the count all-gather for N>1).
     torch.cuda.synchronize(dev)
@@ -456,18 +560,17 @@ def main():
             step(i)
     torch.cuda.synchronize(dev)
     graphs = []
-    graph_all = None
-    if world == 1:  # N > 1: the step (kernel + NCCL all-gather) runs eagerly
+    for i in range(nsets):
+        gi = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gi, stream=stream):
+            step(i)
+        graphs.append(gi)
+    del gi
+    graph_all = torch.cuda.CUDAGraph()  # the nsets steps back to back in one graph
+    with torch.cuda.graph(graph_all, stream=stream):
         for i in range(nsets):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                step(i)
-            graphs.append(g)
-        graph_all = torch.cuda.CUDAGraph()  # the nsets steps back to back in one graph
-        with torch.cuda.graph(graph_all, stream=stream):
-            for i in range(nsets):
-                step(i)
-    run = (lambda i: graphs[i % nsets].replay()) if graphs else step
+            step(i)
+    run = lambda i: graphs[i % nsets].replay()  # noqa: E731
 
     def run_steps(n):
         """n steps in order: whole groups of nsets from the combined graph, the rest singly."""
@@ -537,7 +640,9 @@ def main():
                                           T, E, K, 0, _lib.KB_MAPS_AUTO, cs.cuda_stream),
                        "kb_router_maps")
             if world > 1:
-                dist.all_gather_into_tensor(gathered, counts)
+                _lib.check(lib.kb_ep_counts_allgather(counts_pg.addr, counts.data_ptr(),
+                                                      gathered.data_ptr(), cs.cuda_stream),
+                           "kb_ep_counts_allgather")
             for o, oh in zip(outs, outs_h):
                 oh.copy_(o, non_blocking=True)
 
@@ -563,7 +668,18 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(ems, 4), "steps": e_steps}
 
-    ep = ep_round_trip(dev, world, rank) if world > 1 else None
+    # N > 1: the last step's all-gathered counts against NCCL's all-gather of the same counts.
+    count_parity = None
+    if world > 1:
+        torch.cuda.synchronize(dev)
+        nccl_counts = torch.empty(world, E, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(nccl_counts, counts)
+        flag = torch.tensor([1 if (torch.equal(nccl_counts, gathered) and
+                                   counts_pg.status() == 0) else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        count_parity = bool(flag.item())
+
+    ep = ep_round_trip(dev, world, rank) if not args.no_ep else None
 
     kernels = None
     if not args.no_kernels and world == 1:
@@ -574,16 +690,20 @@ def main():
     chain = None
     if args.chain_tokens:
         chain = decode_chain_times(dev, [int(t) for t in args.chain_tokens.split(",") if t],
-                                   args.chain_layers, stream)
+                                   args.chain_layers, stream, world=world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_reference_rate(T, steps=20, warmup=1, budget_s=20.0)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
+    # Every graph is released before the exchange buffers and the process group go.
+    run = None
+    graphs.clear()
+    graph_all = None
     if world > 1:
         dist.barrier()
-        graphs.clear()
+        counts_pg.close()
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -595,9 +715,11 @@ def main():
         "config": {"workload": f"fused router+expert-maps, T={T} tokens per GPU, E=384, k=6",
                    "tokens_per_gpu": T, "experts": E, "top_k": K,
                    "l2": "4 rotating input sets of 100 MB (> 126 MB L2 together)",
-                   "graph": bool(graphs),
-                   "steps_per_graph_replay": nsets if graphs else 0,
-                   "parallelism": f"token-sharded x{world}" + (" + count all-gather" if world > 1 else "")},
+                   "graph": True,
+                   "steps_per_graph_replay": nsets,
+                   "parallelism": f"token-sharded x{world}" + (
+                       " + per-expert count all-gather over peer memory (kb_ep_counts_allgather)"
+                       if world > 1 else "")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "algorithmic_bytes": alg_bytes, "peak_source": peak_kind,
@@ -607,7 +729,8 @@ def main():
         "decode_chain": chain,
         "kernels": kernels,
         "ep_dispatch": ep,
-        "gpu_launches": launches_per_step * args.steps,
+        "count_exchange_parity": count_parity,
+        "gpu_launches": (launches_per_step + (1 if world > 1 else 0)) * args.steps,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

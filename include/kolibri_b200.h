@@ -71,17 +71,19 @@ KB_API int kb_version(void);
  * kb_workspace_status reads the error word (it waits for `stream` first):
  *   kind   KB_WS_MAPS (kb_expert_maps / kb_router_maps workspace), KB_WS_CHAIN
  *          (kb_decode_chain workspace), KB_WS_NOALLOC (the static scratch of
- *          kb_expert_maps_noalloc on the current device; workspace is ignored)
+ *          kb_expert_maps_noalloc on the current device; workspace is ignored), KB_WS_EP
+ *          (a rank's expert-parallel exchange buffer, section (e) below)
  *   status KB_WS_CLEAN (0), KB_WS_TIMEOUT (1: a bounded wait gave up),
  *          KB_WS_MISALIGNED (2: kb_decode_chain found a layer weight pointer that is not
- *          16-byte aligned)
+ *          16-byte aligned), KB_WS_CAPACITY (3: an expert-parallel exchange received more
+ *          rows than its buffer holds, or a rank's counts were invalid)
  * kb_set_wait_limit sets the number of polls after which every later launch's waits give up
  * (0 restores the defaults, about a second of polling); it returns the previous setting.  A
  * short limit makes waits give up early on purpose, so that the error path can be exercised.
  * No counterpart in the reference (its kernels report launch errors only,
  * kernels/cuda/customKolibriBuildExpertMapsKernel.cu:78-88). */
-enum { KB_WS_MAPS = 0, KB_WS_CHAIN = 1, KB_WS_NOALLOC = 2 };
-enum { KB_WS_CLEAN = 0, KB_WS_TIMEOUT = 1, KB_WS_MISALIGNED = 2 };
+enum { KB_WS_MAPS = 0, KB_WS_CHAIN = 1, KB_WS_NOALLOC = 2, KB_WS_EP = 3 };
+enum { KB_WS_CLEAN = 0, KB_WS_TIMEOUT = 1, KB_WS_MISALIGNED = 2, KB_WS_CAPACITY = 3 };
 KB_API int kb_workspace_status(const void *workspace, int kind, int *status, kb_stream_t stream);
 KB_API long long kb_set_wait_limit(long long polls);
 /* Programmatic dependent launch on (1, default) or off (0) for every later launch
@@ -293,6 +295,85 @@ KB_API int kb_decode_chain(const kb_chain_layer_t *layers, int n_layers, const v
                            int32_t *u2p, void *permuted, float *trace_logits, void *workspace,
                            size_t workspace_bytes, int64_t T, int H, int Hq, int Hkv, int D,
                            int E, int K, float eps, kb_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * (e) Expert-parallel exchange over peer memory: one process per GPU on one node; rank r of N
+ * routes its own tokens and owns experts [r*E/N, (r+1)*E/N).  Every rank allocates one
+ * exchange buffer (kb_ep_alloc, kb_ep_buffer_bytes), exports it (kb_ipc_export), and maps every
+ * other rank's buffer (kb_ipc_import) into a kb_ep_group_t; the transfers are then plain stores
+ * of this GPU's kernels into the peers' buffers over NVLink / NVSwitch, followed by release
+ * increments of the receivers' arrival counters.  No host round trip and no NCCL call: the
+ * splits and the destination rows are derived on the device from the all-gathered counts, so
+ * every call below is asynchronous and can be captured in a CUDA graph.
+ *
+ * The calls are collective: every rank makes the same sequence of kb_ep_* calls on its own
+ * stream (one rank's call waits, bounded, for the others).  Per MoE layer:
+ *   kb_router_maps -> kb_ep_counts_allgather -> kb_ep_dispatch -> expert GEMMs on the rows
+ *   of kb_ep_recv_rows (segments recv_offsets) -> kb_ep_combine.
+ * Row order on the owner: by local expert, then by sending rank, then in the sender's
+ * permuted (expert, token, slot) order -- the order an all-to-all of the expert-sorted rows
+ * followed by a stable grouping by local expert produces.
+ *
+ * Failure contract: every wait is bounded (kb_set_wait_limit; by default about ten seconds
+ * of polling, since a peer may start late).  A wait that gives up, or counts that exceed the
+ * buffer's capacity, set the error word of this rank's buffer (kb_workspace_status with
+ * KB_WS_EP and workspace = buf[rank]: KB_WS_TIMEOUT or KB_WS_CAPACITY); every later kb_ep_*
+ * call on the group then returns at once (kb_ep_counts_allgather writes gathered = -1), and
+ * the peers' waits for this rank give up in turn.  Recovery is a new group (fresh buffers).
+ * The reference runs on one GPU and has no such path; the exchange follows the per-expert
+ * counts of its maps (kernels/cuda/customKolibriBuildExpertMapsKernel.cu:96-156) and the
+ * finalize of its harness (benchmarks/11_profile_2block_e2e.py:259-262). */
+#define KB_MAX_RANKS 8
+#define KB_IPC_HANDLE_BYTES 64
+typedef struct {
+    int world;                 /* number of ranks N, 1 <= N <= KB_MAX_RANKS                 */
+    int rank;                  /* this process's rank                                        */
+    int num_experts;           /* E (a multiple of N, <= 512)                                */
+    int top_k;                 /* K (<= 32)                                                  */
+    int64_t max_tokens;        /* largest token count of any rank's call                     */
+    int64_t row_bytes;         /* bytes of one activation row (a multiple of 16)             */
+    void *buf[KB_MAX_RANKS];   /* every rank's exchange buffer as mapped in this process
+                                  (buf[rank] = this rank's own, from kb_ep_alloc)            */
+} kb_ep_group_t;
+
+/* Size of one rank's exchange buffer (identical on every rank for identical arguments):
+ * control words, the tagged count rows, N*max_tokens*K received rows, max_tokens*K returned
+ * rows.  kb_ep_alloc allocates it with cudaMalloc on the current device and zero-fills it
+ * (set-up call: synchronous, the only allocation in this library); kb_ep_free releases it. */
+KB_API size_t kb_ep_buffer_bytes(int world, int E, int K, int64_t max_tokens, int64_t row_bytes);
+KB_API int kb_ep_alloc(size_t bytes, void **buf);
+KB_API int kb_ep_free(void *buf);
+/* CUDA IPC export of a kb_ep_alloc buffer into KB_IPC_HANDLE_BYTES host bytes, and the
+ * mapping of a peer's exported buffer into this process (peer access enabled on first use). */
+KB_API int kb_ipc_export(const void *buf, void *handle);
+KB_API int kb_ipc_import(const void *handle, void **buf);
+KB_API int kb_ipc_close(void *buf);
+
+/* gathered[q*E + e] = counts[e] of rank q (int32 [N, E]).  One CTA: it stores this rank's
+ * counts, tagged with the call's epoch, into every rank's buffer and waits for every rank's
+ * row (two slots by epoch parity).  Replaces the ncclAllGather of counts. */
+KB_API int kb_ep_counts_allgather(const kb_ep_group_t *g, const int32_t *counts,
+                                  int32_t *gathered, kb_stream_t stream);
+/* Sends this rank's routed rows to their owners: permuted row r (expert e, source token
+ * p2u[r] % T of x [T, row_bytes]) goes straight to its final grouped row on rank e/(E/N) --
+ * the expansion, the pack and the all-to-all in one pass.  recv_offsets int64 [E/N + 1]:
+ * segments of this rank's local experts in its received rows (kb_ep_recv_rows).  Returns
+ * when this rank's rows are sent and every rank's rows for this rank have arrived.
+ * gathered is this call's kb_ep_counts_allgather output; p2u the maps of the same routing. */
+KB_API int kb_ep_dispatch(const kb_ep_group_t *g, const void *x, int64_t T, const int32_t *p2u,
+                          const int32_t *gathered, int64_t *recv_offsets, kb_stream_t stream);
+/* Device address of this rank's received rows ([N*max_tokens*K, row_bytes] capacity; the
+ * first recv_offsets[E/N] rows are valid after kb_ep_dispatch). */
+KB_API int kb_ep_recv_rows(const kb_ep_group_t *g, void **rows);
+/* Returns the expert outputs to their origins and finalizes there: expert_out holds this
+ * rank's grouped rows (same order and count as its received rows; it may be the received
+ * rows themselves); each goes back to the sender's permuted position, then
+ *   out[t, :] = dtype( sum_k float(back[u2p[k*T + t], :]) * weights[t, k] )
+ * exactly as kb_moe_finalize.  T, u2p and weights are this rank's, from the same routing as
+ * the preceding kb_ep_dispatch; dtype KB_BF16, KB_F16 or KB_F32 (row_bytes = H * size). */
+KB_API int kb_ep_combine(const kb_ep_group_t *g, const void *expert_out, const int32_t *gathered,
+                         int64_t T, const int32_t *u2p, const float *weights, void *out,
+                         int dtype, kb_stream_t stream);
 
 #ifdef __cplusplus
 }

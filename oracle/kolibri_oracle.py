@@ -28,6 +28,12 @@ file:line, relative to the reference repository root) and runs it on the CPU:
                            (out = h + RMSNorm(moe_out); next = RMSNorm(out))
   router_logits_ref        benchmarks/11_profile_2block_e2e.py:242-243 ((x @ W_g).float())
   finalize_ref             benchmarks/11_profile_2block_e2e.py:259-262 (weighted combine by u2p)
+  ep_placement_ref         where the expert-parallel exchange puts every routed row (no reference
+                           counterpart: the reference runs on one GPU); the order an all-to-all of
+                           the expert-sorted rows (expert_maps_ref order) followed by a stable
+                           grouping by local expert produces, written as the closed formula the
+                           peer-memory kernels use, so the CPU tests can check the formula against
+                           the collective exchange
 
 Pinning: tests/golden/ holds outputs of the reference's own eager functions (extracted from
 the reference sources by tests/golden/make_golden.py) at the benchmark seeds; the oracle is
@@ -204,3 +210,36 @@ def finalize_ref(expert_out: torch.Tensor, u2p, weights: torch.Tensor) -> torch.
     valid = (perm >= 0).unsqueeze(-1)
     rows = expert_out[perm.clamp(min=0)].float() * valid
     return (rows * weights.float().t().unsqueeze(-1)).sum(0).to(expert_out.dtype)
+
+
+# --------------------------------------------------------------------------------------
+# Expert-parallel exchange: placement of the routed rows
+# --------------------------------------------------------------------------------------
+def ep_placement_ref(counts_all, world: int):
+    """counts_all int [N, E] (every rank's per-expert counts) -> for every owner rank o, the
+    list of (sender q, sender's permuted row i) in the owner's grouped order, and for every
+    sender q, dest[q][i] = (owner, grouped row) of its permuted row i.
+
+    Grouped row of sender q's permuted row i of expert e on owner o = e // (E/N):
+        (S[e] - S[o*Er]) + sum_{q' < q} c[q'][e] + (i - loff_q[e])
+    with tot[e] = sum_q c[q][e], S its exclusive scan, loff_q the exclusive scan of c[q]."""
+    c = np.asarray(counts_all, dtype=np.int64)
+    N, E = c.shape
+    assert N == world and E % N == 0
+    Er = E // N
+    tot = c.sum(0)
+    S = np.concatenate([[0], np.cumsum(tot)])
+    loff = np.concatenate([np.zeros((N, 1), np.int64), np.cumsum(c, 1)], 1)
+    before = np.concatenate([np.zeros((1, E), np.int64), np.cumsum(c, 0)[:-1]], 0)
+    grouped = [[None] * int(S[(o + 1) * Er] - S[o * Er]) for o in range(N)]
+    dest = []
+    for q in range(N):
+        dq = []
+        for e in range(E):
+            o = e // Er
+            for j in range(int(c[q, e])):
+                gpos = int(S[e] - S[o * Er] + before[q, e] + j)
+                grouped[o][gpos] = (q, int(loff[q, e] + j))
+                dq.append((o, gpos))
+        dest.append(dq)
+    return grouped, dest

@@ -26,7 +26,7 @@
 // next and the residual by CTA (t*nvec + v) mod G, Q/K head j by CTA j mod G, map entries and
 // logits by the CTA that owns them, so the writes are spread over all SMs.
 // The next layer's weights (gammas, the owned W rows, the bias) arrive in shared memory by bulk
-// copies (cp.async.bulk into this CTA's own memory, no cluster multicast) while the current
+// copies (plain cp.async.bulk from this GPU's memory into this CTA's own) while the current
 // layer runs; loads of the GEMM stand-ins (q, k, attn_out, moe_out) are issued only when their
 // stage starts and bypass L1, as loads of a tensor that a GEMM has just written would.
 //

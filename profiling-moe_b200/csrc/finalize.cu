@@ -6,9 +6,10 @@
 // 259-262).  A slot whose u2p is negative (an id outside [0, E) at routing) contributes 0.
 //
 // One CTA per token; each thread owns 16-byte vectors of the row (row_shape), gathers the K
-// source vectors (all loads in flight together), and writes the combined vector once.
+// source vectors (all loads in flight together), and writes the combined vector once
+// (finalize_math.cuh).
 // HBM bound: K + 1 row transfers per token.
-#include "kb_common.cuh"
+#include "finalize_math.cuh"
 #include "norm_math.cuh"
 
 #include <algorithm>
@@ -23,47 +24,8 @@ __global__ void __launch_bounds__(512) moe_finalize_kernel(const T* __restrict__
                                                            int K, int64_t rows, int H) {
     pdl_wait();
     pdl_launch();
-    using V = Vec16<T>;
-    constexpr int N = V::N;
-    const int nvec = H / N;
-    for (int64_t t = blockIdx.x; t < ntok; t += gridDim.x) {
-        int64_t src[KMAX];
-        float wk[KMAX];
-#pragma unroll
-        for (int k = 0; k < KMAX; ++k) {
-            src[k] = -1;
-            wk[k] = 0.0f;
-            if (k < K) {
-                const int64_t r = __ldg(u2p + (int64_t)k * ntok + t);
-                src[k] = (r >= 0 && r < rows) ? r : -1;
-                wk[k] = __ldg(w + t * K + k);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < VPT; ++i) {
-            const int v = threadIdx.x + i * blockDim.x;
-            if (v >= nvec) continue;
-            V x[KMAX];
-#pragma unroll
-            for (int k = 0; k < KMAX; ++k)
-                if (src[k] >= 0) x[k].u = ld_stream(reinterpret_cast<const uint4*>(expert_out + src[k] * H) + v);
-            float acc[N];
-#pragma unroll
-            for (int e = 0; e < N; ++e) acc[e] = 0.0f;
-#pragma unroll
-            for (int k = 0; k < KMAX; ++k) {
-                if (src[k] >= 0) {
-#pragma unroll
-                    for (int e = 0; e < N; ++e)
-                        acc[e] = __fadd_rn(acc[e], __fmul_rn(Elem<T>::to_f(x[k].e[e]), wk[k]));
-                }
-            }
-            V o;
-#pragma unroll
-            for (int e = 0; e < N; ++e) o.e[e] = Elem<T>::from_f(acc[e]);
-            st_stream(reinterpret_cast<uint4*>(out + t * H) + v, o.u);
-        }
-    }
+    for (int64_t t = blockIdx.x; t < ntok; t += gridDim.x)
+        finalize_token<T, VPT, KMAX>(expert_out, u2p, w, out, t, ntok, K, rows, H);
 }
 
 namespace {

@@ -41,6 +41,7 @@ long long wait_limit(long long dflt);
 // static scratch of kb_expert_maps_noalloc on the current device (resolved on first use).
 size_t maps_err_offset();
 size_t chain_err_offset();
+size_t ep_err_offset();
 int noalloc_scratch_address(void** out);
 
 template <typename... KArgs, typename... Args>

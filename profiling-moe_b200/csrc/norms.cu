@@ -15,14 +15,38 @@
 #include "norm_math.cuh"
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 namespace kb {
 
 // ------------------------------------------------------------------------------------
 // Register kernels: each thread owns VPT 16-byte vectors v = tid + i*blockDim.
 // ------------------------------------------------------------------------------------
+// This thread's vectors of row `row` of x and y (zeros past the row or past `rows`).
 template <typename T, int VPT>
-__global__ void __launch_bounds__(1024) residual_norm_pair_kernel(
+__device__ __forceinline__ void load_row_pair(const T* __restrict__ x, const T* __restrict__ y,
+                                              int64_t row, int64_t rows, int H, int nvec,
+                                              Vec16<T>* vx, Vec16<T>* vy) {
+    const bool in = row < rows;
+    const uint4* px = reinterpret_cast<const uint4*>(x + (in ? row : 0) * H);
+    const uint4* py = reinterpret_cast<const uint4*>(y + (in ? row : 0) * H);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int v = threadIdx.x + i * blockDim.x;
+        if (in && v < nvec) {
+            vx[i].u = ld_stream(px + v);
+            vy[i].u = ld_stream(py + v);
+        } else {
+            vx[i].u = make_uint4(0, 0, 0, 0);
+            vy[i].u = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(512) residual_norm_pair_kernel(
     const T* __restrict__ a, const T* __restrict__ res, const T* __restrict__ g1,
     const T* __restrict__ g2, T* sum_out, T* norm_out, int64_t rows, int H, float eps) {
     pdl_wait();
@@ -32,21 +56,21 @@ __global__ void __launch_bounds__(1024) residual_norm_pair_kernel(
     __shared__ float red[64];
     int turn = 0;
     const int nvec = H / N;
+    // The CTA walks rows blockIdx.x, + gridDim.x, ...; the next row's loads are issued before
+    // the current row's reductions, so two rows per CTA are in flight.
+    V na[VPT], nr[VPT];
+    load_row_pair<T, VPT>(a, res, (int64_t)blockIdx.x, rows, H, nvec, na, nr);
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-        const uint4* pa = reinterpret_cast<const uint4*>(a + row * H);
-        const uint4* pr = reinterpret_cast<const uint4*>(res + row * H);
         V va[VPT], vr[VPT];
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            va[i].u = na[i].u;
+            vr[i].u = nr[i].u;
+        }
+        load_row_pair<T, VPT>(a, res, row + gridDim.x, rows, H, nvec, na, nr);
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
-            const int v = threadIdx.x + i * blockDim.x;
-            if (v < nvec) {
-                va[i].u = ld_stream(pa + v);
-                vr[i].u = ld_stream(pr + v);
-            } else {
-                va[i].u = make_uint4(0, 0, 0, 0);
-                vr[i].u = make_uint4(0, 0, 0, 0);
-            }
 #pragma unroll
             for (int e = 0; e < N; ++e) {
                 const float x = Elem<T>::to_f(va[i].e[e]);
@@ -94,7 +118,7 @@ __global__ void __launch_bounds__(1024) residual_norm_pair_kernel(
 }
 
 template <typename T, int VPT>
-__global__ void __launch_bounds__(1024) add_rms_norm_kernel(
+__global__ void __launch_bounds__(512) add_rms_norm_kernel(
     const T* __restrict__ a, const T* __restrict__ b, const T* __restrict__ g, T* out, T* sum_out,
     int64_t rows, int H, float eps) {
     pdl_wait();
@@ -104,18 +128,24 @@ __global__ void __launch_bounds__(1024) add_rms_norm_kernel(
     __shared__ float red[64];
     int turn = 0;
     const int nvec = H / N;
+    V na[VPT], nb[VPT];   // next row, loaded one row ahead (see residual_norm_pair_kernel)
+    load_row_pair<T, VPT>(a, b, (int64_t)blockIdx.x, rows, H, nvec, na, nb);
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-        const uint4* pa = reinterpret_cast<const uint4*>(a + row * H);
-        const uint4* pb = reinterpret_cast<const uint4*>(b + row * H);
+        V ca[VPT], cb[VPT];
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            ca[i].u = na[i].u;
+            cb[i].u = nb[i].u;
+        }
+        load_row_pair<T, VPT>(a, b, row + gridDim.x, rows, H, nvec, na, nb);
         V vs[VPT];
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
             const int v = threadIdx.x + i * blockDim.x;
             if (v < nvec) {
-                V va, vb;
-                va.u = ld_stream(pa + v);
-                vb.u = ld_stream(pb + v);
+                const V& va = ca[i];
+                const V& vb = cb[i];
 #pragma unroll
                 for (int e = 0; e < N; ++e) {
                     vs[i].e[e] = Elem<T>::from_f(
@@ -217,6 +247,28 @@ inline unsigned row_grid(int64_t rows) {
     return (unsigned)std::min<int64_t>(rows, (int64_t)INT32_MAX);
 }
 
+// Grid of the register kernels: at most the CTAs that are resident at once (every CTA then
+// walks rows with a stride of the grid and keeps the next row's loads in flight).
+template <typename... KArgs>
+unsigned resident_grid(void (*kern)(KArgs...), int threads, int64_t rows) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int per_sm = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        int& v = cache[std::make_tuple(reinterpret_cast<const void*>(kern), threads, dev)];
+        if (v == 0) {
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kern, threads, 0) != cudaSuccess ||
+                v <= 0)
+                v = 1;
+        }
+        per_sm = v;
+    }
+    return (unsigned)std::min<int64_t>(rows, (int64_t)device_sm_count() * per_sm);
+}
+
 template <typename T>
 int pair_launch(const void* a, const void* res, const void* g1, const void* g2, void* sum_out,
                 void* norm_out, int64_t rows, int H, float eps, cudaStream_t st) {
@@ -233,8 +285,9 @@ int pair_launch(const void* a, const void* res, const void* g1, const void* g2, 
     dim3 grid(row_grid(rows));
 #define KB_PAIR(V)                                                                           \
     case V:                                                                                  \
-        return launch(residual_norm_pair_kernel<T, V>, grid, dim3(rs.threads), 0, st, A, R, G1, \
-                      G2, S, O, rows, H, eps);
+        return launch(residual_norm_pair_kernel<T, V>,                                       \
+                      dim3(resident_grid(residual_norm_pair_kernel<T, V>, rs.threads, rows)),  \
+                      dim3(rs.threads), 0, st, A, R, G1, G2, S, O, rows, H, eps);
     switch (rs.vpt) {
         KB_PAIR(1) KB_PAIR(2) KB_PAIR(3) KB_PAIR(4) KB_PAIR(6) KB_PAIR(8)
         default: break;
@@ -263,8 +316,9 @@ int add_launch(const void* a, const void* b, const void* g, void* out, void* sum
     dim3 grid(row_grid(rows));
 #define KB_ADD(V)                                                                              \
     case V:                                                                                    \
-        return launch(add_rms_norm_kernel<T, V>, grid, dim3(rs.threads), 0, st, A, B, G, O, S, \
-                      rows, H, eps);
+        return launch(add_rms_norm_kernel<T, V>,                                               \
+                      dim3(resident_grid(add_rms_norm_kernel<T, V>, rs.threads, rows)),         \
+                      dim3(rs.threads), 0, st, A, B, G, O, S, rows, H, eps);
     switch (rs.vpt) {
         KB_ADD(1) KB_ADD(2) KB_ADD(3) KB_ADD(4) KB_ADD(6) KB_ADD(8)
         default: break;

@@ -8,51 +8,51 @@
 // RNoPE layers pass no positions (pos == NULL): the rotation is the identity and the kernel
 // is the harness's per-head F.rms_norm (benchmarks/11_profile_2block_e2e.py:195-196).
 //
-// Layout: one warp per (token, head), D/32 consecutive elements per lane, so the NeoX
-// partner of lane l is lane l^16.  A CTA covers HPC heads of one token and computes the
-// D/2 (cos, sin) pairs of that token once in shared memory with the accurate sincosf.
+// Layout: a warp normalises whole heads, D/32 consecutive elements per lane, so the NeoX
+// partner of lane l is lane l^16.  A CTA of HPC warps covers HPC*hpw heads of one token (warp w
+// takes heads w, w+HPC, ...) and computes the D/2 (cos, sin) pairs of that token once in shared
+// memory with the accurate sincosf.  At large T, hpw = ceil(heads/HPC): one CTA per token, so
+// the trigonometry runs once per token instead of once per group of HPC heads (it dominated
+// the instruction count).  At decode T, hpw = 1: the heads spread over more CTAs.
 // Products and sums use _rn intrinsics: no FMA contraction, same roundings as eager torch.
 #include "kb_common.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace kb {
 
-template <int D, int HPC>
+template <int D, int HPC, int MAXW>
 __global__ void __launch_bounds__(HPC * 32) qk_norm_rope_kernel(
     const __nv_bfloat16* q_in, __nv_bfloat16* q_out, const __nv_bfloat16* k_in,
     __nv_bfloat16* k_out, const __nv_bfloat16* __restrict__ gq,
     const __nv_bfloat16* __restrict__ gk, const int32_t* __restrict__ pos,
     const float* __restrict__ inv_freq, int64_t T, int Hq, int Hkv, int64_t qs, int64_t ks,
-    float eps, int groups) {
+    float eps, int groups, int hpw) {
     constexpr int EPL = D / 32;  // elements per lane
     static_assert(EPL == 2 || EPL == 4 || EPL == 8, "D must be 64, 128 or 256");
+    using Lane = typename std::conditional<EPL == 2, uint32_t,
+                 typename std::conditional<EPL == 4, uint2, uint4>::type>::type;
     pdl_wait();
     pdl_launch();
     __shared__ float cs[D / 2], sn[D / 2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t = blockIdx.x / groups;
-    const int head = (int)(blockIdx.x % groups) * HPC + warp;
-    const bool active = head < Hq + Hkv;
-    const bool is_q = head < Hq;
-    const __nv_bfloat16* src = is_q ? q_in + t * qs + (int64_t)head * D
-                                    : k_in + t * ks + (int64_t)(head - Hq) * D;
-    __nv_bfloat16* dst = is_q ? q_out + t * qs + (int64_t)head * D
-                              : k_out + t * ks + (int64_t)(head - Hq) * D;
-    const __nv_bfloat16* g = is_q ? gq : gk;
+    const int head0 = (int)(blockIdx.x % groups) * HPC * hpw + warp;
+    const int heads = Hq + Hkv;
 
-    // Issue the head's loads before the trigonometry.
-    __nv_bfloat16 xv[EPL], gv[EPL];
-    if (active) {
-        if constexpr (EPL == 2) {
-            *reinterpret_cast<uint32_t*>(xv) = *reinterpret_cast<const uint32_t*>(src + lane * 2);
-            *reinterpret_cast<uint32_t*>(gv) = __ldg(reinterpret_cast<const unsigned*>(g + lane * 2));
-        } else if constexpr (EPL == 4) {
-            *reinterpret_cast<uint2*>(xv) = *reinterpret_cast<const uint2*>(src + lane * 4);
-            *reinterpret_cast<uint2*>(gv) = __ldg(reinterpret_cast<const uint2*>(g + lane * 4));
-        } else {
-            *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(src + lane * 8);
-            *reinterpret_cast<uint4*>(gv) = __ldg(reinterpret_cast<const uint4*>(g + lane * 8));
+    // Issue every head's loads (and both gammas) before the trigonometry.
+    Lane xl[MAXW];
+    Lane glq = {}, glk = {};
+    if (Hq > 0) glq = __ldg(reinterpret_cast<const Lane*>(gq) + lane);
+    if (Hkv > 0) glk = __ldg(reinterpret_cast<const Lane*>(gk) + lane);
+#pragma unroll
+    for (int i = 0; i < MAXW; ++i) {
+        const int head = head0 + i * HPC;
+        if (i < hpw && head < heads) {
+            const __nv_bfloat16* src = head < Hq ? q_in + t * qs + (int64_t)head * D
+                                                 : k_in + t * ks + (int64_t)(head - Hq) * D;
+            xl[i] = *(reinterpret_cast<const Lane*>(src) + lane);
         }
     }
     const bool rope = pos != nullptr;
@@ -66,42 +66,46 @@ __global__ void __launch_bounds__(HPC * 32) qk_norm_rope_kernel(
         }
         __syncthreads();
     }
-    if (!active) return;
 
-    float y[EPL];
-    float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-        y[i] = __bfloat162float(xv[i]);
-        ss = fmaf(y[i], y[i], ss);
-    }
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(ss / (float)D + eps);
+    for (int i = 0; i < MAXW; ++i) {
+        const int head = head0 + i * HPC;
+        if (!(i < hpw && head < heads)) continue;
+        const bool is_q = head < Hq;
+        __nv_bfloat16 xv[EPL], gv[EPL];
+        *reinterpret_cast<Lane*>(xv) = xl[i];
+        *reinterpret_cast<Lane*>(gv) = is_q ? glq : glk;
+        __nv_bfloat16* dst = is_q ? q_out + t * qs + (int64_t)head * D
+                                  : k_out + t * ks + (int64_t)(head - Hq) * D;
+        float y[EPL];
+        float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) y[i] = __fmul_rn(__fmul_rn(y[i], r), __bfloat162float(gv[i]));
-
-    __nv_bfloat16 ov[EPL];
-    if (rope) {
-        const bool first_half = lane < 16;
-#pragma unroll
-        for (int i = 0; i < EPL; ++i) {
-            const float other = __shfl_xor_sync(FULL_MASK, y[i], 16);
-            const int j = (lane * EPL + i) & (D / 2 - 1);
-            const float c = cs[j], s = sn[j];
-            const float o = first_half ? __fsub_rn(__fmul_rn(y[i], c), __fmul_rn(other, s))
-                                       : __fadd_rn(__fmul_rn(y[i], c), __fmul_rn(other, s));
-            ov[i] = __float2bfloat16_rn(o);
+        for (int e = 0; e < EPL; ++e) {
+            y[e] = __bfloat162float(xv[e]);
+            ss = fmaf(y[e], y[e], ss);
         }
-    } else {
+        ss = warp_sum(ss);
+        const float r = 1.0f / sqrtf(ss / (float)D + eps);
 #pragma unroll
-        for (int i = 0; i < EPL; ++i) ov[i] = __float2bfloat16_rn(y[i]);
-    }
-    if constexpr (EPL == 2) {
-        *reinterpret_cast<uint32_t*>(dst + lane * 2) = *reinterpret_cast<uint32_t*>(ov);
-    } else if constexpr (EPL == 4) {
-        *reinterpret_cast<uint2*>(dst + lane * 4) = *reinterpret_cast<uint2*>(ov);
-    } else {
-        *reinterpret_cast<uint4*>(dst + lane * 8) = *reinterpret_cast<uint4*>(ov);
+        for (int e = 0; e < EPL; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], r), __bfloat162float(gv[e]));
+
+        __nv_bfloat16 ov[EPL];
+        if (rope) {
+            const bool first_half = lane < 16;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                const float other = __shfl_xor_sync(FULL_MASK, y[e], 16);
+                const int j = (lane * EPL + e) & (D / 2 - 1);
+                const float c = cs[j], s = sn[j];
+                const float o = first_half ? __fsub_rn(__fmul_rn(y[e], c), __fmul_rn(other, s))
+                                           : __fadd_rn(__fmul_rn(y[e], c), __fmul_rn(other, s));
+                ov[e] = __float2bfloat16_rn(o);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) ov[e] = __float2bfloat16_rn(y[e]);
+        }
+        *(reinterpret_cast<Lane*>(dst) + lane) = *reinterpret_cast<Lane*>(ov);
     }
 }
 
@@ -111,16 +115,21 @@ template <int D>
 int qk_launch(const void* q_in, void* q_out, const void* k_in, void* k_out, const void* gq,
               const void* gk, const int32_t* pos, const float* inv_freq, int64_t T, int Hq,
               int Hkv, int64_t qs, int64_t ks, float eps, cudaStream_t st) {
-    constexpr int HPC = 8;
+    constexpr int HPC = 8, MAXW = 9;
     const int heads = Hq + Hkv;
-    const int groups = (heads + HPC - 1) / HPC;
+    const int per_warp = (heads + HPC - 1) / HPC;
+    // Decode batches: one head per warp over more CTAs; otherwise one CTA per token (up to
+    // HPC*MAXW heads), so the token's (cos, sin) pairs are computed once.
+    const bool spread = T * per_warp <= 4LL * device_sm_count();
+    const int hpw = spread ? 1 : std::min(per_warp, MAXW);
+    const int groups = (heads + HPC * hpw - 1) / (HPC * hpw);
     const int64_t ctas = T * groups;
     if (ctas > (int64_t)INT32_MAX) return KB_ERR_TOO_LARGE;
-    return launch(qk_norm_rope_kernel<D, HPC>, dim3((unsigned)ctas), dim3(HPC * 32), 0, st,
+    return launch(qk_norm_rope_kernel<D, HPC, MAXW>, dim3((unsigned)ctas), dim3(HPC * 32), 0, st,
                   static_cast<const __nv_bfloat16*>(q_in), static_cast<__nv_bfloat16*>(q_out),
                   static_cast<const __nv_bfloat16*>(k_in), static_cast<__nv_bfloat16*>(k_out),
                   static_cast<const __nv_bfloat16*>(gq), static_cast<const __nv_bfloat16*>(gk),
-                  pos, inv_freq, T, Hq, Hkv, qs, ks, eps, groups);
+                  pos, inv_freq, T, Hq, Hkv, qs, ks, eps, groups, hpw);
 }
 
 inline bool aligned_to(const void* p, unsigned a) {

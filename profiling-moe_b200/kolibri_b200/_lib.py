@@ -19,8 +19,10 @@ KB_ERR_WORKSPACE = -4
 KB_ERR_TOO_LARGE = -5
 KB_ERR_SCRATCH_LIMIT = -6
 KB_NOALLOC_REZERO = 1
-KB_WS_MAPS, KB_WS_CHAIN, KB_WS_NOALLOC = 0, 1, 2
-KB_WS_CLEAN, KB_WS_TIMEOUT, KB_WS_MISALIGNED = 0, 1, 2
+KB_WS_MAPS, KB_WS_CHAIN, KB_WS_NOALLOC, KB_WS_EP = 0, 1, 2, 3
+KB_WS_CLEAN, KB_WS_TIMEOUT, KB_WS_MISALIGNED, KB_WS_CAPACITY = 0, 1, 2, 3
+KB_MAX_RANKS = 8
+KB_IPC_HANDLE_BYTES = 64
 
 KB_BF16, KB_F16, KB_F32 = 0, 1, 2
 KB_MAPS_AUTO, KB_MAPS_SINGLE_CTA, KB_MAPS_MULTI_CTA, KB_MAPS_TWO_KERNEL = 0, 1, 2, 3
@@ -57,6 +59,18 @@ SIGNATURES = {
                                       c_void_p, c_int64, c_int64, c_float, c_int, c_void_p]),
     "kb_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                 c_int64, c_float, c_int, c_void_p]),
+    "kb_ep_buffer_bytes": (c_size_t, [c_int, c_int, c_int, c_int64, c_int64]),
+    "kb_ep_alloc": (c_int, [c_size_t, c_void_p]),
+    "kb_ep_free": (c_int, [c_void_p]),
+    "kb_ipc_export": (c_int, [c_void_p, c_void_p]),
+    "kb_ipc_import": (c_int, [c_void_p, c_void_p]),
+    "kb_ipc_close": (c_int, [c_void_p]),
+    "kb_ep_counts_allgather": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kb_ep_dispatch": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                               c_void_p]),
+    "kb_ep_recv_rows": (c_int, [c_void_p, c_void_p]),
+    "kb_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                              c_void_p, c_int, c_void_p]),
     "kb_decode_chain_workspace_bytes": (c_size_t, []),
     "kb_decode_chain": (c_int, [c_void_p, c_int] + [c_void_p] * 22 + [c_void_p, c_size_t, c_int64,
                                 c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p]),
@@ -69,6 +83,13 @@ class ChainLayer(ctypes.Structure):
                 ("g_input_ln", c_void_p), ("g_q", c_void_p), ("g_k", c_void_p),
                 ("w_gate_t", c_void_p), ("gate_bias", c_void_p), ("rnope", ctypes.c_int32),
                 ("reserved", ctypes.c_int32)]
+
+
+class EpGroup(ctypes.Structure):
+    """kb_ep_group_t: the ranks' exchange buffers as mapped in this process."""
+    _fields_ = [("world", c_int), ("rank", c_int), ("num_experts", c_int), ("top_k", c_int),
+                ("max_tokens", c_int64), ("row_bytes", c_int64),
+                ("buf", c_void_p * KB_MAX_RANKS)]
 
 
 class KolibriError(RuntimeError):

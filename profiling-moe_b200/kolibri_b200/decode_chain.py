@@ -13,6 +13,10 @@ full attention without RoPE).  Per layer i, on one stream:
   4. router + maps      top-6 of logits + bias, sigmoid weights, counts/offsets/p2u/u2p
                         (R2_moe_prologue, :240-246)
   5. expansion          permuted[r] = moe_in[p2u[r] % T]            (R2, optional)
+     or, token-sharded over ranks (ep=PeerExpertParallel), the expert-parallel exchange:
+                        count all-gather, dispatch of the routed rows to their owners,
+                        identity experts, combine back and finalize, whose output is the
+                        layer's moe_out (finalize :259-262)
   6. post-MoE + next    r = h + RMSNorm(moe_out)*g_post_ffn ; nxt = RMSNorm(r)*g_input_ln
                         (R3_post_moe_norm :264-266 fused with the next layer's
                         input_layernorm :222-227)
@@ -77,10 +81,14 @@ class DecodeChain:
                  seed: int = 5, expansion: bool = True, gate_gemm: bool = True,
                  H: int = wl.HIDDEN, Hq: int = wl.HQ, Hkv: int = wl.HKV, D: int = wl.HEAD_DIM,
                  E: int = wl.NUM_EXPERTS, K: int = wl.TOP_K, eps: float = wl.EPS,
-                 theta: float = wl.ROPE_THETA):
+                 theta: float = wl.ROPE_THETA, ep=None):
         self.T, self.H, self.Hq, self.Hkv, self.D, self.E, self.K = T, H, Hq, Hkv, D, E, K
         self.eps, self.layers, self.device = float(eps), layers, device
-        self.expansion, self.gate_gemm = expansion, gate_gemm
+        self.expansion, self.gate_gemm = expansion and ep is None, gate_gemm
+        self.ep = ep
+        if ep is not None and (ep.H != H or ep.E != E or ep.K != K or
+                               T > ep.pg.max_tokens or ep.dtype != torch.bfloat16):
+            raise ValueError("the expert-parallel group does not match the chain's shapes")
         self.lib = _lib.load()
         g = torch.Generator(device=device).manual_seed(seed)
         bf = torch.bfloat16
@@ -112,7 +120,8 @@ class DecodeChain:
         self.offsets = torch.empty(E + 1, dtype=torch.int64, device=device)
         self.p2u = torch.empty(T * K, dtype=torch.int32, device=device)
         self.u2p = torch.empty(T * K, dtype=torch.int32, device=device)
-        self.permuted = torch.empty(T * K, H, dtype=bf, device=device) if expansion else None
+        self.permuted = torch.empty(T * K, H, dtype=bf, device=device) if self.expansion else None
+        self.moe_out_ep = torch.empty(T, H, dtype=bf, device=device) if ep is not None else None
         self.ws_bytes = int(self.lib.kb_router_maps_workspace_bytes(T, E, K))
         self.ws = torch.zeros(max(self.ws_bytes, 256), dtype=torch.uint8, device=device)
         self.inv_freq = ops.rope_inv_freq(theta, D, device)
@@ -122,7 +131,8 @@ class DecodeChain:
     def launches_per_layer(self) -> int:
         """Kernels of this library launched per layer (the cuBLAS GEMM and cast excluded)."""
         _, launches, _ = self._describe()
-        return 3 + launches + (1 if self.expansion else 0)
+        # the exchange: count all-gather, dispatch, combine send + finalize
+        return 3 + launches + (1 if self.expansion else 0) + (4 if self.ep is not None else 0)
 
     def _describe(self):
         import ctypes
@@ -184,14 +194,33 @@ class DecodeChain:
                     if record:
                         record(i, "expansion", dict(x=self.moe_in, p2u=self.p2u,
                                                     permuted=self.permuted))
+                moe_out = self.moe_out
+                if self.ep is not None:
+                    ep = self.ep
+                    _lib.check(lib.kb_ep_counts_allgather(ep.pg.addr, self.counts.data_ptr(),
+                                                          ep.gathered.data_ptr(), st),
+                               "kb_ep_counts_allgather")
+                    _lib.check(lib.kb_ep_dispatch(ep.pg.addr, self.moe_in.data_ptr(), T,
+                                                  self.p2u.data_ptr(), ep.gathered.data_ptr(),
+                                                  ep.recv_offsets.data_ptr(), st),
+                               "kb_ep_dispatch")
+                    # identity experts: the owner returns the rows it received
+                    _lib.check(lib.kb_ep_combine(ep.pg.addr, ep.rows.data_ptr(),
+                                                 ep.gathered.data_ptr(), T, self.u2p.data_ptr(),
+                                                 self.w.data_ptr(), self.moe_out_ep.data_ptr(),
+                                                 bf16, st), "kb_ep_combine")
+                    moe_out = self.moe_out_ep
+                    if record:
+                        record(i, "ep", dict(x=self.moe_in, u2p=self.u2p, w=self.w,
+                                             p2u=self.p2u, out=self.moe_out_ep))
                 if record:
                     h_in = self.h.clone()
                 _lib.check(lib.kb_residual_norm_pair(
-                    self.moe_out.data_ptr(), self.h.data_ptr(), L.g_post_ffn.data_ptr(),
+                    moe_out.data_ptr(), self.h.data_ptr(), L.g_post_ffn.data_ptr(),
                     L.g_input_ln.data_ptr(), self.r.data_ptr(), self.nxt.data_ptr(), T, H,
                     self.eps, bf16, st), "kb_residual_norm_pair")
                 if record:
-                    record(i, "post_moe", dict(a=self.moe_out, residual=h_in, g1=L.g_post_ffn,
+                    record(i, "post_moe", dict(a=moe_out, residual=h_in, g1=L.g_post_ffn,
                                                g2=L.g_input_ln, sum=self.r, norm=self.nxt))
 
     # ------------------------------------------------------------------------------------

@@ -45,3 +45,45 @@ def assert_chain_close(out: torch.Tensor, ref: torch.Tensor, inter: torch.Tensor
     assert not bool(bad.any()), (
         f"{what}: {int(bad.sum())} of {d.numel()} elements outside the bar; "
         f"worst {float((d - allow).max()):.3g} over at {tuple(torch.nonzero(bad)[0].tolist())}")
+
+
+def bf16_ulp_dist(out: torch.Tensor, ref: torch.Tensor) -> torch.Tensor:
+    """Element-wise distance in bf16 ulps (ordered-integer distance; +0 and -0 are equal)."""
+    a = out.detach().to(torch.bfloat16).cpu().contiguous().view(torch.int16).to(torch.int32)
+    b = ref.detach().to(torch.bfloat16).cpu().contiguous().view(torch.int16).to(torch.int32)
+
+    def ordered(x):
+        return torch.where(x < 0, -(x & 0x7FFF), x)
+    return (ordered(a) - ordered(b)).abs()
+
+
+def assert_bf16_ulp(out: torch.Tensor, ref: torch.Tensor, what: str = "",
+                    inter: torch.Tensor = None, atol: float = 0.0,
+                    max_frac: float = 1e-3) -> tuple:
+    """The strict norm/RoPE bar: every element within 1 bf16 ulp of the oracle, except two
+    named, counted cases (each at most max_frac of the elements):
+      inter  the oracle's rounded bf16 intermediate (post = bf16(RMSNorm(a)*g) of
+             h = bf16(res + post)): |out - ref| <= ulp(ref) + ulp(inter), when a 1-fp32-ulp
+             difference in the rsqrt factor moved the intermediate across a rounding boundary;
+      atol   cancellation (RoPE's y1*c - y2*s near zero): |out - ref| <= atol.
+    Returns (worst ulp distance, elements accepted by the two cases)."""
+    d = bf16_ulp_dist(out, ref)
+    worst = int(d.max().item()) if d.numel() else 0
+    over = d > 1
+    n_over = int(over.sum().item())
+    if n_over == 0:
+        return worst, 0
+    o = out.detach().float().cpu()
+    r = ref.detach().float().cpu()
+    ok = torch.zeros_like(over)
+    if inter is not None:
+        ok |= (o - r).abs() <= bf16_ulp(r) + bf16_ulp(inter)
+    if atol > 0:
+        ok |= (o - r).abs() <= atol
+    bad = over & ~ok
+    assert not bool(bad.any()), (
+        f"{what}: {int(bad.sum())} elements beyond 1 bf16 ulp outside the named cases "
+        f"(worst {worst} ulp)")
+    assert n_over <= max(1, int(max_frac * d.numel())), (
+        f"{what}: {n_over} of {d.numel()} elements beyond 1 ulp (worst {worst} ulp)")
+    return worst, n_over

@@ -103,3 +103,50 @@ def test_product_never_imports_oracle():
     for p in pkg.rglob("*.py"):
         src = p.read_text()
         assert not re.search(r"^\s*(from|import)\s+oracle\b", src, re.M), p
+
+
+def _ep_group(world=2, rank=0, E=384, K=6, max_tokens=64, row_bytes=12288, bufs=None):
+    import ctypes
+    if bufs is None:
+        bufs = [0x100000 * (q + 1) for q in range(min(world, _lib.KB_MAX_RANKS))]  # fakes
+    arr = (ctypes.c_void_p * _lib.KB_MAX_RANKS)(*(bufs + [None] * (_lib.KB_MAX_RANKS - len(bufs))))
+    g = _lib.EpGroup(world, rank, E, K, max_tokens, row_bytes, arr)
+    return g, ctypes.addressof(g)
+
+
+def test_ep_host_validation_without_gpu():
+    """kb_ep_* reject a bad group or bad arguments before any CUDA call."""
+    lib = _lib.load()
+    g, a = _ep_group(world=9)
+    assert lib.kb_ep_counts_allgather(a, 16, 16, None) == _lib.KB_ERR_INVALID_ARG
+    g, a = _ep_group(world=2, rank=2)
+    assert lib.kb_ep_counts_allgather(a, 16, 16, None) == _lib.KB_ERR_INVALID_ARG
+    g, a = _ep_group(world=3, E=384 + 1)                     # E not a multiple of N
+    assert lib.kb_ep_counts_allgather(a, 16, 16, None) == _lib.KB_ERR_UNSUPPORTED
+    g, a = _ep_group(row_bytes=12290)
+    assert lib.kb_ep_dispatch(a, 16, 4, 16, 16, 16, None) == _lib.KB_ERR_ALIGNMENT
+    g, a = _ep_group(bufs=[0x100000, 0x100008])              # peer buffer not 256-aligned
+    assert lib.kb_ep_dispatch(a, 16, 4, 16, 16, 16, None) == _lib.KB_ERR_ALIGNMENT
+    g, a = _ep_group(bufs=[0x100000, 0])
+    assert lib.kb_ep_combine(a, 16, 16, 4, 16, 16, 16, _lib.KB_BF16, None) == _lib.KB_ERR_INVALID_ARG
+    g, a = _ep_group(max_tokens=64)
+    assert lib.kb_ep_dispatch(a, 16, 65, 16, 16, 16, None) == _lib.KB_ERR_INVALID_ARG   # T > max
+    assert lib.kb_ep_dispatch(a, 24, 4, 16, 16, 16, None) == _lib.KB_ERR_ALIGNMENT      # x
+    assert lib.kb_ep_combine(a, 16, 16, 4, 16, 16, 16, 9, None) == _lib.KB_ERR_UNSUPPORTED
+    assert lib.kb_ep_counts_allgather(None, 16, 16, None) == _lib.KB_ERR_INVALID_ARG
+    g, a = _ep_group(world=8, max_tokens=1 << 26)             # N*T*K overflows int32
+    assert lib.kb_ep_counts_allgather(a, 16, 16, None) == _lib.KB_ERR_TOO_LARGE
+    assert lib.kb_ep_alloc(0, None) == _lib.KB_ERR_INVALID_ARG
+    assert lib.kb_ipc_export(None, None) == _lib.KB_ERR_INVALID_ARG
+
+
+def test_ep_buffer_bytes():
+    """One rank's buffer: control + tagged counts, N*T*K received rows, T*K returned rows."""
+    lib = _lib.load()
+    assert lib.kb_ep_buffer_bytes(0, 384, 6, 64, 16) == 0
+    assert lib.kb_ep_buffer_bytes(9, 384, 6, 64, 16) == 0
+    for N, T in ((1, 1), (2, 512), (8, 4096)):
+        b = lib.kb_ep_buffer_bytes(N, 384, 6, T, 12288)
+        rows = N * T * 6 + T * 6
+        assert rows * 12288 <= b <= rows * 12288 + 2 * 8 * 384 * 8 + 4096
+        assert b % 256 == 0

@@ -59,6 +59,18 @@ def _worker(rank, world, port, T, E, K, H, q):
         assert bool((grouped_exp[1:] >= grouped_exp[:-1]).all())
         assert torch.equal(torch.bincount(grouped_exp.long(), minlength=Er).cumsum(0),
                            d.expert_offsets[1:])
+        # the closed-form placement of the peer-memory kernels reproduces the grouping
+        ids_l, _, counts, _, p2u, _ = OracleOps(E).router_maps(logits, bias, K)
+        permuted = orc.expansion_ref(x, np.asarray(p2u))
+        all_counts = [torch.empty_like(counts) for _ in range(world)]
+        dist.all_gather(all_counts, counts)
+        all_perm = [torch.empty_like(permuted) for _ in range(world)]
+        dist.all_gather(all_perm, permuted)
+        grouped, dest = orc.ep_placement_ref(torch.stack(all_counts).numpy(), world)
+        assert len(grouped[rank]) == d.rows.shape[0]
+        for gpos, (sender, i) in enumerate(grouped[rank]):
+            assert torch.equal(d.rows[gpos], all_perm[sender][i])
+            assert dest[sender][i] == (rank, gpos)
         out = ep.combine(d, d.rows)           # identity experts
         ids, w = orc.router_ref(logits, bias, k=K)
         ref = x * w.sum(-1, keepdim=True)

@@ -21,10 +21,12 @@ def _cpu(t):
     return None if t is None else t.detach().cpu()
 
 
-def make_checker(seen):
+def make_checker(seen, layers_to_check=None):
     def check(i, stage, t):
-        c = {k: _cpu(v) for k, v in t.items()}
         seen.append((i, stage))
+        if layers_to_check is not None and i not in layers_to_check:
+            return
+        c = {k: _cpu(v) for k, v in t.items()}
         if stage in ("sandwich", "post_moe"):
             rs, rn = (orc.sandwich_ref if stage == "sandwich" else orc.post_moe_pre_attn_ref)(
                 c["a"], c["residual"], c["g1"], c["g2"], eps=wl.EPS)
@@ -66,6 +68,19 @@ def test_chain_stages_match_oracle(T):
     assert len(seen) == 5 * 6
 
 
+@pytest.mark.parametrize("T", [256, 8192])
+def test_chain_stages_benchmark_sizes(T):
+    """The stage path at the benchmark's larger batches: every stage of the first and of the
+    last layer (the RNoPE layer) checked against the oracle on the inputs it received."""
+    dev = torch.device("cuda")
+    layers = dc.make_layers(5, dev)
+    chain = dc.DecodeChain(T, layers, dev)
+    seen = []
+    chain.run_layers(torch.cuda.current_stream(), record=make_checker(seen, {0, 4}))
+    torch.cuda.synchronize()
+    assert len(seen) == 5 * 6
+
+
 def test_chain_graph_replay_matches_eager():
     dev = torch.device("cuda")
     layers = dc.make_layers(10, dev)
@@ -95,14 +110,14 @@ def test_chain_without_gate_gemm():
     assert chain.launches_per_layer() == 4
 
 
-@pytest.mark.parametrize("T", [1, 2, 4])
-def test_decode_chain_kernel_matches_stages(T):
-    """kb_decode_chain (one launch for all layers) against the stage-by-stage path: the
-    routing-independent state is bit-identical, every layer's logits agree with cuBLAS to
-    bf16 rounding and with the CPU oracle, and the last layer's router, maps and expansion
-    match the oracle on the kernel's own logits."""
+@pytest.mark.parametrize("T,n_layers", [(1, 5), (2, 5), (4, 5), (1, 50), (4, 50)])
+def test_decode_chain_kernel_matches_stages(T, n_layers):
+    """kb_decode_chain (one launch for all layers) against the stage-by-stage path, up to the
+    benchmark's 50 layers: the routing-independent state is bit-identical, every layer's
+    logits agree with cuBLAS to bf16 rounding and with the CPU oracle, and the last layer's
+    router, maps and expansion match the oracle on the kernel's own logits."""
     dev = torch.device("cuda")
-    layers = dc.make_layers(5, dev)
+    layers = dc.make_layers(n_layers, dev)
     chain = dc.DecodeChain(T, layers, dev)
     s = torch.cuda.Stream()
     ref_logits = []
@@ -115,7 +130,7 @@ def test_decode_chain_kernel_matches_stages(T):
     ref = {n: getattr(chain, n).clone() for n in ("r", "nxt", "h", "moe_in", "q_out", "k_out")}
     for n in ("r", "nxt", "h", "moe_in", "q_out", "k_out", "ids", "logits", "p2u"):
         getattr(chain, n).zero_()
-    trace = torch.full((5, T, wl.NUM_EXPERTS), float("nan"), device=dev)
+    trace = torch.full((n_layers, T, wl.NUM_EXPERTS), float("nan"), device=dev)
     chain.run_mega(s, trace=trace)
     chain.run_mega(s)            # a second call on the same workspace
     torch.cuda.synchronize()
@@ -196,3 +211,42 @@ def test_decode_chain_kernel_routing_ties_and_small_E(case, T):
     assert torch.equal(chain.permuted.cpu(), orc.expansion_ref(chain.moe_in.cpu(), rp2u))
     if case == "all_equal":
         assert rid.tolist() == [list(range(K))] * T
+
+
+@pytest.mark.parametrize("T", [1, 32, 256])
+def test_chain_with_expert_parallel_exchange(T):
+    """The token-sharded layer on one rank: the exchange stage's MoE output equals the one-GPU
+    finalize(expand(moe_in)) of the layer's own routing bit for bit, every other stage matches
+    the oracle, and the CUDA-graph replay equals the eager run."""
+    from kolibri_b200 import ops
+    from kolibri_b200.ep import PeerExpertParallel
+    dev = torch.device("cuda")
+    layers = dc.make_layers(5, dev)
+    ep = PeerExpertParallel(wl.NUM_EXPERTS, wl.TOP_K, wl.HIDDEN, max_tokens=T, device=dev)
+    try:
+        chain = dc.DecodeChain(T, layers, dev, ep=ep)
+        seen = []
+        check = make_checker(seen)
+
+        def rec(i, stage, t):
+            if stage == "ep":
+                seen.append((i, stage))
+                ref = ops.moe_finalize(ops.expand_rows(t["x"], t["p2u"]), t["u2p"], t["w"])
+                assert torch.equal(t["out"], ref), f"layer {i} exchange"
+            else:
+                check(i, stage, t)
+        s = torch.cuda.Stream()
+        chain.run_layers(s, record=rec)
+        torch.cuda.synchronize()
+        assert len(seen) == 5 * 6
+        eager = [chain.r.clone(), chain.nxt.clone(), chain.moe_out_ep.clone()]
+        g = chain.capture(s)
+        chain.r.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for a, b in zip(eager, [chain.r, chain.nxt, chain.moe_out_ep]):
+            assert torch.equal(a, b)
+        assert ep.pg.status() == 0
+        del g
+    finally:
+        ep.close()

@@ -1,0 +1,158 @@
+"""The expert-parallel exchange on peer memory (kb_ep_counts_allgather, kb_ep_dispatch,
+kb_ep_combine) against the one-GPU path and against the collective exchange
+(ExpertParallel over NCCL):
+
+  * one rank (no process group): the received rows are the expansion of x by the maps,
+    segments = the expert offsets, and combine(dispatch(x)) with identity experts equals
+    finalize(expand(x)) bit for bit, over several calls (epochs) and inside a CUDA graph;
+  * two GPUs (skipped with fewer): rows, segments and combine output bit-identical to
+    ExpertParallel's, and combine(dispatch(x)) = finalize(expand(x)) of each rank's routing,
+    with a different token count on each rank and an empty rank.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+E, K, H = 384, 6, 6144
+
+
+def _inputs(T, seed, dev):
+    from kolibri_b200 import workloads as wl
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
+    logits, bias = wl.router_inputs(T, seed=seed + 1)
+    return x, logits.to(dev), bias.to(dev)
+
+
+def _one_gpu_reference(x, logits, bias):
+    from kolibri_b200 import ops
+    ids, w, counts, offsets, p2u, u2p = ops.router_maps(logits, bias, k=K)
+    permuted = ops.expand_rows(x, p2u)
+    return counts, offsets, permuted, ops.moe_finalize(permuted, u2p, w)
+
+
+@pytest.mark.parametrize("T", [1, 4, 100, 2048])
+def test_single_rank_exchange_matches_local_path(T):
+    from kolibri_b200.ep import PeerExpertParallel
+    dev = torch.device("cuda")
+    ep = PeerExpertParallel(E, K, H, max_tokens=2048, device=dev)
+    try:
+        for call in range(3):                      # successive epochs on one buffer
+            x, logits, bias = _inputs(T, 10 * call + T, dev)
+            d = ep.dispatch(x, logits, bias)
+            out = ep.combine(d, d.rows)
+            counts, offsets, permuted, ref = _one_gpu_reference(x, logits, bias)
+            torch.cuda.synchronize()
+            assert torch.equal(d.gathered[0], counts)
+            assert torch.equal(d.expert_offsets, offsets)
+            R = d.num_rows()
+            assert R == T * K
+            assert torch.equal(d.rows[:R], permuted)
+            assert torch.equal(out, ref)
+        assert ep.pg.status() == 0
+    finally:
+        ep.close()
+
+
+def test_single_rank_exchange_in_cuda_graph():
+    from kolibri_b200.ep import PeerExpertParallel
+    from kolibri_b200 import ops
+    dev = torch.device("cuda")
+    T = 256
+    ep = PeerExpertParallel(E, K, H, max_tokens=T, device=dev)
+    try:
+        x, logits, bias = _inputs(T, 3, dev)
+        ops.reserve_workspace(T)
+        s = torch.cuda.Stream()
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        with torch.cuda.stream(s):
+            d = ep.dispatch(x, logits, bias)
+            ep.combine(d, d.rows, out)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            d = ep.dispatch(x, logits, bias)
+            ep.combine(d, d.rows, out)
+        out.zero_()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        _, _, _, ref = _one_gpu_reference(x, logits, bias)
+        assert torch.equal(out, ref)
+        assert ep.pg.status() == 0
+        del g
+    finally:
+        ep.close()
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    ep = None
+    try:
+        from kolibri_b200.ep import ExpertParallel, PeerExpertParallel
+        ep = PeerExpertParallel(E, K, H, max_tokens=1024, device=dev)
+        ref_ep = ExpertParallel(E, K)
+        ok = True
+        # token counts per call and rank: equal, different, one rank empty
+        for call, Ts in enumerate(([512, 512], [1024, 300], [0, 700], [1, 1])):
+            T = Ts[rank]
+            x, logits, bias = _inputs(T, 100 * call + rank, dev)
+            d = ep.dispatch(x, logits, bias)
+            out = ep.combine(d, d.rows)
+            if T > 0:
+                _, _, _, ref = _one_gpu_reference(x, logits, bias)
+            else:
+                ref = torch.empty(0, H, dtype=torch.bfloat16, device=dev)
+            # the collective path on the same routing (both ranks take part, or neither)
+            r = ref_ep.dispatch(x, logits, bias) if min(Ts) > 0 else None
+            torch.cuda.synchronize()
+            R = d.num_rows()
+            ok &= torch.equal(out, ref)
+            if r is not None:
+                ok &= R == r.rows.shape[0]
+                ok &= torch.equal(d.rows[:R], r.rows)
+                ok &= torch.equal(d.expert_offsets, r.expert_offsets)
+                ok &= torch.equal(ref_ep.combine(r, r.rows), ref)
+        ok &= ep.pg.status() == 0
+        q.put((rank, bool(ok)))
+    except Exception as e:  # report, then leave the group cleanly
+        q.put((rank, repr(e)))
+    finally:
+        if ep is not None:
+            ep.close()
+        dist.destroy_process_group()
+
+
+def _run_two(target):
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
+def test_peer_exchange_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run_two(_worker)
+    assert all(r[1] is True for r in res), res

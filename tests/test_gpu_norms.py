@@ -9,7 +9,7 @@ import torch
 from conftest import GOLDEN
 import torch.nn.functional as F
 
-from kb_testutil import assert_bf16_close, assert_chain_close
+from kb_testutil import assert_bf16_close, assert_bf16_ulp, assert_chain_close
 from kolibri_b200 import ops
 from kolibri_b200 import workloads as wl
 from oracle import kolibri_oracle as orc
@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("T", [1, 64, 1024, 16384])
-def test_sandwich_and_post_moe_pair_config3(T, api):
+def test_sandwich_and_post_moe_pair_config3(T, api, record_property):
     ni = wl.norm_inputs(T, seed=3)
     c = lambda t: t.cuda()  # noqa: E731
     h, x = api.fused_sandwich_norm(c(ni.attn_out), c(ni.residual), c(ni.g_post_attn),
@@ -27,6 +27,12 @@ def test_sandwich_and_post_moe_pair_config3(T, api):
     post = F.rms_norm(ni.attn_out, (wl.HIDDEN,), ni.g_post_attn, eps=wl.EPS)
     assert_chain_close(h, rh, post, "sandwich h")
     assert_chain_close(x, rx, post, "sandwich x")
+    # Strict bar: <= 1 bf16 ulp, except counted elements explained by the rounded intermediate
+    # (the sums); each normalised output against the oracle's norm of the kernel's own sum.
+    H = wl.HIDDEN
+    rep = {"h": assert_bf16_ulp(h, rh, "sandwich h", inter=post),
+           "x": assert_bf16_ulp(x, F.rms_norm(h.cpu(), (H,), ni.g_pre_moe, eps=wl.EPS),
+                                "sandwich x on its own h")}
     # second half of config 3 on the oracle's h (so each stage is checked on its own input)
     o, n = api.fused_post_moe_pre_attn_norm(c(ni.moe_out), c(rh), c(ni.g_post_moe),
                                             c(ni.g_pre_attn), eps=wl.EPS)
@@ -34,6 +40,13 @@ def test_sandwich_and_post_moe_pair_config3(T, api):
     pm = F.rms_norm(ni.moe_out, (wl.HIDDEN,), ni.g_post_moe, eps=wl.EPS)
     assert_chain_close(o, ro, pm, "pair out")
     assert_chain_close(n, rn, pm, "pair next")
+    rep["out"] = assert_bf16_ulp(o, ro, "pair out", inter=pm)
+    rep["next"] = assert_bf16_ulp(n, F.rms_norm(o.cpu(), (H,), ni.g_pre_attn, eps=wl.EPS),
+                                  "pair next on its own out")
+    for k, (worst, named) in rep.items():   # worst ulp distance, elements of the named case
+        record_property(f"worst_ulp_{k}", worst)
+        record_property(f"named_case_{k}", named)
+    print(f"T={T} worst bf16 ulp / named-case elements: {rep}")
 
 
 def test_norms_golden_reference_eager(api):
