@@ -5,8 +5,9 @@ Step = one pass of the fused router + expert-map build (kb_router_maps) over one
 T tokens of synthetic router logits (fp32 [T, 384] ~ N(0,1), bias ~ N(0, 0.1)); T = 65536
 per GPU (the large-T configuration of the metric).  With N GPUs every rank routes its own
 T tokens and the ranks all-gather their per-expert counts (the expert-parallel exchange
-step) with kb_ep_counts_allgather, a kernel that stores into the peers' memory over
-NVLink; the work per GPU is fixed ("weak" scaling) and value = N*T / step time.
+step) inside the same kernel (kb_router_maps_allgather: its tail stores the counts into the
+peers' memory over NVLink and collects theirs); the work per GPU is fixed ("weak" scaling)
+and value = N*T / step time.
 
   value     device-resident throughput: inputs already in HBM, steps replayed from CUDA
             graphs, four rotating 100 MB input sets (together > the 126 MB L2)
@@ -68,6 +69,9 @@ def parse():
     p.add_argument("--only-T", type=int, default=0)
     p.add_argument("--no-ep", action="store_true",
                    help="skip the expert-parallel round trip")
+    p.add_argument("--exchange", choices=["fused", "separate"], default="fused",
+                   help="N > 1: count all-gather inside the router+maps kernel, or as a "
+                        "second kernel")
     return p.parse_args()
 
 
@@ -283,8 +287,10 @@ def run_reference(args):
 # ------------------------------------------------------------------------------------
 # 50-layer decode chain (replicas only: every rank times its own copy at N>1)
 # ------------------------------------------------------------------------------------
-def _time_graph(g, stream, dev, steps, warmup, world):
-    """Device time of one replay of g (CUDA events on `stream`, max over ranks), in ms."""
+def _time_graph(g, stream, dev, steps, warmup, world, pg=None):
+    """Device time of one replay of g (CUDA events on `stream`, max over ranks), in ms.  With
+    N > 1 a device-side barrier of the peer group (pg) precedes the start event, so that no
+    rank's first step waits for a rank whose host started later."""
     import torch.distributed as dist
     if world > 1:
         dist.barrier()
@@ -296,6 +302,8 @@ def _time_graph(g, stream, dev, steps, warmup, world):
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        if pg is not None and world > 1:
+            pg.barrier(stream)
         a.record(stream)
         for _ in range(steps):
             g.replay()
@@ -367,7 +375,7 @@ def decode_chain_times(dev, tokens, n_layers, stream, world=1, steps=20, warmup=
             if T in sharded:
                 ch = dc.DecodeChain(T // world, layers, dev, gate_gemm=True, ep=ep)
                 g = ch.capture(stream)
-                ms = _time_graph(g, stream, dev, max(3, steps // 2), warmup, world)
+                ms = _time_graph(g, stream, dev, max(3, steps // 2), warmup, world, ep.pg)
                 rec["ep_sharded"] = {"us_per_step": round(ms * 1e3, 2),
                                      "us_per_token": round(ms * 1e3 / T, 4),
                                      "tokens_per_rank": T // world,
@@ -453,7 +461,7 @@ def ep_round_trip(dev, world, rank, T=4096, H=HIDDEN, steps=10, warmup=3):
         with torch.cuda.graph(graph, stream=s):
             dd = pep.dispatch(x, logits, bias)
             pep.combine(dd, dd.rows, obuf)
-        ms = _time_graph(graph, s, dev, steps, warmup, world)
+        ms = _time_graph(graph, s, dev, steps, warmup, world, pep.pg)
         ok = ok and torch.equal(obuf, local) and pep.pg.status() == 0
         if world > 1:
             flag = torch.tensor([1 if ok else 0], device=dev)
@@ -539,19 +547,33 @@ def main():
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
     stream = torch.cuda.Stream(dev)
 
+    def router_maps(lg, bs, cs):
+        """One step: kb_router_maps, or with N > 1 kb_router_maps_allgather (the count
+        all-gather fused into the same kernel's tail; --exchange separate: kb_router_maps
+        followed by kb_ep_counts_allgather)."""
+        if world > 1 and args.exchange == "separate":
+            _lib.check(lib.kb_router_maps(lg.data_ptr(), bs.data_ptr(), ids.data_ptr(),
+                                          w.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
+                                          p2u.data_ptr(), u2p.data_ptr(), ws.data_ptr(), ws_bytes,
+                                          T, E, K, 0, _lib.KB_MAPS_AUTO, cs), "kb_router_maps")
+            _lib.check(lib.kb_ep_counts_allgather(counts_pg.addr, counts.data_ptr(),
+                                                  gathered.data_ptr(), cs),
+                       "kb_ep_counts_allgather")
+        elif world > 1:
+            _lib.check(lib.kb_router_maps_allgather(
+                counts_pg.addr, lg.data_ptr(), bs.data_ptr(), ids.data_ptr(), w.data_ptr(),
+                counts.data_ptr(), offsets.data_ptr(), p2u.data_ptr(), u2p.data_ptr(),
+                ws.data_ptr(), ws_bytes, T, 0, _lib.KB_MAPS_AUTO, gathered.data_ptr(), cs),
+                "kb_router_maps_allgather")
+        else:
+            _lib.check(lib.kb_router_maps(lg.data_ptr(), bs.data_ptr(), ids.data_ptr(),
+                                          w.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
+                                          p2u.data_ptr(), u2p.data_ptr(), ws.data_ptr(), ws_bytes,
+                                          T, E, K, 0, _lib.KB_MAPS_AUTO, cs), "kb_router_maps")
+
     def step(i):
         lg, bs = sets[i % nsets]
-        _lib.check(lib.kb_router_maps(lg.data_ptr(), bs.data_ptr(), ids.data_ptr(), w.data_ptr(),
-                                      counts.data_ptr(), offsets.data_ptr(), p2u.data_ptr(),
-                                      u2p.data_ptr(), ws.data_ptr(), ws_bytes, T, E, K, 0,
-                                      _lib.KB_MAPS_AUTO,
-                                      torch.cuda.current_stream(dev).cuda_stream),
-                   "kb_router_maps")
-        if world > 1:
-            _lib.check(lib.kb_ep_counts_allgather(counts_pg.addr, counts.data_ptr(),
-                                                  gathered.data_ptr(),
-                                                  torch.cuda.current_stream(dev).cuda_stream),
-                       "kb_ep_counts_allgather")
+        router_maps(lg, bs, torch.cuda.current_stream(dev).cuda_stream)
 
     # Graphs: one per input set (router+maps, and the count all-gather for N>1).
     torch.cuda.synchronize(dev)
@@ -588,7 +610,7 @@ def main():
                                     ctypes.byref(launch_c), ctypes.byref(grid_c)),
                "kb_maps_describe")
     launches_per_step = launch_c.value
-    path_name = {1: "single-CTA", 2: "persistent multi-CTA", 3: "two-kernel",
+    path_name = {1: "single-CTA", 2: "tile kernel, persistent multi-CTA", 3: "two-kernel",
                  4: "hybrid-router persistent", 5: "warp-router persistent"}[path_c.value]
 
     with torch.cuda.stream(stream):
@@ -601,6 +623,8 @@ def main():
     clocks = ClockSampler(dev)
     with clocks:
         with torch.cuda.stream(stream):
+            if world > 1:
+                counts_pg.barrier(stream)   # the ranks enter the timed region together
             start.record(stream)
             run_steps(args.steps)
             end.record(stream)
@@ -634,15 +658,7 @@ def main():
             cs = torch.cuda.current_stream(dev)
             lg_d.copy_(lg_h, non_blocking=True)
             bs_d.copy_(bs_h, non_blocking=True)
-            _lib.check(lib.kb_router_maps(lg_d.data_ptr(), bs_d.data_ptr(), ids.data_ptr(),
-                                          w.data_ptr(), counts.data_ptr(), offsets.data_ptr(),
-                                          p2u.data_ptr(), u2p.data_ptr(), ws.data_ptr(), ws_bytes,
-                                          T, E, K, 0, _lib.KB_MAPS_AUTO, cs.cuda_stream),
-                       "kb_router_maps")
-            if world > 1:
-                _lib.check(lib.kb_ep_counts_allgather(counts_pg.addr, counts.data_ptr(),
-                                                      gathered.data_ptr(), cs.cuda_stream),
-                           "kb_ep_counts_allgather")
+            router_maps(lg_d, bs_d, cs.cuda_stream)
             for o, oh in zip(outs, outs_h):
                 oh.copy_(o, non_blocking=True)
 
@@ -654,6 +670,8 @@ def main():
         if world > 1:
             dist.barrier()
         with torch.cuda.stream(stream):
+            if world > 1:
+                counts_pg.barrier(stream)
             start.record(stream)
             for _ in range(e_steps):
                 e2e_step()
@@ -718,7 +736,11 @@ def main():
                    "graph": True,
                    "steps_per_graph_replay": nsets,
                    "parallelism": f"token-sharded x{world}" + (
-                       " + per-expert count all-gather over peer memory (kb_ep_counts_allgather)"
+                       (" + per-expert count all-gather over peer memory, fused into the "
+                        "router+maps kernel (kb_router_maps_allgather)")
+                       if args.exchange == "fused" else
+                       (" + per-expert count all-gather over peer memory "
+                        "(kb_ep_counts_allgather after kb_router_maps)")
                        if world > 1 else "")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -730,7 +752,8 @@ def main():
         "kernels": kernels,
         "ep_dispatch": ep,
         "count_exchange_parity": count_parity,
-        "gpu_launches": (launches_per_step + (1 if world > 1 else 0)) * args.steps,
+        "gpu_launches": (launches_per_step + (1 if world > 1 and args.exchange == "separate"
+                                              else 0)) * args.steps,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

@@ -184,6 +184,14 @@ KB_API int kb_expert_maps_noalloc(const int32_t *ids, int32_t *counts, int64_t *
  */
 KB_API int kb_expand_rows(const void *x, void *out, const int32_t *p2u, int64_t T, int64_t rows,
                    int64_t row_bytes, kb_stream_t stream);
+/* The expansion of T*K rows together with the permuted routing weights, in one pass:
+ * out[r] = x[p2u[r] % T] and scales[r] = weights[(p2u[r] % T)*K + p2u[r] / T] (fp32 [T*K];
+ * 0 for a row past offsets[E], whose p2u is -1).  row_bytes a multiple of 16, x and out
+ * 16-byte aligned.  Replaces the permuted_scales gather of the router-dispatch entry point
+ * (kernels/cuda/router_dispatch_bindings.cpp:62-126, kernels/cuda/kolibri_router_dispatch.py:49-64). */
+KB_API int kb_expand_rows_scaled(const void *x, void *out, const int32_t *p2u,
+                                 const float *weights, float *scales, int64_t T, int K,
+                                 int64_t row_bytes, kb_stream_t stream);
 
 /* MoE finalize (combine), the consumer of the maps and weights:
  *   out[t, :] = dtype( sum_{k < K} float(expert_out[u2p[k*T + t], :]) * weights[t, k] )
@@ -354,6 +362,21 @@ KB_API int kb_ipc_close(void *buf);
  * row (two slots by epoch parity).  Replaces the ncclAllGather of counts. */
 KB_API int kb_ep_counts_allgather(const kb_ep_group_t *g, const int32_t *counts,
                                   int32_t *gathered, kb_stream_t stream);
+/* kb_router_maps on this rank's T tokens (E and K of the group) followed by
+ * kb_ep_counts_allgather of its counts, with the all-gather fused into the tail of the router +
+ * maps kernel when the tile path runs (one launch: CTA q stores the counts into rank q's buffer
+ * as soon as the expert totals are known, and the last CTA out collects every rank's row);
+ * otherwise two launches.  Outputs as kb_router_maps, plus gathered int32 [N, E]. */
+KB_API int kb_router_maps_allgather(const kb_ep_group_t *g, const float *logits,
+                                    const float *bias, int32_t *ids, float *weights,
+                                    int32_t *counts, int64_t *offsets, int32_t *p2u,
+                                    int32_t *u2p, void *workspace, size_t workspace_bytes,
+                                    int64_t T, int renorm, int mode, int32_t *gathered,
+                                    kb_stream_t stream);
+/* Device-side barrier of the group: returns (on the stream) once every rank has entered its
+ * own call, so the work queued after it starts on every GPU at about the same time (used to
+ * align the ranks before a timed region). */
+KB_API int kb_ep_barrier(const kb_ep_group_t *g, kb_stream_t stream);
 /* Sends this rank's routed rows to their owners: permuted row r (expert e, source token
  * p2u[r] % T of x [T, row_bytes]) goes straight to its final grouped row on rank e/(E/N) --
  * the expansion, the pack and the all-to-all in one pass.  recv_offsets int64 [E/N + 1]:

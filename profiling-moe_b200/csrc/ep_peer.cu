@@ -27,6 +27,7 @@
 // polls its counters with ld.acquire.sys until they reach the call's epoch.  Every call waits
 // for every rank, and a rank's next send into a buffer region happens only after the owner of
 // that region has finished reading it (see the hazard notes at each kernel).
+#include "ep_common.cuh"
 #include "finalize_math.cuh"
 #include "norm_math.cuh"
 
@@ -36,21 +37,11 @@
 namespace kb {
 namespace {
 
-constexpr int kMaxRanks = KB_MAX_RANKS;
-constexpr long long kPeerSpin = 10000000;   // polls before a peer wait gives up (~10 s)
-
-// Control words at the start of every rank's buffer.  Epochs and tickets are written only by
-// the owning rank; the arrival counters [kMaxRanks] are incremented by the peers.
-constexpr size_t kErr = 0;            // error word (KB_WS_TIMEOUT / KB_WS_CAPACITY), sticky
-constexpr size_t kCountEpoch = 4;     // completed kb_ep_counts_allgather calls
-constexpr size_t kDispEpoch = 8;      // completed kb_ep_dispatch calls
-constexpr size_t kCombEpoch = 12;     // completed kb_ep_combine calls
-constexpr size_t kDispTicket = 16;    // CTAs of the running dispatch that are done sending
-constexpr size_t kCombTicket = 20;    // CTAs of the running combine send that are done
-constexpr size_t kFinTicket = 24;     // CTAs of the running combine finalize that are done
-constexpr size_t kDispArrive = 128;   // [q]: dispatches rank q has completed into this buffer
-constexpr size_t kCombArrive = 256;   // [q]: combines owner q has completed into this buffer
-constexpr size_t kCountsOff = 512;    // uint64 [2][kMaxRanks][E] tagged count rows
+constexpr int kMaxRanks = kEpMaxRanks;
+constexpr long long kPeerSpin = kEpSpin;
+constexpr size_t kErr = kEpErr, kDispEpoch = kEpDispEpoch, kCombEpoch = kEpCombEpoch;
+constexpr size_t kDispTicket = kEpDispTicket, kCombTicket = kEpCombTicket, kFinTicket = kEpFinTicket;
+constexpr size_t kDispArrive = kEpDispArrive, kCombArrive = kEpCombArrive, kCountsOff = kEpCountsOff;
 
 constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -86,20 +77,10 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const void* p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_relaxed_sys_u64(void* p, unsigned long long v) {
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 __device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_volatile(const unsigned* p) {
-    return *reinterpret_cast<const volatile unsigned*>(p);
-}
+__device__ __forceinline__ unsigned ld_volatile(const unsigned* p) { return ep_ld_volatile(p); }
 __device__ __forceinline__ void set_err(const EpDev& g, unsigned code) {
     atomicCAS(word(g, g.rank, kErr), 0u, code);
 }
@@ -166,58 +147,29 @@ __device__ __forceinline__ void warp_copy_row(const uint4* __restrict__ src, uin
 }
 
 // ------------------------------------------------------------------------------------
-// Count all-gather: one CTA.  Slot reuse is safe: rank p writes slot s again two calls
-// later, which needs this rank's row of the call in between, which this rank sends only
-// after it has read slot s.
+// Count all-gather: one CTA (the protocol of ep_common.cuh).
 // ------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) ep_counts_kernel(EpDev g, const int32_t* __restrict__ counts,
-                                                        int32_t* __restrict__ gathered) {
+__global__ void __launch_bounds__(512) ep_counts_kernel(CountPush cp, const int32_t* __restrict__ counts) {
     pdl_wait();
     __shared__ unsigned tag_s;
     __shared__ int bad;
-    __shared__ volatile int lost;
-    const int tid = threadIdx.x, n = g.world * g.E;
-    if (tid == 0) {
-        unsigned tag = ld_volatile(word(g, g.rank, kCountEpoch)) + 1u;
-        tag_s = tag ? tag : 1u;
-        bad = ld_volatile(word(g, g.rank, kErr)) != 0u;
-        lost = 0;
+    __shared__ int sc[E_MAX];
+    if (threadIdx.x == 0) {
+        tag_s = count_push_tag(cp);
+        bad = ep_ld_volatile(reinterpret_cast<const unsigned*>(cp.buf[cp.rank] + kEpErr)) != 0u;
     }
+    for (int e = threadIdx.x; e < cp.E; e += blockDim.x) sc[e] = __ldg(counts + e);
     __syncthreads();
     if (bad) {
-        for (int i = tid; i < n; i += blockDim.x) gathered[i] = -1;
+        for (int i = threadIdx.x; i < cp.world * cp.E; i += blockDim.x) cp.gathered[i] = -1;
         return;
     }
-    const unsigned tag = tag_s;
-    const size_t slot = tag & 1u;
-    for (int i = tid; i < n; i += blockDim.x) {   // this rank's row, into every rank's buffer
-        const int q = i / g.E, e = i - q * g.E;
-        const unsigned long long v = ((unsigned long long)tag << 32) | (unsigned)__ldg(counts + e);
-        st_relaxed_sys_u64(g.buf[q] + kCountsOff + ((slot * kMaxRanks + g.rank) * g.E + e) * 8, v);
-    }
+    // this rank's row into every rank's buffer: warp group q % 4 of the CTA sends to rank q
+    const int per = blockDim.x / 4;
+    for (int q = threadIdx.x / per; q < cp.world; q += 4)
+        count_push_send(cp, sc, q, tag_s, threadIdx.x % per, per);
     pdl_launch();
-    for (int i = tid; i < n; i += blockDim.x) {   // every rank's row, from this rank's buffer
-        const int q = i / g.E, e = i - q * g.E;
-        const char* p = g.buf[g.rank] + kCountsOff + ((slot * kMaxRanks + q) * g.E + e) * 8;
-        unsigned long long v = ld_relaxed_sys_u64(p);
-        long long it = 0;
-        while ((unsigned)(v >> 32) != tag && it < g.spin && !lost) {   // one budget per call
-            __nanosleep(64);
-            v = ld_relaxed_sys_u64(p);
-            ++it;
-        }
-        if ((unsigned)(v >> 32) == tag) {
-            gathered[i] = (int32_t)(unsigned)v;
-        } else {
-            gathered[i] = -1;
-            lost = 1;
-        }
-    }
-    __syncthreads();
-    if (tid == 0) {
-        if (lost) set_err(g, KB_WS_TIMEOUT);
-        *reinterpret_cast<volatile unsigned*>(word(g, g.rank, kCountEpoch)) = tag;
-    }
+    count_push_gather(cp, tag_s);
 }
 
 // Shared tables of the row kernels, built by every CTA from gathered [N][E]:
@@ -429,6 +381,18 @@ __global__ void __launch_bounds__(512) ep_finalize_kernel(EpDev g, const int32_t
     }
 }
 
+// Device barrier of the group: one thread signals every rank, then waits for every rank's
+// signal of this call.  Work queued behind it on the stream starts on all ranks together.
+__global__ void ep_barrier_kernel(EpDev g) {
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    if (ld_volatile(word(g, g.rank, kErr)) != 0u) return;
+    const unsigned epoch = ld_volatile(word(g, g.rank, kEpBarEpoch));
+    for (int q = 0; q < g.world; ++q) red_release_sys_add(word(g, q, kEpBarArrive) + g.rank, 1u);
+    if (!wait_arrivals(g, kEpBarArrive, epoch + 1u)) set_err(g, KB_WS_TIMEOUT);
+    *reinterpret_cast<volatile unsigned*>(word(g, g.rank, kEpBarEpoch)) = epoch + 1u;
+}
+
 // ------------------------------------------------------------------------------------
 // Host side.
 // ------------------------------------------------------------------------------------
@@ -502,6 +466,19 @@ int finalize_k(const EpDev& d, const int32_t* u2p, const float* w, void* out, in
 
 size_t ep_err_offset() { return kErr; }
 
+int make_count_push(const kb_ep_group_t* g, int32_t* gathered, CountPush* cp) {
+    if (const int s = check_group(g)) return s;
+    if (!gathered) return KB_ERR_INVALID_ARG;
+    *cp = CountPush{};
+    for (int q = 0; q < g->world; ++q) cp->buf[q] = static_cast<char*>(g->buf[q]);
+    cp->gathered = gathered;
+    cp->world = g->world;
+    cp->rank = g->rank;
+    cp->E = g->num_experts;
+    cp->spin = wait_limit(kEpSpin);
+    return KB_OK;
+}
+
 }  // namespace kb
 
 using namespace kb;
@@ -559,10 +536,11 @@ extern "C" int kb_ipc_close(void* buf) {
 
 extern "C" int kb_ep_counts_allgather(const kb_ep_group_t* g, const int32_t* counts,
                                       int32_t* gathered, kb_stream_t stream) {
-    if (const int s = check_group(g)) return s;
-    if (!counts || !gathered) return KB_ERR_INVALID_ARG;
+    CountPush cp;
+    if (const int s = make_count_push(g, gathered, &cp)) return s;
+    if (!counts) return KB_ERR_INVALID_ARG;
     return launch(ep_counts_kernel, dim3(1), dim3(512), 0, static_cast<cudaStream_t>(stream),
-                  make_dev(g), counts, gathered);
+                  cp, counts);
 }
 
 extern "C" int kb_ep_dispatch(const kb_ep_group_t* g, const void* x, int64_t T, const int32_t* p2u,
@@ -609,4 +587,10 @@ extern "C" int kb_ep_combine(const kb_ep_group_t* g, const void* expert_out, con
         case KB_F16: return finalize_k<__half>(d, u2p, weights, out, T, H, st);
         default: return finalize_k<float>(d, u2p, weights, out, T, H, st);
     }
+}
+
+extern "C" int kb_ep_barrier(const kb_ep_group_t* g, kb_stream_t stream) {
+    if (const int s = check_group(g)) return s;
+    return launch(ep_barrier_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+                  make_dev(g));
 }

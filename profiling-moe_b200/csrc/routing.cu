@@ -27,6 +27,7 @@
 //  * Small T: one CTA does everything in shared memory.  A two-kernel variant (tile
 //    histograms, last-arriving CTA folds super-tiles, one CTA per super-tile scatters) remains
 //    as the path for shapes the persistent kernel cannot hold.
+#include "ep_common.cuh"
 #include "kb_common.cuh"
 #include "route_math.cuh"
 
@@ -528,6 +529,7 @@ struct PersistWs {
     int* rowhist;    // [grid][E] per-CTA histograms, CTA-major
     int* gsum;       // [ceil(grid/kGS)][E] histogram sums of kGS-CTA groups; zero between calls
     long long spin;  // poll limit of the bounded waits (kb_set_wait_limit)
+    CountPush cp;    // tile kernel: the count all-gather fused into its tail (cp.world == 0: off)
 };
 
 constexpr int kPW = 8;                      // warps per persistent CTA
@@ -836,6 +838,9 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     scan_experts(totsm, E, offs, scratch);
     __syncthreads();
     if (c == 0) write_offsets(offs, totsm, E, T * K, counts, offsets, p2u);
+    // Fused count all-gather: CTA q < N stores this rank's totals into rank q's buffer now,
+    // so the transfer overlaps the placement below; the last CTA out collects every rank's.
+    if (c < ws.cp.world) count_push_send(ws.cp, totsm, c, count_push_tag(ws.cp), tid, nthr);
     // Global row of CTA-sorted position lpos of expert e = offs[e] + hist[e] + lpos - loc[e].
     for (int e = tid; e < E; e += nthr) hist[e] = offs[e] + hist[e] - loc[e];
     __syncthreads();
@@ -879,6 +884,7 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     if (last) {
         for (int i = tid; i < ng * E; i += nthr) ws.gsum[i] = 0;
         if (tid == 0) atomicExch(ws.bar, 0u);
+        if (ws.cp.world > 0) count_push_gather(ws.cp, count_push_tag(ws.cp));
     }
 }
 
@@ -1701,6 +1707,7 @@ PersistWs carve_persist(void* ws, int grid, int E) {
     w.gsum = reinterpret_cast<int*>(b + kGsumOff);
     w.rowhist = reinterpret_cast<int*>(b + kScratchOff);
     w.spin = wait_limit(kSpinLimit);
+    w.cp = CountPush{};
     return w;
 }
 
@@ -2083,7 +2090,7 @@ struct MapsLaunchT {
         static int run_kt(const MapsPlan& p, const float* logits, const float* bias,
                           const int32_t* ids_in, int32_t* ids_out, float* w, int32_t* counts,
                           int64_t* offsets, int32_t* p2u, int32_t* u2p, void* ws, int64_t T, int E,
-                          int K, int renorm, cudaStream_t st) {
+                          int K, int renorm, cudaStream_t st, CountPush* push) {
             if (p.path == Path::Single) {
                 auto* kern = maps_single_kernel<VPL, VEC, ROUTE, KT>;
                 int err = allow_smem(kern, p.smem_single);
@@ -2097,10 +2104,14 @@ struct MapsLaunchT {
                     auto* kern = maps_tile_kernel<E_, (KT == 6 ? 6 : 0)>;
                     int err = allow_smem(kern, p.smem_persist);
                     if (err) return err;
+                    PersistWs pw = carve_persist(ws, p.grid, E);
+                    if (push && p.grid >= push->world) {
+                        pw.cp = *push;
+                        push->fused = 1;
+                    }
                     return launch_coop(kern, dim3(p.grid), dim3(32 * (1 + 2 * p.tnw)),
                                        p.smem_persist, st, p.tmap, logits, bias, ids_out, w, T, K,
-                                       renorm, p.tpc, p.tnw, counts, offsets, p2u, u2p,
-                                       carve_persist(ws, p.grid, E));
+                                       renorm, p.tpc, p.tnw, counts, offsets, p2u, u2p, pw);
                 }
                 if (p.path == Path::TPersistent) {
                     constexpr int E_ = 32 * VPL;
@@ -2138,7 +2149,8 @@ struct MapsLaunchT {
         static int run(const float* logits, const float* bias, const int32_t* ids_in,
                        int32_t* ids_out, float* w, int32_t* counts, int64_t* offsets,
                        int32_t* p2u, int32_t* u2p, void* ws, size_t ws_bytes, int64_t T,
-                       int E, int K, int renorm, int mode, cudaStream_t st) {
+                       int E, int K, int renorm, int mode, cudaStream_t st,
+                       CountPush* push = nullptr) {
             // The tile path's tensor copies need a 16-byte aligned logits base and the
             // driver's tensor-map encoder; without either the next path is taken.
             MapsPlan p = plan(T, E, K, mode, !ROUTE || aligned16(logits));
@@ -2153,13 +2165,13 @@ struct MapsLaunchT {
             }
             if (VEC && ROUTE && K == 6)
                 return run_kt<6>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
-                                 ws, T, E, K, renorm, st);
+                                 ws, T, E, K, renorm, st, push);
             if (p.path == Path::TPersistent ||
                 p.path == Path::Tile)  // runtime-K (K <= 8)
                 return run_kt<0>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p,
-                                 ws, T, E, K, renorm, st);
+                                 ws, T, E, K, renorm, st, push);
             return run_kt<0>(p, logits, bias, ids_in, ids_out, w, counts, offsets, p2u, u2p, ws,
-                             T, E, K, renorm, st);
+                             T, E, K, renorm, st, push);
         }
 
         // Workspace large enough for every multi-CTA path at this T.
@@ -2336,6 +2348,35 @@ extern "C" int kb_router_maps(const float* logits, const float* bias, int32_t* i
     return with_layout<RouterMaps>(E, logits, bias, nullptr, ids, weights, counts, offsets, p2u,
                                    u2p, workspace, workspace_bytes, T, E, K, renorm, mode,
                                    (cudaStream_t)stream);
+}
+
+extern "C" int kb_router_maps_allgather(const kb_ep_group_t* g, const float* logits,
+                                        const float* bias, int32_t* ids, float* weights,
+                                        int32_t* counts, int64_t* offsets, int32_t* p2u,
+                                        int32_t* u2p, void* workspace, size_t workspace_bytes,
+                                        int64_t T, int renorm, int mode, int32_t* gathered,
+                                        kb_stream_t stream) {
+    CountPush cp;
+    if (const int s = make_count_push(g, gathered, &cp)) return s;
+    if (!counts) return KB_ERR_INVALID_ARG;
+    const int E = g->num_experts, K = g->top_k;
+    int st = check_common(T, E, K);
+    if (st) return st;
+    if (mode < KB_MAPS_AUTO || mode > KB_MAPS_WARP_ROUTER) return KB_ERR_INVALID_ARG;
+    if (T > 0) {
+        if (!logits || !ids || !weights || !p2u || !offsets) return KB_ERR_INVALID_ARG;
+        if ((E % 128 == 0) && (!aligned16(logits) || (bias && !aligned16(bias))))
+            return KB_ERR_ALIGNMENT;
+        if (mode == KB_MAPS_SINGLE_CTA && T * K > kMaxSingleSel) return KB_ERR_UNSUPPORTED;
+        st = with_layout<RouterMaps>(E, logits, bias, nullptr, ids, weights, counts, offsets, p2u,
+                                     u2p, workspace, workspace_bytes, T, E, K, renorm, mode,
+                                     (cudaStream_t)stream, &cp);
+    } else {
+        st = kb_router_maps(logits, bias, ids, weights, counts, offsets, p2u, u2p, workspace,
+                            workspace_bytes, T, E, K, renorm, mode, stream);
+    }
+    if (st || cp.fused) return st;
+    return kb_ep_counts_allgather(g, counts, gathered, stream);
 }
 
 extern "C" int kb_maps_describe(int64_t T, int E, int K, int route, int mode, int* path,

@@ -1,7 +1,7 @@
 """The fused router + dispatch entry point of the reference's
 kernels/cuda/kolibri_router_dispatch.py:49-64 (binding kernels/cuda/router_dispatch_bindings.cpp:
 62-126), on the sm_100a kernels: one fused router + expert-map launch (kb_router_maps) and
-the activation expansion (kb_expand_rows).
+the activation expansion with the permuted scales (kb_expand_rows_scaled, one pass).
 
 Returns [permuted_output [T*6, H], permuted_scales fp32 [T*6], permuted_row_to_unpermuted_row
 int32 [T*6], expert_first_token_offset int64 [385]], as the reference does.  Differences from
@@ -36,7 +36,5 @@ def fused_kolibri_router_dispatch(unpermuted_input: torch.Tensor, scores_in: tor
     if unpermuted_input.dtype not in (torch.float16, torch.bfloat16):
         raise RuntimeError("Unsupported dtype: only float16 and bfloat16 are supported")
     ids, w, _, offsets, p2u, _ = ops.router_maps(scores_in, bias, k=TOP_K, inverse=False)
-    permuted_output = ops.expand_rows(unpermuted_input, p2u)
-    src = p2u.long()
-    permuted_scales = w.reshape(-1)[(src % max(T, 1)) * TOP_K + src // max(T, 1)]
+    permuted_output, permuted_scales = ops.expand_rows_scaled(unpermuted_input, p2u, w)
     return [permuted_output, permuted_scales, p2u, offsets]

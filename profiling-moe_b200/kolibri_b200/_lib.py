@@ -52,6 +52,8 @@ SIGNATURES = {
                                 c_int, c_void_p]),
     "kb_expand_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                c_void_p]),
+    "kb_expand_rows_scaled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_int64, c_int, c_int64, c_void_p]),
     "kb_qk_norm_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int64,
                                 c_int64, c_float, c_void_p]),
@@ -66,9 +68,13 @@ SIGNATURES = {
     "kb_ipc_import": (c_int, [c_void_p, c_void_p]),
     "kb_ipc_close": (c_int, [c_void_p]),
     "kb_ep_counts_allgather": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kb_router_maps_allgather": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_size_t, c_int64, c_int, c_int, c_void_p, c_void_p]),
     "kb_ep_dispatch": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                c_void_p]),
     "kb_ep_recv_rows": (c_int, [c_void_p, c_void_p]),
+    "kb_ep_barrier": (c_int, [c_void_p, c_void_p]),
     "kb_ep_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                               c_void_p, c_int, c_void_p]),
     "kb_decode_chain_workspace_bytes": (c_size_t, []),

@@ -131,8 +131,14 @@ class DecodeChain:
     def launches_per_layer(self) -> int:
         """Kernels of this library launched per layer (the cuBLAS GEMM and cast excluded)."""
         _, launches, _ = self._describe()
-        # the exchange: count all-gather, dispatch, combine send + finalize
-        return 3 + launches + (1 if self.expansion else 0) + (4 if self.ep is not None else 0)
+        # the exchange: dispatch, combine send + finalize (the count all-gather rides on the
+        # router + maps launch on its tile path, one more launch elsewhere)
+        extra = 0
+        if self.ep is not None:
+            p, _, grid = self._describe()      # the tile path reports KB_MAPS_MULTI_CTA
+            fused = p == _lib.KB_MAPS_MULTI_CTA and grid >= self.ep.world
+            extra = 3 + (0 if fused else 1)
+        return 3 + launches + (1 if self.expansion else 0) + extra
 
     def _describe(self):
         import ctypes
@@ -177,11 +183,19 @@ class DecodeChain:
                     self.logits.copy_(self.logits_bf)
                     if record:
                         record(i, "gate", dict(x=self.moe_in, w=L.w_gate_t.t(), logits=self.logits))
-                _lib.check(lib.kb_router_maps(
-                    self.logits.data_ptr(), L.gate_bias.data_ptr(), self.ids.data_ptr(),
-                    self.w.data_ptr(), self.counts.data_ptr(), self.offsets.data_ptr(),
-                    self.p2u.data_ptr(), self.u2p.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
-                    T, E, K, 0, _lib.KB_MAPS_AUTO, st), "kb_router_maps")
+                if self.ep is None:
+                    _lib.check(lib.kb_router_maps(
+                        self.logits.data_ptr(), L.gate_bias.data_ptr(), self.ids.data_ptr(),
+                        self.w.data_ptr(), self.counts.data_ptr(), self.offsets.data_ptr(),
+                        self.p2u.data_ptr(), self.u2p.data_ptr(), self.ws.data_ptr(),
+                        self.ws_bytes, T, E, K, 0, _lib.KB_MAPS_AUTO, st), "kb_router_maps")
+                else:   # the count all-gather of the exchange rides on the same launch
+                    _lib.check(lib.kb_router_maps_allgather(
+                        self.ep.pg.addr, self.logits.data_ptr(), L.gate_bias.data_ptr(),
+                        self.ids.data_ptr(), self.w.data_ptr(), self.counts.data_ptr(),
+                        self.offsets.data_ptr(), self.p2u.data_ptr(), self.u2p.data_ptr(),
+                        self.ws.data_ptr(), self.ws_bytes, T, 0, _lib.KB_MAPS_AUTO,
+                        self.ep.gathered.data_ptr(), st), "kb_router_maps_allgather")
                 if record:
                     record(i, "router_maps", dict(logits=self.logits, bias=L.gate_bias,
                                                   ids=self.ids, w=self.w, counts=self.counts,
@@ -197,9 +211,6 @@ class DecodeChain:
                 moe_out = self.moe_out
                 if self.ep is not None:
                     ep = self.ep
-                    _lib.check(lib.kb_ep_counts_allgather(ep.pg.addr, self.counts.data_ptr(),
-                                                          ep.gathered.data_ptr(), st),
-                               "kb_ep_counts_allgather")
                     _lib.check(lib.kb_ep_dispatch(ep.pg.addr, self.moe_in.data_ptr(), T,
                                                   self.p2u.data_ptr(), ep.gathered.data_ptr(),
                                                   ep.recv_offsets.data_ptr(), st),

@@ -17,7 +17,8 @@ Two implementations with the same row order and bit-identical results:
 
   PeerExpertParallel  the B200 path.  Steps 2-4 are libkolibri_b200 kernels that store into
                       the peers' exchange buffers (CUDA IPC mappings over NVLink / NVSwitch):
-                      kb_ep_counts_allgather, kb_ep_dispatch (the expansion, the pack and the
+                      kb_router_maps_allgather (router + maps with the count all-gather in the
+                      same kernel's tail), kb_ep_dispatch (the expansion, the pack and the
                       all-to-all in one pass: every row is written once, at its final grouped
                       row on the owner) and kb_ep_combine (return trip + finalize).  Nothing
                       synchronises with the host, so a layer can be captured in a CUDA graph.
@@ -236,6 +237,13 @@ class PeerGroup:
                             device=self.device)
         return t.view(dtype) if tdt != dtype else t
 
+    def barrier(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Device-side barrier (kb_ep_barrier) on `stream`: the work queued after it starts on
+        every rank together."""
+        from . import _lib
+        st = stream or torch.cuda.current_stream(self.device)
+        _lib.check(self._lib.kb_ep_barrier(self.addr, st.cuda_stream), "kb_ep_barrier")
+
     def status(self) -> int:
         """The error word of this rank's buffer (0 clean, 1 timeout, 3 capacity)."""
         import ctypes
@@ -323,8 +331,10 @@ class PeerExpertParallel:
         T = x.shape[0]
         if x.dtype != self.dtype or x.shape[1] != self.H or not x.is_contiguous():
             raise ValueError("x must be a contiguous [T, hidden] tensor of the group's dtype")
-        ids, w, counts, offsets, p2u, u2p = ops.router_maps(logits, bias, k=self.K)
-        self.counts_allgather(counts)
+        if logits.shape[1] != self.E:
+            raise ValueError(f"logits must have {self.E} columns")
+        ids, w, counts, offsets, p2u, u2p = ops.router_maps_allgather(
+            self.pg.addr, logits, bias, self.gathered, k=self.K)
         _lib.check(self.pg._lib.kb_ep_dispatch(
             self.pg.addr, x.data_ptr(), T, p2u.data_ptr(), self.gathered.data_ptr(),
             self.recv_offsets.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream),

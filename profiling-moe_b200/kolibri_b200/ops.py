@@ -19,7 +19,7 @@ __all__ = [
     "router", "expert_maps", "router_maps", "expand_rows", "qk_norm_rope", "rope_inv_freq",
     "residual_norm_pair", "add_rms_norm", "reserve_workspace", "set_pdl", "expert_maps_noalloc",
     "set_wait_limit", "workspace_status",
-    "moe_finalize",
+    "moe_finalize", "expand_rows_scaled", "router_maps_allgather",
     "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA", "KB_MAPS_TWO_KERNEL",
     "KB_MAPS_HYBRID_ROUTER", "KB_MAPS_WARP_ROUTER",
 ]
@@ -219,6 +219,28 @@ def router_maps(logits: torch.Tensor, bias: Optional[torch.Tensor] = None, k: in
     return ids, w, c, off, p2u, u2p
 
 
+def router_maps_allgather(group_addr: int, logits: torch.Tensor, bias: Optional[torch.Tensor],
+                          gathered: torch.Tensor, k: int = 6, renorm: bool = False,
+                          mode: int = KB_MAPS_AUTO):
+    """router_maps on this rank's tokens plus the all-gather of every rank's counts into
+    gathered int32 [N, E] (group_addr: address of a kb_ep_group_t, see ep.PeerGroup), fused
+    into one kernel on the tile path.  -> (ids, w, counts, offsets, p2u, u2p)."""
+    T, E = _check_logits(logits, bias)
+    dev = logits.device
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, k), dtype=torch.float32, device=dev)
+    c, off, p2u, u2p = _maps_outputs(T, E, k, dev, True, True)
+    lib = load()
+    need = lib.kb_router_maps_workspace_bytes(T, E, k)
+    ws = _workspace(need, dev) if need else None
+    check(lib.kb_router_maps_allgather(group_addr, _p(logits), _p(bias), _p(ids), _p(w), _p(c),
+                                       _p(off), _p(p2u), _p(u2p), _p(ws),
+                                       0 if ws is None else ws.numel(), T, int(bool(renorm)),
+                                       int(mode), _p(gathered), _stream(dev)),
+          "kb_router_maps_allgather")
+    return ids, w, c, off, p2u, u2p
+
+
 def expand_rows(x: torch.Tensor, p2u: torch.Tensor) -> torch.Tensor:
     """out[r] = x[p2u[r] % T] for every permuted row r (T = x.shape[0])."""
     _cuda(x, "unpermuted_input")
@@ -234,6 +256,28 @@ def expand_rows(x: torch.Tensor, p2u: torch.Tensor) -> torch.Tensor:
     check(load().kb_expand_rows(_p(x), _p(out), _p(p2u), T, rows, row_bytes,
                                 _stream(x.device)), "kb_expand_rows")
     return out
+
+
+def expand_rows_scaled(x: torch.Tensor, p2u: torch.Tensor, weights: torch.Tensor):
+    """(out, scales): out[r] = x[p2u[r] % T] and scales[r] = weights[p2u[r] % T, p2u[r] // T],
+    in one pass (weights fp32 [T, K], p2u int32 [T*K])."""
+    _cuda(x, "unpermuted_input")
+    _cuda(p2u, "permuted_row_to_unpermuted_row")
+    _cuda(weights, "weights")
+    for t, n in ((x, "unpermuted_input"), (p2u, "permuted_row_to_unpermuted_row"),
+                 (weights, "weights")):
+        _contig(t, n)
+    if p2u.dtype != torch.int32 or weights.dtype != torch.float32 or weights.dim() != 2:
+        raise ValueError("p2u must be int32 and weights float32 [T, K]")
+    T, K = weights.shape
+    if x.shape[0] != T or p2u.numel() != T * K:
+        raise ValueError("x must hold T rows and p2u T*K entries")
+    row_bytes = (x.numel() // max(T, 1)) * x.element_size()
+    out = torch.empty((T * K,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    scales = torch.empty(T * K, dtype=torch.float32, device=x.device)
+    check(load().kb_expand_rows_scaled(_p(x), _p(out), _p(p2u), _p(weights), _p(scales), T, K,
+                                       row_bytes, _stream(x.device)), "kb_expand_rows_scaled")
+    return out, scales
 
 
 def moe_finalize(expert_out: torch.Tensor, u2p: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:

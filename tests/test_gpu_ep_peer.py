@@ -7,7 +7,8 @@ kb_ep_combine) against the one-GPU path and against the collective exchange
     finalize(expand(x)) bit for bit, over several calls (epochs) and inside a CUDA graph;
   * two GPUs (skipped with fewer): rows, segments and combine output bit-identical to
     ExpertParallel's, and combine(dispatch(x)) = finalize(expand(x)) of each rank's routing,
-    with a different token count on each rank and an empty rank.
+    with a different token count on each rank and an empty rank; the fused router + maps +
+    count all-gather against NCCL's all-gather of the same counts.
 """
 from __future__ import annotations
 
@@ -91,6 +92,35 @@ def test_single_rank_exchange_in_cuda_graph():
         ep.close()
 
 
+@pytest.mark.parametrize("T", [1, 64, 4096, 65536])
+def test_router_maps_allgather_single_rank(T):
+    """kb_router_maps_allgather (fused into the tile kernel's tail at large T): the maps equal
+    kb_router_maps', and gathered[0] = counts, over successive calls."""
+    from kolibri_b200 import ops
+    from kolibri_b200.ep import PeerGroup
+    from kolibri_b200 import workloads as wl
+    dev = torch.device("cuda")
+    pg = PeerGroup(E, K, 0, 16, device=dev)
+    try:
+        gathered = torch.full((1, E), -7, dtype=torch.int32, device=dev)
+        for call in range(3):
+            logits, bias = wl.router_inputs(T, seed=50 + call)
+            logits, bias = logits.to(dev), bias.to(dev)
+            got = ops.router_maps_allgather(pg.addr, logits, bias, gathered, k=K)
+            ref = ops.router_maps(logits, bias, k=K)
+            torch.cuda.synchronize()
+            for a, b in zip(got, ref):
+                assert torch.equal(a, b)
+            assert torch.equal(gathered[0], ref[2])
+        assert pg.status() == 0
+        for _ in range(3):                       # the device barrier of a one-rank group
+            pg.barrier()
+        torch.cuda.synchronize()
+        assert pg.status() == 0
+    finally:
+        pg.close()
+
+
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
@@ -125,6 +155,22 @@ def _worker(rank, world, port, q):
                 ok &= torch.equal(d.rows[:R], r.rows)
                 ok &= torch.equal(d.expert_offsets, r.expert_offsets)
                 ok &= torch.equal(ref_ep.combine(r, r.rows), ref)
+        ok &= ep.pg.status() == 0
+        # the fused router + maps + count all-gather against NCCL's all-gather
+        from kolibri_b200 import ops
+        from kolibri_b200 import workloads as wl
+        for T in (64, 4096, 65536):
+            logits, bias = wl.router_inputs(T, seed=70 + rank)
+            logits, bias = logits.to(dev), bias.to(dev)
+            gathered = torch.empty(world, E, dtype=torch.int32, device=dev)
+            _, _, counts, *_ = ops.router_maps_allgather(ep.pg.addr, logits, bias, gathered, k=K)
+            ref = torch.empty(world, E, dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(ref, counts)
+            torch.cuda.synchronize()
+            ok &= torch.equal(gathered, ref)
+        for _ in range(5):                       # device barriers across the two GPUs
+            ep.pg.barrier()
+        torch.cuda.synchronize()
         ok &= ep.pg.status() == 0
         q.put((rank, bool(ok)))
     except Exception as e:  # report, then leave the group cleanly
