@@ -514,6 +514,13 @@ def main():
         if rank == 0:
             print(json.dumps({"decode_chain_calls": 4, "T": args.only_T or 1}), flush=True)
         return
+    if args.only_kernel == "ep_exchange":  # the expert-parallel round trip alone (profiling)
+        res = ep_round_trip(dev, world, rank, T=args.only_T or 4096, steps=3, warmup=1)
+        if rank == 0:
+            print(json.dumps({"ep_dispatch": res}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if args.only_kernel:  # one kernel of the per-kernel table alone (profiling runs)
         peak, _ = measured_peak()
         tab = kernel_table(dev, torch.cuda.Stream(dev), peak, args.only_kernel, args.only_T)

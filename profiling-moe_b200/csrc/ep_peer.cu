@@ -131,7 +131,8 @@ __device__ __forceinline__ int last_le(const int* a, int n, int v) {
     return lo;
 }
 
-// Copy one row of vpr 16-byte vectors with one warp, UNROLL vectors per lane in flight.
+// Copy one row of vpr 16-byte vectors with one warp, UNROLL vectors per lane in flight; the
+// destination is written once and not read again by this kernel (evict-first stores).
 template <int UNROLL>
 __device__ __forceinline__ void warp_copy_row(const uint4* __restrict__ src, uint4* dst,
                                               int64_t vpr, int lane) {
@@ -141,9 +142,9 @@ __device__ __forceinline__ void warp_copy_row(const uint4* __restrict__ src, uin
 #pragma unroll
         for (int i = 0; i < UNROLL; ++i) buf[i] = __ldg(src + v + 32 * i);
 #pragma unroll
-        for (int i = 0; i < UNROLL; ++i) dst[v + 32 * i] = buf[i];
+        for (int i = 0; i < UNROLL; ++i) st_stream(dst + v + 32 * i, buf[i]);
     }
-    for (; v < vpr; v += 32) dst[v] = __ldg(src + v);
+    for (; v < vpr; v += 32) st_stream(dst + v, __ldg(src + v));
 }
 
 // ------------------------------------------------------------------------------------
@@ -431,10 +432,22 @@ EpDev make_dev(const kb_ep_group_t* g) {
     return d;
 }
 
-// CTAs of the row kernels: about eight rows per CTA, at most four CTAs per SM.
+// CTAs of the row kernels: about eight rows per CTA (one per warp), at most eight CTAs of
+// 256 threads per SM (all resident at once).
 unsigned row_grid(int64_t rows) {
-    const int64_t cap = (int64_t)device_sm_count() * 4;
+    const int64_t cap = (int64_t)device_sm_count() * 8;
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, cap));
+}
+
+// Grid of the finalize: the CTAs that are resident at once (each waits for the arrivals
+// once, then walks tokens with a stride of the grid), at most one per token.
+template <typename... KArgs>
+unsigned resident_grid(void (*kern)(KArgs...), int threads, int64_t ntok) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) != cudaSuccess ||
+        per_sm <= 0)
+        per_sm = 1;
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntok, (int64_t)device_sm_count() * per_sm));
 }
 
 template <typename T, int KMAX>
@@ -442,11 +455,11 @@ int finalize_launch(const EpDev& d, const int32_t* u2p, const float* w, void* ou
                     int H, cudaStream_t st) {
     constexpr int N = 16 / sizeof(T);
     const RowShape rs = row_shape(H / N);
-    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntok, INT32_MAX));
 #define KB_EPF(V)                                                                              \
     case V:                                                                                    \
-        return launch(ep_finalize_kernel<T, V, KMAX>, dim3(grid), dim3(rs.threads), 0, st, d,   \
-                      u2p, w, static_cast<T*>(out), ntok, H);
+        return launch(ep_finalize_kernel<T, V, KMAX>,                                           \
+                      dim3(resident_grid(ep_finalize_kernel<T, V, KMAX>, rs.threads, ntok)),    \
+                      dim3(rs.threads), 0, st, d, u2p, w, static_cast<T*>(out), ntok, H);
     switch (rs.vpt) {
         KB_EPF(1) KB_EPF(2) KB_EPF(3) KB_EPF(4) KB_EPF(6) KB_EPF(8)
         default: break;
