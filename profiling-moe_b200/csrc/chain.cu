@@ -35,6 +35,7 @@
 // routing-independent output is bit-identical to the stage-by-stage path.  Every wait is
 // bounded; a wait that gives up sets the workspace error word, the CTAs leave at the end of
 // the layer, and later calls report offsets = -1 until the workspace is zero-filled again.
+#include "f32x2.cuh"
 #include "kb_common.cuh"
 #include "norm_math.cuh"
 #include "route_math.cuh"
@@ -251,44 +252,6 @@ union V8 {
     bf16 e[8];
 };
 
-// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE round-to-nearest operations per
-// instruction, the same results as the scalar __fmul_rn / __fadd_rn / fmaf).
-typedef unsigned long long f2_t;
-__device__ __forceinline__ f2_t f2_pack(float lo, float hi) {
-    f2_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(f2_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ f2_t f2_mul(f2_t a, f2_t b) {
-    f2_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
-    f2_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
-    f2_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-// bf16 pair (element 2j in the low half) -> fp32 pair, exactly.
-__device__ __forceinline__ f2_t bf2_to_f2(uint32_t u) {
-    return f2_pack(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
-}
-// fp32 pair -> bf16 pair, round to nearest even (as __float2bfloat16_rn on each).
-__device__ __forceinline__ uint32_t f2_to_bf2(f2_t v) {
-    float lo, hi;
-    f2_unpack(v, lo, hi);
-    uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
-}
 union V4 {
     uint2 u;
     bf16 e[4];

@@ -14,13 +14,25 @@
 // memory with the accurate sincosf.  At large T, hpw = ceil(heads/HPC): one CTA per token, so
 // the trigonometry runs once per token instead of once per group of HPC heads (it dominated
 // the instruction count).  At decode T, hpw = 1: the heads spread over more CTAs.
-// Products and sums use _rn intrinsics: no FMA contraction, same roundings as eager torch.
+//
+// Instruction count per head (the large-T kernel is issue-bound): the gammas are unpacked once
+// per CTA; the products run as packed f32x2 pairs (two IEEE round-to-nearest operations per
+// instruction, so the same bits as the scalar __fmul_rn / __fadd_rn); the (cos, sin) table is
+// laid out in each lane's element order with the first half's sine negated, so the rotation is
+// one uniform out = y*c + other*s' (y*c - other*s = y*c + other*(-s) exactly) read with one
+// vector load per table.  Sums of squares keep the scalar fmaf order of the reference kernel.
+#include "f32x2.cuh"
 #include "kb_common.cuh"
 
 #include <algorithm>
 #include <type_traits>
 
 namespace kb {
+
+template <int EPL> struct LaneWords;
+template <> struct LaneWords<2> { using T = uint32_t; };
+template <> struct LaneWords<4> { using T = uint2; };
+template <> struct LaneWords<8> { using T = uint4; };
 
 template <int D, int HPC, int MAXW>
 __global__ void __launch_bounds__(HPC * 32) qk_norm_rope_kernel(
@@ -30,30 +42,46 @@ __global__ void __launch_bounds__(HPC * 32) qk_norm_rope_kernel(
     const float* __restrict__ inv_freq, int64_t T, int Hq, int Hkv, int64_t qs, int64_t ks,
     float eps, int groups, int hpw) {
     constexpr int EPL = D / 32;  // elements per lane
+    constexpr int NP = EPL / 2;  // packed pairs per lane
     static_assert(EPL == 2 || EPL == 4 || EPL == 8, "D must be 64, 128 or 256");
-    using Lane = typename std::conditional<EPL == 2, uint32_t,
-                 typename std::conditional<EPL == 4, uint2, uint4>::type>::type;
+    using Lane = typename LaneWords<EPL>::T;
+    union LaneU {
+        Lane l;
+        uint32_t w[NP];
+    };
     pdl_wait();
     pdl_launch();
-    __shared__ float cs[D / 2], sn[D / 2];
+    // The rotation table in lane-element order: entry e = l*EPL + i holds cos(a_j) and
+    // -sin(a_j) (first half, e < D/2) or +sin(a_j) (second half), j = e mod D/2.
+    __shared__ __align__(16) float cs[D], sn[D];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t = blockIdx.x / groups;
     const int head0 = (int)(blockIdx.x % groups) * HPC * hpw + warp;
     const int heads = Hq + Hkv;
+    const __nv_bfloat16* qt = q_in + t * qs;
+    const __nv_bfloat16* kt = k_in + t * ks;
 
     // Issue every head's loads (and both gammas) before the trigonometry.
-    Lane xl[MAXW];
-    Lane glq = {}, glk = {};
-    if (Hq > 0) glq = __ldg(reinterpret_cast<const Lane*>(gq) + lane);
-    if (Hkv > 0) glk = __ldg(reinterpret_cast<const Lane*>(gk) + lane);
+    LaneU xl[MAXW];
 #pragma unroll
     for (int i = 0; i < MAXW; ++i) {
         const int head = head0 + i * HPC;
+        xl[i].l = Lane{};
         if (i < hpw && head < heads) {
-            const __nv_bfloat16* src = head < Hq ? q_in + t * qs + (int64_t)head * D
-                                                 : k_in + t * ks + (int64_t)(head - Hq) * D;
-            xl[i] = *(reinterpret_cast<const Lane*>(src) + lane);
+            const __nv_bfloat16* src = head < Hq ? qt + head * D : kt + (head - Hq) * D;
+            xl[i].l = *(reinterpret_cast<const Lane*>(src) + lane);
         }
+    }
+    LaneU glq, glk;
+    glq.l = Lane{};
+    glk.l = Lane{};
+    if (Hq > 0) glq.l = __ldg(reinterpret_cast<const Lane*>(gq) + lane);
+    if (Hkv > 0) glk.l = __ldg(reinterpret_cast<const Lane*>(gk) + lane);
+    f2_t gqp[NP], gkp[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        gqp[k] = bf2_to_f2(glq.w[k]);
+        gkp[k] = bf2_to_f2(glk.w[k]);
     }
     const bool rope = pos != nullptr;
     if (rope) {
@@ -62,9 +90,19 @@ __global__ void __launch_bounds__(HPC * 32) qk_norm_rope_kernel(
             float s_, c_;
             sincosf(__fmul_rn(p, __ldg(inv_freq + j)), &s_, &c_);
             cs[j] = c_;
-            sn[j] = s_;
+            sn[j] = -s_;
+            cs[j + D / 2] = c_;
+            sn[j + D / 2] = s_;
         }
         __syncthreads();
+    }
+    f2_t csp[NP], snp[NP];
+    if (rope) {
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            csp[k] = f2_pack(cs[lane * EPL + 2 * k], cs[lane * EPL + 2 * k + 1]);
+            snp[k] = f2_pack(sn[lane * EPL + 2 * k], sn[lane * EPL + 2 * k + 1]);
+        }
     }
 
 #pragma unroll
@@ -72,40 +110,31 @@ __global__ void __launch_bounds__(HPC * 32) qk_norm_rope_kernel(
         const int head = head0 + i * HPC;
         if (!(i < hpw && head < heads)) continue;
         const bool is_q = head < Hq;
-        __nv_bfloat16 xv[EPL], gv[EPL];
-        *reinterpret_cast<Lane*>(xv) = xl[i];
-        *reinterpret_cast<Lane*>(gv) = is_q ? glq : glk;
-        __nv_bfloat16* dst = is_q ? q_out + t * qs + (int64_t)head * D
-                                  : k_out + t * ks + (int64_t)(head - Hq) * D;
-        float y[EPL];
+        f2_t y[NP];
         float ss = 0.0f;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) {
-            y[e] = __bfloat162float(xv[e]);
-            ss = fmaf(y[e], y[e], ss);
+        for (int k = 0; k < NP; ++k) {
+            y[k] = bf2_to_f2(xl[i].w[k]);
+            float lo, hi;
+            f2_unpack(y[k], lo, hi);
+            ss = fmaf(lo, lo, ss);
+            ss = fmaf(hi, hi, ss);
         }
         ss = warp_sum(ss);
         const float r = 1.0f / sqrtf(ss / (float)D + eps);
+        const f2_t rr = f2_pack(r, r);
+        LaneU ov;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) y[e] = __fmul_rn(__fmul_rn(y[e], r), __bfloat162float(gv[e]));
-
-        __nv_bfloat16 ov[EPL];
-        if (rope) {
-            const bool first_half = lane < 16;
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) {
-                const float other = __shfl_xor_sync(FULL_MASK, y[e], 16);
-                const int j = (lane * EPL + e) & (D / 2 - 1);
-                const float c = cs[j], s = sn[j];
-                const float o = first_half ? __fsub_rn(__fmul_rn(y[e], c), __fmul_rn(other, s))
-                                           : __fadd_rn(__fmul_rn(y[e], c), __fmul_rn(other, s));
-                ov[e] = __float2bfloat16_rn(o);
+        for (int k = 0; k < NP; ++k) {
+            f2_t v = f2_mul(f2_mul(y[k], rr), is_q ? gqp[k] : gkp[k]);
+            if (rope) {
+                const f2_t other = (f2_t)__shfl_xor_sync(FULL_MASK, (unsigned long long)v, 16);
+                v = f2_add(f2_mul(v, csp[k]), f2_mul(other, snp[k]));
             }
-        } else {
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) ov[e] = __float2bfloat16_rn(y[e]);
+            ov.w[k] = f2_to_bf2(v);
         }
-        *(reinterpret_cast<Lane*>(dst) + lane) = *reinterpret_cast<Lane*>(ov);
+        __nv_bfloat16* dst = is_q ? q_out + t * qs + head * D : k_out + t * ks + (head - Hq) * D;
+        *(reinterpret_cast<Lane*>(dst) + lane) = ov.l;
     }
 }
 
