@@ -276,7 +276,11 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(cb["ms_per_step"], 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": f"router+expert-maps T={args.tokens} E=384 k=6 (CPU eager)"},
+        # the same workload keys as the B200 arm's config (the rest of that dict describes
+        # the device run: graph replays, L2 policy, the exchange)
+        "config": {"workload": f"fused router+expert-maps, T={args.tokens} tokens per GPU, "
+                               f"E=384, k=6", "tokens_per_gpu": args.tokens, "experts": E,
+                   "top_k": K, "implementation": "eager CPU path on the host cores"},
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": round(cb["value"], 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

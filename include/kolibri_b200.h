@@ -363,10 +363,11 @@ KB_API int kb_ipc_close(void *buf);
 KB_API int kb_ep_counts_allgather(const kb_ep_group_t *g, const int32_t *counts,
                                   int32_t *gathered, kb_stream_t stream);
 /* kb_router_maps on this rank's T tokens (E and K of the group) followed by
- * kb_ep_counts_allgather of its counts, with the all-gather fused into the tail of the router +
- * maps kernel when the tile path runs (one launch: CTA q stores the counts into rank q's buffer
- * as soon as the expert totals are known, and the last CTA out collects every rank's row);
- * otherwise two launches.  Outputs as kb_router_maps, plus gathered int32 [N, E]. */
+ * kb_ep_counts_allgather of its counts, with the all-gather fused into the router + maps kernel
+ * on its single-CTA path (decode T) and its tile path (large T): one launch, the counts leave
+ * for every rank as soon as the expert totals are known and the kernel's last CTA collects
+ * every rank's row; the other paths take two launches.  Outputs as kb_router_maps, plus
+ * gathered int32 [N, E]. */
 KB_API int kb_router_maps_allgather(const kb_ep_group_t *g, const float *logits,
                                     const float *bias, int32_t *ids, float *weights,
                                     int32_t *counts, int64_t *offsets, int32_t *p2u,

@@ -375,15 +375,18 @@ __device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bo
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c = blockIdx.x, G = gridDim.x;
     const int HH = p.Hq + p.Hkv, nh = TT * HH;
+    // Nothing in the chain reads q_out / k_out, so a CTA computes only the heads it owns
+    // (head hd belongs to CTA hd mod G): at most ceil(nh / G) of them, warp w taking its w-th.
+    const int n_own = c < nh ? (nh - c + G - 1) / G : 0;
     constexpr int QC = TT <= 2 ? kQkChunk : kQkChunk / 2;  // fewer heads at once at larger T
     bool waited = false;
     f2_t gq[2], gk[2];
-    for (int base = warp; base < nh; base += kCW * QC) {
+    for (int base = warp; base < n_own; base += kCW * QC) {
         V4 xv[QC];
         int tt[QC], hq[QC];
 #pragma unroll
         for (int cc = 0; cc < QC; ++cc) {  // clamped heads: all loads in flight at once
-            const int hd = min(base + cc * kCW, nh - 1);
+            const int hd = c + min(base + cc * kCW, n_own - 1) * G;
             const int t = TT == 1 ? 0 : (hd >= HH) + (hd >= 2 * HH) + (hd >= 3 * HH);
             tt[cc] = t;
             hq[cc] = hd - t * HH;
@@ -461,8 +464,7 @@ __device__ __forceinline__ void stage_qk(const ChainParams& p, const Smem& s, bo
         }
 #pragma unroll
         for (int cc = 0; cc < QC; ++cc) {
-            const int hd = base + cc * kCW;
-            if (hd < nh && (hd == c || hd == c + G || hd == c + 2 * G)) {  // hd mod G == c
+            if (base + cc * kCW < n_own) {  // each owned head once (the clamped ones repeat)
                 const int t = tt[cc];
                 bf16* dst = hq[cc] < p.Hq ? p.q_out + ((size_t)t * p.Hq + hq[cc]) * 128
                                           : p.k_out + ((size_t)t * p.Hkv + (hq[cc] - p.Hq)) * 128;

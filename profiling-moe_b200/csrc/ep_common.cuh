@@ -70,21 +70,36 @@ __device__ __forceinline__ char* count_slot(const CountPush& cp, int q, unsigned
 // once, where a plain store may stay in this GPU until the kernel ends, holding back a kernel
 // that goes on (or waits for the peer's row); a system-scope fence after the stores would
 // flush them too, but it stalls the writing CTA for the NVLink round trip.
+__device__ __forceinline__ bool count_push_failed(const CountPush& cp) {
+    return ep_ld_volatile(reinterpret_cast<const unsigned*>(cp.buf[cp.rank] + kEpErr)) != 0u;
+}
+
+// A group whose error word is set sends nothing (its peers' waits give up in turn).
 __device__ __forceinline__ void count_push_send(const CountPush& cp, const int* counts, int peer,
                                                 unsigned tag, int tid, int nthreads) {
+    if (count_push_failed(cp)) return;
     unsigned long long* dst = reinterpret_cast<unsigned long long*>(count_slot(cp, peer, tag, cp.rank));
     for (int e = tid; e < cp.E; e += nthreads)
         ep_exch_relaxed_sys_u64(dst + e, ((unsigned long long)tag << 32) | (unsigned)counts[e]);
 }
 
 // Whole CTA: wait for every rank's row of this call in this rank's buffer and write
-// gathered (-1 and the error word on a wait that gave up); thread 0 then advances the epoch.
+// gathered (-1 and the error word on a wait that gave up, -1 alone when the group had already
+// failed); thread 0 then advances the epoch.
 // Every thread's polls share one budget: once any wait has given up the others stop too.
 __device__ inline void count_push_gather(const CountPush& cp, unsigned tag) {
     __shared__ volatile int lost;
-    if (threadIdx.x == 0) lost = 0;
+    __shared__ int failed;
+    if (threadIdx.x == 0) {
+        lost = 0;
+        failed = count_push_failed(cp);
+    }
     __syncthreads();
     const int n = cp.world * cp.E;
+    if (failed) {   // a group whose error word is set: gathered = -1, nothing else
+        for (int i = threadIdx.x; i < n; i += blockDim.x) cp.gathered[i] = -1;
+        return;
+    }
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int q = i / cp.E, e = i - q * cp.E;
         const char* p = count_slot(cp, cp.rank, tag, q) + (size_t)e * 8;

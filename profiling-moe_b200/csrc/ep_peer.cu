@@ -247,16 +247,24 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpDev g, const uint4* 
     __syncthreads();
     pdl_launch();
     if (!bad) {
-        const int nrows = mine[g.E];
+        // The rows of each owner are one contiguous run of the permuted order.  Warp gw walks
+        // the owners starting at gw mod N, so at every moment the warps spread over all
+        // owners: NVLink to every peer and this GPU's own HBM are busy together (walking the
+        // rows in order would feed one owner at a time).
         const int64_t TK = T * g.K;
         const int warps = gridDim.x * (blockDim.x >> 5);
-        for (int r = blockIdx.x * (blockDim.x >> 5) + (tid >> 5); r < nrows; r += warps) {
-            const int64_t u = __ldg(p2u + r);
-            if (u < 0 || u >= TK) continue;
-            const int e = last_le(mine, g.E, r);
-            const int64_t dest = (int64_t)pos[e] + r;
-            uint4* dst = reinterpret_cast<uint4*>(g.buf[e / Er] + g.recv) + dest * g.vpr;
-            warp_copy_row<UNROLL>(x + (u % T) * g.vpr, dst, g.vpr, lane);
+        const int gw = blockIdx.x * (blockDim.x >> 5) + (tid >> 5);
+        for (int oo = 0; oo < g.world; ++oo) {
+            const int o = (gw + oo) % g.world;
+            const int r1 = mine[(o + 1) * Er];
+            for (int r = mine[o * Er] + gw; r < r1; r += warps) {
+                const int64_t u = __ldg(p2u + r);
+                if (u < 0 || u >= TK) continue;
+                const int e = last_le(mine, g.E, r);
+                const int64_t dest = (int64_t)pos[e] + r;
+                uint4* dst = reinterpret_cast<uint4*>(g.buf[o] + g.recv) + dest * g.vpr;
+                warp_copy_row<UNROLL>(x + (u % T) * g.vpr, dst, g.vpr, lane);
+            }
         }
     }
     // Count this CTA out; the last one signals every owner, then waits for every sender.

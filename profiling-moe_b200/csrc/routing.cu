@@ -477,7 +477,8 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
     const float* __restrict__ logits, const float* __restrict__ bias,
     const int32_t* __restrict__ ids_in, int32_t* __restrict__ ids_out, float* __restrict__ w,
     int64_t T, int E, int K, int renorm, int32_t* __restrict__ counts,
-    int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p) {
+    int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p,
+    CountPush cp) {
     pdl_wait();
     pdl_launch();
     extern __shared__ __align__(16) int smem[];
@@ -507,6 +508,14 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
     __syncthreads();
     scan_over_warps(E, whist, tot);
     __syncthreads();
+    // Fused count all-gather (kb_router_maps_allgather): the totals go to every rank now, a
+    // quarter of the CTA per destination, and the rows of the others are collected at the end.
+    if (cp.world > 0) {
+        const unsigned tag = count_push_tag(cp);
+        const int per = blockDim.x / 4;
+        for (int q = threadIdx.x / per; q < cp.world; q += 4)
+            count_push_send(cp, tot, q, tag, threadIdx.x % per, per);
+    }
     scan_experts(tot, E, offs, scratch);
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -516,6 +525,7 @@ __global__ void __launch_bounds__(1024) maps_single_kernel(
     write_offsets(offs, tot, E, n, counts, offsets, p2u);
     __syncthreads();
     rank_scatter(sel, n, 0, T, E, K, whist, p2u, u2p);
+    if (cp.world > 0) count_push_gather(cp, count_push_tag(cp));
 }
 
 // ------------------------------------------------------------------------------------
@@ -2095,8 +2105,13 @@ struct MapsLaunchT {
                 auto* kern = maps_single_kernel<VPL, VEC, ROUTE, KT>;
                 int err = allow_smem(kern, p.smem_single);
                 if (err) return err;
+                CountPush cp{};
+                if (push) {
+                    cp = *push;
+                    push->fused = 1;
+                }
                 return launch(kern, dim3(1), dim3(kSingleThreads), p.smem_single, st, logits, bias,
-                              ids_in, ids_out, w, T, E, K, renorm, counts, offsets, p2u, u2p);
+                              ids_in, ids_out, w, T, E, K, renorm, counts, offsets, p2u, u2p, cp);
             }
             if constexpr (ROUTE && VEC && 32 * VPL <= 384) {
                 if (p.path == Path::Tile) {

@@ -132,11 +132,12 @@ class DecodeChain:
         """Kernels of this library launched per layer (the cuBLAS GEMM and cast excluded)."""
         _, launches, _ = self._describe()
         # the exchange: dispatch, combine send + finalize (the count all-gather rides on the
-        # router + maps launch on its tile path, one more launch elsewhere)
+        # router + maps launch on its single-CTA and tile paths, one more launch elsewhere)
         extra = 0
         if self.ep is not None:
             p, _, grid = self._describe()      # the tile path reports KB_MAPS_MULTI_CTA
-            fused = p == _lib.KB_MAPS_MULTI_CTA and grid >= self.ep.world
+            fused = p == _lib.KB_MAPS_SINGLE_CTA or (p == _lib.KB_MAPS_MULTI_CTA and
+                                                      grid >= self.ep.world)
             extra = 3 + (0 if fused else 1)
         return 3 + launches + (1 if self.expansion else 0) + extra
 

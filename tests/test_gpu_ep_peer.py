@@ -61,6 +61,38 @@ def test_single_rank_exchange_matches_local_path(T):
         ep.close()
 
 
+@pytest.mark.parametrize("E_,K_,H_,dtype", [(256, 8, 4096, torch.bfloat16),
+                                             (128, 4, 2048, torch.float32),
+                                             (384, 6, 6144, torch.float16)])
+def test_single_rank_exchange_other_shapes(E_, K_, H_, dtype):
+    """Other expert counts, top-K, widths and dtypes: rows = the expansion, combine output =
+    the one-GPU finalize, bit for bit."""
+    from kolibri_b200 import ops
+    from kolibri_b200.ep import PeerExpertParallel
+    dev = torch.device("cuda")
+    T = 300
+    ep = PeerExpertParallel(E_, K_, H_, dtype=dtype, max_tokens=T, device=dev)
+    try:
+        g = torch.Generator().manual_seed(17)
+        x = torch.randn(T, H_, generator=g).to(dtype).to(dev)
+        logits = torch.randn(T, E_, generator=g).to(dev)
+        bias = (0.1 * torch.randn(E_, generator=g)).to(dev)
+        d = ep.dispatch(x, logits, bias)
+        out = ep.combine(d, d.rows)
+        ids, w, counts, offsets, p2u, u2p = ops.router_maps(logits, bias, k=K_)
+        permuted = ops.expand_rows(x, p2u)
+        ref = ops.moe_finalize(permuted, u2p, w)
+        torch.cuda.synchronize()
+        R = d.num_rows()
+        assert R == T * K_
+        assert torch.equal(d.expert_offsets, offsets)
+        assert torch.equal(d.rows[:R], permuted)
+        assert torch.equal(out, ref)
+        assert ep.pg.status() == 0
+    finally:
+        ep.close()
+
+
 def test_single_rank_exchange_in_cuda_graph():
     from kolibri_b200.ep import PeerExpertParallel
     from kolibri_b200 import ops
@@ -202,3 +234,56 @@ def test_peer_exchange_two_gpus():
         pytest.skip("needs two GPUs")
     res = _run_two(_worker)
     assert all(r[1] is True for r in res), res
+
+
+def test_exchange_error_word_reported_and_sticky():
+    """A pre-set error word (as a wait that gave up leaves it): the count all-gather writes
+    gathered = -1, later calls do nothing, and the status reads KB_WS_TIMEOUT."""
+    from kolibri_b200 import _lib
+    from kolibri_b200.ep import PeerExpertParallel
+    dev = torch.device("cuda")
+    ep = PeerExpertParallel(E, K, H, max_tokens=64, device=dev)
+    try:
+        x, logits, bias = _inputs(64, 5, dev)
+        d = ep.dispatch(x, logits, bias)
+        ep.combine(d, d.rows)
+        torch.cuda.synchronize()
+        assert ep.pg.status() == _lib.KB_WS_CLEAN
+        err = torch.as_tensor(_ErrWord(ep.pg._own), device=dev)
+        err.fill_(_lib.KB_WS_TIMEOUT)
+        ep.gathered.fill_(5)
+        ep.dispatch(x, logits, bias)
+        torch.cuda.synchronize()
+        assert bool((ep.gathered == -1).all())
+        assert ep.pg.status() == _lib.KB_WS_TIMEOUT
+    finally:
+        ep.close()
+
+
+def test_exchange_rejects_invalid_counts():
+    """Counts that cannot be right (negative) stop the dispatch with KB_WS_CAPACITY."""
+    from kolibri_b200 import _lib
+    from kolibri_b200.ep import PeerExpertParallel
+    dev = torch.device("cuda")
+    ep = PeerExpertParallel(E, K, H, max_tokens=64, device=dev)
+    try:
+        x, logits, bias = _inputs(64, 6, dev)
+        from kolibri_b200 import ops
+        ids, w, counts, offsets, p2u, u2p = ops.router_maps(logits, bias, k=K)
+        bad = torch.full((1, E), -3, dtype=torch.int32, device=dev)
+        _lib.check(ep.pg._lib.kb_ep_dispatch(ep.pg.addr, x.data_ptr(), 64, p2u.data_ptr(),
+                                             bad.data_ptr(), ep.recv_offsets.data_ptr(),
+                                             torch.cuda.current_stream().cuda_stream),
+                   "kb_ep_dispatch")
+        torch.cuda.synchronize()
+        assert ep.pg.status() == _lib.KB_WS_CAPACITY
+    finally:
+        ep.close()
+
+
+class _ErrWord:
+    """The 4-byte error word at the start of an exchange buffer, as a torch view."""
+
+    def __init__(self, ptr):
+        self.__cuda_array_interface__ = {"shape": (1,), "typestr": "<i4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
