@@ -72,7 +72,8 @@ KB_API int kb_version(void);
  *   kind   KB_WS_MAPS (kb_expert_maps / kb_router_maps workspace), KB_WS_CHAIN
  *          (kb_decode_chain workspace), KB_WS_NOALLOC (the static scratch of
  *          kb_expert_maps_noalloc on the current device; workspace is ignored), KB_WS_EP
- *          (a rank's expert-parallel exchange buffer, section (e) below)
+ *          (a rank's expert-parallel exchange buffer, section (e) below), KB_WS_RGEMM
+ *          (kb_router_gemm workspace)
  *   status KB_WS_CLEAN (0), KB_WS_TIMEOUT (1: a bounded wait gave up),
  *          KB_WS_MISALIGNED (2: kb_decode_chain found a layer weight pointer that is not
  *          16-byte aligned), KB_WS_CAPACITY (3: an expert-parallel exchange received more
@@ -82,7 +83,7 @@ KB_API int kb_version(void);
  * short limit makes waits give up early on purpose, so that the error path can be exercised.
  * No counterpart in the reference (its kernels report launch errors only,
  * kernels/cuda/customKolibriBuildExpertMapsKernel.cu:78-88). */
-enum { KB_WS_MAPS = 0, KB_WS_CHAIN = 1, KB_WS_NOALLOC = 2, KB_WS_EP = 3 };
+enum { KB_WS_MAPS = 0, KB_WS_CHAIN = 1, KB_WS_NOALLOC = 2, KB_WS_EP = 3, KB_WS_RGEMM = 4 };
 enum { KB_WS_CLEAN = 0, KB_WS_TIMEOUT = 1, KB_WS_MISALIGNED = 2, KB_WS_CAPACITY = 3 };
 KB_API int kb_workspace_status(const void *workspace, int kind, int *status, kb_stream_t stream);
 KB_API long long kb_set_wait_limit(long long polls);
@@ -145,6 +146,32 @@ KB_API int kb_router_maps(const float *logits, const float *bias, int32_t *ids, 
  * pointer may be NULL.  Library introspection; no counterpart in the reference. */
 KB_API int kb_maps_describe(int64_t T, int E, int K, int route, int mode, int *path,
                             int *launches, int *grid);
+
+/* (f3) Router projection on the tensor cores with the routing fused into its epilogue:
+ *   logits[t, e] = bf16(sum_h x[t, h] * w_gate[e, h]) widened to fp32 (fp32 accumulation,
+ *   one rounding: the `(x @ W_g).float()` of a bf16 GEMM), then ids / weights from those
+ *   logits exactly as kb_router (bias, top-K, sigmoid of the rounded logit, renorm option).
+ *   x       bf16 [T, H] row-major, 16-byte aligned
+ *   w_gate  bf16 [E, H] row-major (the nn.Linear layout: logits = x @ w_gate^T), 16-byte aligned
+ *   bias    fp32 [E] or NULL;  logits fp32 [T, E] or NULL (not stored)
+ *   ids     int32 [T, K] or NULL (no routing: logits only);  weights fp32 [T, K]
+ *   H % 64 == 0, E % 64 == 0, E <= 512, 1 <= K <= 8, T <= 524288 (else KB_ERR_TOO_LARGE).
+ * The workspace (kb_router_gemm_workspace_bytes(T, H, E, K), 256-byte aligned) must be
+ * zero-filled before its first use; every call leaves its counters at zero.  A bounded wait
+ * that gives up sets its error word (kb_workspace_status kind KB_WS_RGEMM); the workspace must
+ * then be zero-filled again.  The hidden dimension is split over several CTAs when T is small
+ * (their fp32 partials are summed in split order, so results do not depend on timing).
+ * Replaces the gate GEMM + router of the reference's layer: gate_gemm and R2_moe_prologue of
+ * benchmarks/11_profile_2block_e2e.py:236-246 (torch.matmul on cuBLAS, then
+ * fused_moe_prologue / the routing kernels of (a1)). */
+KB_API size_t kb_router_gemm_workspace_bytes(int64_t T, int H, int E, int K);
+KB_API int kb_router_gemm(const void *x, const void *w_gate, const float *bias, float *logits,
+                          int32_t *ids, float *weights, void *workspace, size_t workspace_bytes,
+                          int64_t T, int H, int E, int K, int renorm, kb_stream_t stream);
+/* The tile shape kb_router_gemm takes for this shape: *bn experts per CTA tile, *ks hidden
+ * splits, *grid CTAs.  Any output pointer may be NULL.  Library introspection; no counterpart
+ * in the reference. */
+KB_API int kb_router_gemm_describe(int64_t T, int H, int E, int K, int *bn, int *ks, int *grid);
 
 /* kb_expert_maps (mode KB_MAPS_AUTO, same outputs and rules) for callers that may not
  * allocate device memory: its workspace is a static 8 MiB device array inside this

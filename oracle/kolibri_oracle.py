@@ -202,6 +202,17 @@ def router_logits_ref(x: torch.Tensor, w_gate: torch.Tensor) -> torch.Tensor:
     return (x @ w_gate).float()
 
 
+def router_gemm_ref(x: torch.Tensor, w_gate_t: torch.Tensor, bias: Optional[torch.Tensor],
+                    k: int = 6, renorm: bool = False):
+    """The gate GEMM + router of benchmarks/11_profile_2block_e2e.py:241-246: logits =
+    (moe_in @ W_g).float() with W_g = w_gate_t.T, i.e. an exact product rounded once to bf16
+    (the fp64 product stands in for the exact one), then router_ref on those logits.
+    -> (ids, w, logits fp32 [T, E])."""
+    logits = (x.double() @ w_gate_t.double().t()).to(torch.bfloat16).float()
+    ids, w = router_ref(logits, bias, k=k, renorm=renorm)
+    return ids, w, logits
+
+
 def finalize_ref(expert_out: torch.Tensor, u2p, weights: torch.Tensor) -> torch.Tensor:
     """(expert_out[u2p.view(K, T)].float() * weights.float().t().unsqueeze(-1)).sum(0).to(dtype);
     slots whose u2p is negative contribute zero."""

@@ -77,12 +77,14 @@ extern "C" int kb_workspace_status(const void* workspace, int kind, int* status,
         const int st = kb::noalloc_scratch_address(&p);
         if (st) return st;
         word = static_cast<const unsigned char*>(p) + kb::maps_err_offset();
-    } else if (kind == KB_WS_MAPS || kind == KB_WS_CHAIN || kind == KB_WS_EP) {
+    } else if (kind == KB_WS_MAPS || kind == KB_WS_CHAIN || kind == KB_WS_EP ||
+               kind == KB_WS_RGEMM) {
         if (!workspace) return KB_ERR_INVALID_ARG;
         word = static_cast<const unsigned char*>(workspace) +
                (kind == KB_WS_MAPS    ? kb::maps_err_offset()
                 : kind == KB_WS_CHAIN ? kb::chain_err_offset()
-                                      : kb::ep_err_offset());
+                : kind == KB_WS_EP    ? kb::ep_err_offset()
+                                      : 0);   // kb_router_gemm: the first word
     } else {
         return KB_ERR_INVALID_ARG;
     }

@@ -19,7 +19,7 @@ KB_ERR_WORKSPACE = -4
 KB_ERR_TOO_LARGE = -5
 KB_ERR_SCRATCH_LIMIT = -6
 KB_NOALLOC_REZERO = 1
-KB_WS_MAPS, KB_WS_CHAIN, KB_WS_NOALLOC, KB_WS_EP = 0, 1, 2, 3
+KB_WS_MAPS, KB_WS_CHAIN, KB_WS_NOALLOC, KB_WS_EP, KB_WS_RGEMM = 0, 1, 2, 3, 4
 KB_WS_CLEAN, KB_WS_TIMEOUT, KB_WS_MISALIGNED, KB_WS_CAPACITY = 0, 1, 2, 3
 KB_MAX_RANKS = 8
 KB_IPC_HANDLE_BYTES = 64
@@ -44,6 +44,12 @@ SIGNATURES = {
     "kb_router_maps": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_void_p, c_void_p, c_void_p, c_size_t, c_int64, c_int, c_int,
                                c_int, c_int, c_void_p]),
+    "kb_router_gemm_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int]),
+    "kb_router_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_size_t, c_int64, c_int, c_int, c_int, c_int,
+                               c_void_p]),
+    "kb_router_gemm_describe": (c_int, [c_int64, c_int, c_int, c_int, c_void_p, c_void_p,
+                                        c_void_p]),
     "kb_maps_describe": (c_int, [c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                  c_void_p]),
     "kb_expert_maps_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -22,7 +22,7 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libkolibri_b200.so"
 BUILD_DIR = ROOT / "_build"
 
-SOURCES = ["capi.cu", "routing.cu", "norms.cu", "qk_norm_rope.cu", "expand.cu", "chain.cu", "finalize.cu", "ep_peer.cu"]
+SOURCES = ["capi.cu", "routing.cu", "norms.cu", "qk_norm_rope.cu", "expand.cu", "chain.cu", "finalize.cu", "ep_peer.cu", "router_gemm.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

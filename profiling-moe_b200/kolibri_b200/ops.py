@@ -19,7 +19,7 @@ __all__ = [
     "router", "expert_maps", "router_maps", "expand_rows", "qk_norm_rope", "rope_inv_freq",
     "residual_norm_pair", "add_rms_norm", "reserve_workspace", "set_pdl", "expert_maps_noalloc",
     "set_wait_limit", "workspace_status",
-    "moe_finalize", "expand_rows_scaled", "router_maps_allgather",
+    "moe_finalize", "expand_rows_scaled", "router_maps_allgather", "router_gemm",
     "KB_MAPS_AUTO", "KB_MAPS_SINGLE_CTA", "KB_MAPS_MULTI_CTA", "KB_MAPS_TWO_KERNEL",
     "KB_MAPS_HYBRID_ROUTER", "KB_MAPS_WARP_ROUTER",
 ]
@@ -79,9 +79,9 @@ _WS_LOCK = threading.Lock()
 _WS: dict = {}
 
 
-def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+def _workspace(nbytes: int, device: torch.device, tag: str = "maps") -> torch.Tensor:
     stream = _stream(device)
-    key = (device.index, stream)
+    key = (device.index, stream, tag)
     with _WS_LOCK:
         buf = _WS.get(key)
         if buf is None or buf.numel() < nbytes:
@@ -135,6 +135,45 @@ def router(logits: torch.Tensor, bias: Optional[torch.Tensor] = None, k: int = 6
     check(load().kb_router(_p(logits), _p(bias), _p(ids), _p(w), _DTYPE_CODE[w_dtype], T, E, k,
                            int(bool(renorm)), _stream(dev)), "kb_router")
     return ids, w
+
+
+def router_gemm(x: torch.Tensor, w_gate: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                k: int = 6, renorm: bool = False, route: bool = True, logits: bool = True):
+    """Router projection on the tensor cores with the routing fused into its epilogue:
+    logits = (x @ w_gate.T) rounded to bf16 and widened to fp32, then the top-k router on
+    them.  x bf16 [T, H], w_gate bf16 [E, H] (nn.Linear layout).
+    -> (ids int32 [T, k] or None, w fp32 [T, k] or None, logits fp32 [T, E] or None)."""
+    _cuda(x, "x")
+    _cuda(w_gate, "w_gate")
+    if x.dim() != 2 or w_gate.dim() != 2 or x.shape[1] != w_gate.shape[1]:
+        raise ValueError("x must be [num_tokens, hidden] and w_gate [num_experts, hidden]")
+    if x.dtype != torch.bfloat16 or w_gate.dtype != torch.bfloat16:
+        raise ValueError("x and w_gate must be bfloat16")
+    if w_gate.device != x.device:
+        raise ValueError("x and w_gate must be on the same device")
+    _contig(x, "x")
+    _contig(w_gate, "w_gate")
+    T, H = x.shape
+    E = w_gate.shape[0]
+    if bias is not None:
+        _cuda(bias, "bias")
+        if bias.dtype != torch.float32 or bias.numel() != E or bias.device != x.device:
+            raise ValueError(f"bias must be float32 [{E}] on {x.device}")
+        _contig(bias, "bias")
+    if not route and not logits:
+        raise ValueError("router_gemm needs route=True or logits=True")
+    dev = x.device
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev) if route else None
+    w = torch.empty((T, k), dtype=torch.float32, device=dev) if route else None
+    lg = torch.empty((T, E), dtype=torch.float32, device=dev) if logits else None
+    lib = load()
+    with torch.cuda.device(dev):
+        need = lib.kb_router_gemm_workspace_bytes(T, H, E, k if route else 1)
+        ws = _workspace(need, dev, "rgemm")
+        check(lib.kb_router_gemm(_p(x), _p(w_gate), _p(bias), _p(lg), _p(ids), _p(w), _p(ws),
+                                 ws.numel(), T, H, E, k, int(bool(renorm)), _stream(dev)),
+              "kb_router_gemm")
+    return ids, w, lg
 
 
 def _maps_outputs(T: int, E: int, k: int, dev, counts: bool, inverse: bool):
