@@ -149,6 +149,17 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+def measured_tensor_peak():
+    """Dense bf16 TFLOP/s of a cuBLAS GEMM burst on this pool (MEASURED_PEAKS.json), else the
+    fallback figure."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def ncu_traffic(T: int):
     """DRAM bytes per call of the router+map kernels from the committed ncu summary."""
     p = REPO / "profiles" / "router_maps_dram.json"
@@ -216,6 +227,14 @@ def cpu_kernel_times(entries: dict, budget_s: float = 120.0):
         if name == "add_rms_norm":
             return lambda: orc.add_post_moe_norm_ref(ni.moe_out, ni.residual, ni.g_post_moe,
                                                      wl.EPS)
+        if name.startswith("router_gemm"):   # the reference's eager gate GEMM + router
+            def gate_inputs():
+                g = torch.Generator().manual_seed(40)
+                return (torch.randn(T, wl.HIDDEN, generator=g).to(torch.bfloat16),
+                        (0.02 * torch.randn(wl.HIDDEN, wl.NUM_EXPERTS, generator=g)).to(
+                            torch.bfloat16), 0.1 * torch.randn(wl.NUM_EXPERTS, generator=g))
+            x, wg, b = cached(("gate", T), gate_inputs)
+            return lambda: orc.router_eager_reference(orc.router_logits_ref(x, wg), b)
         logits, bias = cached(("router", T), lambda: wl.router_inputs(T, seed=1))
         if name == "router_maps":
             return lambda: orc.router_maps_eager_reference(logits, bias)
@@ -261,7 +280,8 @@ def kernel_table(dev, stream, peak, only=None, only_T=0):
         for T in Ts:
             if only_T and T != only_T:
                 continue
-            out[name][str(T)] = kbench.run_kernel(name, dev, T, peak, stream)
+            out[name][str(T)] = kbench.run_kernel(name, dev, T, peak, stream,
+                                                  measured_tensor_peak()[0])
             torch.cuda.empty_cache()
     return out
 
@@ -333,12 +353,17 @@ def decode_chain_times(dev, tokens, n_layers, stream, world=1, steps=20, warmup=
     out = {"layers": n_layers, "rnope_layers": sum(L.rnope for L in layers),
            "stages": "qk_norm_rope, sandwich, gate GEMM/GEMV, router+maps, expansion or the "
                      "expert-parallel exchange, post-MoE+pre-attn norm",
-           "paths": {"with_gate_gemm": "CUDA graph of per-stage kernels + cuBLAS gate GEMM",
+           "paths": {"with_gate_gemm": "CUDA graph of per-stage kernels; the gate GEMM and router "
+                                       "are kb_router_gemm (tcgen05, routing in its epilogue), "
+                                       "then kb_expert_maps",
+                     "with_gate_cublas": "the same graph with the gate GEMM on cuBLAS "
+                                         "(torch.matmul + fp32 cast + kb_router_maps), as the "
+                                         "reference runs it",
                      "non_gemm_only": "the same graph without the gate GEMM",
                      "one_launch_with_gate_gemv": "kb_decode_chain: all layers in one "
                                                   "persistent launch (T <= 4)",
                      "ep_sharded": "T/N tokens per rank; per layer the per-stage kernels, "
-                                   "cuBLAS gate GEMM, then the peer-memory count all-gather, "
+                                   "tcgen05 gate GEMM, then the peer-memory count all-gather, "
                                    "dispatch to the 384/N expert owners, identity experts, "
                                    "combine back + finalize as the layer's MoE output"},
            "graph": True, "n_gpus": world, "by_T": {}}
@@ -350,11 +375,12 @@ def decode_chain_times(dev, tokens, n_layers, stream, world=1, steps=20, warmup=
         for T in tokens:
             rec = {}
             if world == 1:
-                for gemm in (True, False):
-                    ch = dc.DecodeChain(T, layers, dev, gate_gemm=gemm, expansion=True)
+                for key, gemm, gate in (("with_gate_gemm", True, "tcgen05"),
+                                        ("with_gate_cublas", True, "cublas"),
+                                        ("non_gemm_only", False, "tcgen05")):
+                    ch = dc.DecodeChain(T, layers, dev, gate_gemm=gemm, expansion=True, gate=gate)
                     g = ch.capture(stream)
                     ms = _time_graph(g, stream, dev, steps, warmup, world)
-                    key = "with_gate_gemm" if gemm else "non_gemm_only"
                     rec[key] = {"us_per_step": round(ms * 1e3, 2),
                                 "us_per_token": round(ms * 1e3 / T, 4),
                                 "kb_launches_per_step": ch.launches_per_layer() * n_layers}

@@ -27,6 +27,7 @@
 // issuing work, waits (bounded) for its own tensor copies and frees its tensor memory.
 #include "kb_common.cuh"
 #include "route_math.cuh"
+#include "warp_route.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -51,6 +52,7 @@ constexpr long long kSpin = 1LL << 22;
 // scratch.  The zone does not depend on the shape, so calls of different shapes can share one
 // workspace: no call's scratch overlaps another call's counters.
 constexpr size_t kErrOff = 0;
+constexpr size_t kSplitBarOff = 128;   // cooperative path: grid-barrier counter, then exits
 constexpr size_t kTicketOff = 256;
 constexpr size_t kZeroBytes = 256 * 1024;
 constexpr int64_t kMaxTokens = 524288;   // its tickets fit the zero zone at every tile shape
@@ -59,10 +61,11 @@ __host__ __device__ constexpr size_t align256(size_t v) { return (v + 255) / 256
 
 struct Plan {
     int bn = 0, n_tiles = 0, ks = 0, kb_per = 0, stages = 0, tmem_cols = 0;
+    int coop = 0;   // the grid fits the SMs: cooperative launch, whole-token routing
     int64_t m_tiles = 0;
     size_t smem = 0;
     // workspace layout
-    size_t tk_mn = 0, tk_m = 0, zero_bytes = 0, part = 0, cand = 0, total = 0;
+    size_t tk_mn = 0, tk_m = 0, zero_bytes = 0, part = 0, lgs = 0, cand = 0, total = 0;
 };
 
 // ------------------------------------------------------------------------------------
@@ -163,6 +166,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+// The float whose okey is k (k from okey of a float; the NaN key gives a NaN).
+__device__ __forceinline__ float okey_inv(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 __device__ __forceinline__ float bf16_round(float v) {
     return __bfloat162float(__float2bfloat16_rn(v));
 }
@@ -174,34 +187,92 @@ __device__ __forceinline__ float bf16_round(float v) {
 // score (okey maps every float, NaN included, to a key >= 0x00800000).
 // ------------------------------------------------------------------------------------
 struct TopK {
-    uint32_t key[KMAX];
-    int idx[KMAX];
-    float raw[KMAX];
+    // positions 0..7 as scalars (never an indexed array, so the list stays in registers)
+    uint32_t k0, k1, k2, k3, k4, k5, k6, k7;
+    int i0, i1, i2, i3, i4, i5, i6, i7;
+    float r0, r1, r2, r3, r4, r5, r6, r7;
     uint32_t thr;   // key of position K-1: an element enters only above it
     __device__ __forceinline__ void init() {
-#pragma unroll
-        for (int j = 0; j < KMAX; ++j) { key[j] = 0u; idx[j] = 0; raw[j] = 0.0f; }
+        k0 = k1 = k2 = k3 = k4 = k5 = k6 = k7 = 0u;
+        i0 = i1 = i2 = i3 = i4 = i5 = i6 = i7 = 0;
+        r0 = r1 = r2 = r3 = r4 = r5 = r6 = r7 = 0.0f;
         thr = 0u;
     }
+    __device__ __forceinline__ uint32_t key_at(int j) const {
+        switch (j) {
+            case 0: return k0; case 1: return k1; case 2: return k2; case 3: return k3;
+            case 4: return k4; case 5: return k5; case 6: return k6; default: return k7;
+        }
+    }
+    __device__ __forceinline__ int idx_at(int j) const {
+        switch (j) {
+            case 0: return i0; case 1: return i1; case 2: return i2; case 3: return i3;
+            case 4: return i4; case 5: return i5; case 6: return i6; default: return i7;
+        }
+    }
+    __device__ __forceinline__ float raw_at(int j) const {
+        switch (j) {
+            case 0: return r0; case 1: return r1; case 2: return r2; case 3: return r3;
+            case 4: return r4; case 5: return r5; case 6: return r6; default: return r7;
+        }
+    }
+    // The new element goes before the first smaller key; from there on every element moves
+    // down one place (a displaced element must not be compared again: it could fail to pass
+    // an equal key with a higher expert and land after it).
     __device__ __forceinline__ void offer(uint32_t k, int i, float r, int K) {
         if (k <= thr) return;
-        // the new element goes before the first smaller key; from there on every element
-        // moves down one place (a displaced element must not be compared again: it could
-        // fail to pass an equal key with a higher expert and land after it)
-        bool shift = false;
-#pragma unroll
-        for (int j = 0; j < KMAX; ++j) {
-            shift = shift || k > key[j];
-            const uint32_t tk = key[j];
-            const int ti = idx[j];
-            const float tr = raw[j];
-            if (shift) { key[j] = k; idx[j] = i; raw[j] = r; k = tk; i = ti; r = tr; }
+        bool sh = false;
+#define KB_TOPK_STEP(KJ, IJ, RJ)                                                     \
+        {                                                                            \
+            sh = sh || k > KJ;                                                       \
+            const uint32_t tk_ = KJ;                                                 \
+            const int ti_ = IJ;                                                      \
+            const float tr_ = RJ;                                                    \
+            if (sh) { KJ = k; IJ = i; RJ = r; k = tk_; i = ti_; r = tr_; }           \
         }
-#pragma unroll
-        for (int j = 0; j < KMAX; ++j)
-            if (j == K - 1) thr = key[j];
+        KB_TOPK_STEP(k0, i0, r0) KB_TOPK_STEP(k1, i1, r1) KB_TOPK_STEP(k2, i2, r2)
+        KB_TOPK_STEP(k3, i3, r3) KB_TOPK_STEP(k4, i4, r4) KB_TOPK_STEP(k5, i5, r5)
+        KB_TOPK_STEP(k6, i6, r6) KB_TOPK_STEP(k7, i7, r7)
+#undef KB_TOPK_STEP
+        thr = key_at(K - 1);
     }
 };
+
+// The K-th largest 16-column group maximum (as a key) of s = row + bias over a BN-wide
+// segment in shared memory (K <= BN / 16).  The K largest maxima are kept sorted in g0..g7.
+template <int BN>
+__device__ __forceinline__ uint32_t group_tau(const float* row, const float* bias_sm, int K) {
+    uint32_t g0 = 0, g1 = 0, g2 = 0, g3 = 0, g4 = 0, g5 = 0, g6 = 0, g7 = 0;
+#pragma unroll 1
+    for (int g = 0; g < BN / 16; ++g) {
+        float sv[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 x = reinterpret_cast<const float4*>(row + 16 * g)[q];
+            const float4 b = reinterpret_cast<const float4*>(bias_sm + 16 * g)[q];
+            sv[4 * q] = x.x + b.x; sv[4 * q + 1] = x.y + b.y;
+            sv[4 * q + 2] = x.z + b.z; sv[4 * q + 3] = x.w + b.w;
+        }
+        float mx = sv[0];
+#pragma unroll
+        for (int j = 1; j < 15; j += 2) mx = fmax3_nan(mx, sv[j], sv[j + 1]);
+        mx = fmax3_nan(mx, sv[15], sv[15]);
+        uint32_t k = okey(mx), o;
+        // sorted insertion of a bare key: a max/min ladder
+        o = min(k, g0); g0 = max(k, g0); k = o;
+        o = min(k, g1); g1 = max(k, g1); k = o;
+        o = min(k, g2); g2 = max(k, g2); k = o;
+        o = min(k, g3); g3 = max(k, g3); k = o;
+        o = min(k, g4); g4 = max(k, g4); k = o;
+        o = min(k, g5); g5 = max(k, g5); k = o;
+        o = min(k, g6); g6 = max(k, g6); k = o;
+        g7 = max(k, g7);
+    }
+    switch (K) {
+        case 1: return g0; case 2: return g1; case 3: return g2; case 4: return g3;
+        case 5: return g4; case 6: return g5; case 7: return g6; default: return g7;
+    }
+}
 
 // Sum of K <= 8 weights in the order of a 32-lane xor butterfly (lanes >= K hold zero), the
 // order in which the warp routers renormalise.
@@ -214,7 +285,7 @@ __device__ __forceinline__ void write_row(const TopK& tk, int64_t t, int K, int 
                                           int32_t* __restrict__ ids, float* __restrict__ w) {
     float wv[KMAX];
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j) wv[j] = (j < K) ? sigmoid_acc(tk.raw[j]) : 0.0f;
+    for (int j = 0; j < KMAX; ++j) wv[j] = (j < K) ? sigmoid_acc(tk.raw_at(j)) : 0.0f;
     if (renorm) {
         const float inv = 1.0f / (butterfly_sum8(wv) + 1e-20f);
 #pragma unroll
@@ -223,7 +294,7 @@ __device__ __forceinline__ void write_row(const TopK& tk, int64_t t, int K, int 
 #pragma unroll
     for (int j = 0; j < KMAX; ++j)
         if (j < K) {
-            ids[t * K + j] = tk.idx[j];
+            ids[t * K + j] = tk.idx_at(j);
             w[t * K + j] = wv[j];
         }
 }
@@ -238,6 +309,185 @@ struct Args {
     int E, K, renorm, nkb;   // nkb: k-blocks of the whole hidden dimension
     long long spin;
 };
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Barrier over the whole (co-resident) grid: the arrival counter reaches `target`.  Bounded:
+// false (error word set) if it did not within the poll limit or another wait gave up.
+__device__ __forceinline__ bool grid_sync(unsigned* cnt, unsigned target, int* err, long long spin,
+                                          int* flag) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // release: this CTA's stores (ordered before by the CTA barrier) precede the arrival
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+        unsigned v = ld_acquire_gpu(cnt);
+        long long it = 0;
+        while (v < target && it < spin) {
+            if ((it & 255) == 255 && *(volatile int*)err) break;
+            if (it > 256) __nanosleep(32);
+            v = ld_acquire_gpu(cnt);
+            ++it;
+        }
+        if (v < target) atomicExch(err, KB_WS_TIMEOUT);
+        flag[2] = (v >= target) && *(volatile int*)err == 0;
+        __threadfence();
+    }
+    __syncthreads();
+    return flag[2] != 0;
+}
+
+// A 384-wide row in the warp routers' layout (lane l holds experts 4*(l + 32q) + i), read
+// through L2: other CTAs of this launch wrote it.
+__device__ __forceinline__ void load_row_cg(const float* row, int lane, float (&x)[12]) {
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(row) + lane + 32 * q);
+        x[4 * q] = v.x; x[4 * q + 1] = v.y; x[4 * q + 2] = v.z; x[4 * q + 3] = v.w;
+    }
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                 ::"r"(su32(smem_dst)), "l"(gmem_src) : "memory");
+}
+
+// The epilogue of a cooperative launch (every CTA resident: the grid fits the SMs).
+//   1. the CTA's tile goes from TMEM to shared memory (rounded to bf16 when the hidden
+//      dimension is not split) and from there, row segments coalesced, to global memory: the
+//      logits (or the workspace when the caller wants none), or with several hidden splits
+//      the fp32 partial part[z][t][e]
+//   2. (several splits) grid barrier; each CTA sums a contiguous share of the [T][E] logits
+//      over the splits in split order (so the sum does not depend on timing): cp.async copies
+//      gather all splits of a chunk into shared memory at once, one thread per float4 adds
+//      them up, rounds to bf16 and stores
+//   3. grid barrier; one warp per token ranks the whole row with the library's warp router
+//      (route_fast; route_exact when it cannot decide: the order of torch.sort) and weighs
+//      the picks with pick_weight, the next token's row loaded while this one is ranked
+//   4. the last CTA out resets the barrier counters
+__device__ __forceinline__ void coop_epilogue(const Args& a, const Plan& p, uint32_t trow, int r,
+                                             int64_t m0, int z, int n0, int* flag, float* red,
+                                             int rs, size_t region) {
+    const int E = a.E, K = a.K;
+    int* err = reinterpret_cast<int*>(a.ws + kErrOff);
+    unsigned* bar = reinterpret_cast<unsigned*>(a.ws + kSplitBarOff);
+    unsigned* leave = bar + 1;
+    float* part = reinterpret_cast<float*>(a.ws + p.part);
+    float* out = a.logits ? a.logits : reinterpret_cast<float*>(a.ws + p.lgs);
+    const int bn = p.bn;
+    const bool split = p.ks > 1;
+#pragma unroll 1
+    for (int c = 0; c < bn; c += 32) {
+        float v[32];
+        tmem_ld32(trow + (uint32_t)c, v);
+        if (!split) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
+        }
+        float4* srow = reinterpret_cast<float4*>(red + r * rs + c);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            srow[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    __syncthreads();
+    {
+        const int rows = (int)(a.T - m0 < BM ? a.T - m0 : (int64_t)BM);
+        const int q4 = bn / 4;
+        float* dst = split ? part + (int64_t)z * a.T * E : out;
+        for (int i = threadIdx.x; i < rows * q4; i += THREADS) {
+            const int rr = i / q4, qq = i - rr * q4;
+            reinterpret_cast<float4*>(dst + (m0 + rr) * E + n0)[qq] =
+                reinterpret_cast<const float4*>(red + rr * rs)[qq];
+        }
+    }
+    const unsigned G = gridDim.x * gridDim.y * gridDim.z;
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (!grid_sync(bar, G, err, a.spin, flag)) return;
+
+    if (split) {
+        const int64_t n4 = a.T * (int64_t)E / 4;
+        const int64_t per = (n4 + G - 1) / G;
+        const int64_t lo = (int64_t)cta * per, hi = min(n4, lo + per);
+        const float4* p4 = reinterpret_cast<const float4*>(part);
+        float4* buf = reinterpret_cast<float4*>(red);   // the tile is in global memory now
+        const int64_t chunk = (int64_t)(region / (16 * (size_t)p.ks));
+        for (int64_t c0 = lo; c0 < hi; c0 += chunk) {
+            const int nch = (int)min(chunk, hi - c0);
+            for (int q = threadIdx.x; q < nch * p.ks; q += THREADS) {
+                const int zz = q / nch, ii = q - zz * nch;
+                cp_async16(buf + q, p4 + (int64_t)zz * n4 + c0 + ii);
+            }
+            asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+            __syncthreads();
+            for (int ii = threadIdx.x; ii < nch; ii += THREADS) {
+                float4 acc = buf[ii];
+                for (int zz = 1; zz < p.ks; ++zz) {
+                    const float4 v = buf[zz * nch + ii];
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                }
+                reinterpret_cast<float4*>(out)[c0 + ii] =
+                    make_float4(bf16_round(acc.x), bf16_round(acc.y), bf16_round(acc.z),
+                                bf16_round(acc.w));
+            }
+            __syncthreads();
+        }
+        if (!grid_sync(bar, 2 * G, err, a.spin, flag)) return;
+    }
+
+    if (a.ids) {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        int* sel = reinterpret_cast<int*>(red) + warp * 32;   // per-warp pick scratch
+        const int64_t nw = (int64_t)G * (THREADS / 32);
+        int64_t tt = (int64_t)cta * (THREADS / 32) + warp;
+        if (E == 384 && K <= 8) {
+            // E = 384: 12 experts per lane as three float4 (expert 4*(lane + 32q) + i)
+            float b[12];
+            load_bias<12, true>(a.bias, E, lane, b);
+            float nxt[12];
+            if (tt < a.T) load_row_cg(out + tt * E, lane, nxt);
+            for (; tt < a.T; tt += nw) {
+                float sv[12];
+#pragma unroll
+                for (int j = 0; j < 12; ++j) sv[j] = nxt[j] + b[j];
+                const float* row = out + tt * E;
+                if (tt + nw < a.T) load_row_cg(out + (tt + nw) * E, lane, nxt);
+                const bool done = K == 6 ? route_fast<12, 6>(sv, K, lane, sel)
+                                         : route_fast<12, 0>(sv, K, lane, sel);
+                if (!done) route_exact<12, true>(row, a.bias, E, K, lane, sel);
+                const int id = lane < K ? sel[lane] : 0;
+                const float wv = pick_weight(lane < K ? row[id] : 0.0f, K, lane, a.renorm);
+                if (lane < K) {
+                    a.ids[tt * K + lane] = id;
+                    a.weights[tt * K + lane] = wv;
+                }
+                __syncwarp();
+            }
+        } else {
+            for (; tt < a.T; tt += nw) {
+                const float* row = out + tt * E;
+                route_exact<16, false>(row, a.bias, E, K, lane, sel);
+                const int id = lane < K ? sel[lane] : 0;
+                const float wv = pick_weight(lane < K ? row[id] : 0.0f, K, lane, a.renorm);
+                if (lane < K) {
+                    a.ids[tt * K + lane] = id;
+                    a.weights[tt * K + lane] = wv;
+                }
+                __syncwarp();
+            }
+        }
+    }
+    // the last CTA out resets the counters (every CTA has passed the barriers by then)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (atomicAdd(leave, 1u) == G - 1) {
+            atomicExch(bar, 0u);
+            atomicExch(leave, 0u);
+        }
+    }
+}
 
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (m_tiles, n_tiles, ks); BN experts per tile; S ring slots.
@@ -260,7 +510,9 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     uint64_t* accum = empty + S;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
     int* flag = reinterpret_cast<int*>(tmem_slot + 1);
-    float* bias_sm = reinterpret_cast<float*>(flag + 4);
+    // the bias tile is read as float4: 16-byte aligned
+    float* bias_sm = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(flag + 4) + 15) & ~uintptr_t(15));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t m = blockIdx.x;
@@ -339,104 +591,76 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     pdl_launch();
     const int E = a.E, K = a.K;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    TopK tk;
-    tk.init();
-    bool have_row = false;   // tk holds this row's tile candidates
+    constexpr int RS = BN + 4;                     // padded row stride of the tile (floats)
+    float* red = reinterpret_cast<float*>(sm);     // the tile's logits [BM][RS] (ring is free)
+    bool have = false;                             // red holds the rounded tile (per-tile path)
 
-    if (ok && p.ks == 1) {
+    if (ok && p.coop) {
+        // the grid fits the SMs: tokens are routed whole after a grid barrier
+        coop_epilogue(a, p, trow, r, m0, z, n0, flag, red, RS, region);
+        ok = false;
+    } else if (ok) {
+        // one hidden split, more tiles than SMs: TMEM -> bf16-rounded row in shared memory
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
             float v[32];
             tmem_ld32(trow + (uint32_t)c, v);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
-            if (valid) {
-                if (a.logits) {
-                    float4* dst = reinterpret_cast<float4*>(a.logits + t * E + n0 + c);
+            float4* srow = reinterpret_cast<float4*>(red + r * RS + c);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                }
-                if (a.ids) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        tk.offer(okey(v[j] + bias_sm[c + j]), n0 + c + j, v[j], K);
-                }
-            }
+            for (int q = 0; q < 8; ++q)
+                srow[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         }
-        have_row = valid && a.ids;
-    } else if (ok) {
-        // several hidden splits: store this split's fp32 partial, the last split sums them
-        float* part = reinterpret_cast<float*>(a.ws + p.part);
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-            float v[32];
-            tmem_ld32(trow + (uint32_t)c, v);
-            if (valid) {
-                float4* dst = reinterpret_cast<float4*>(part + ((int64_t)z * a.T + t) * E + n0 + c);
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            }
-        }
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            int* tkt = reinterpret_cast<int*>(a.ws + p.tk_mn) + m * p.n_tiles + n;
-            const int old = atomicAdd(tkt, 1);
-            const bool last = old == p.ks - 1;
-            if (last) *tkt = 0;   // left zero for the next call
-            flag[0] = last;
-        }
-        __syncthreads();
-        if (flag[0]) {
-            __threadfence();
-            // cooperative, coalesced sum of the ks partial tiles (split order) into shared
-            // memory (the ring is free: every MMA completed), rounded to bf16
-            const int rows = (int)(a.T - m0 < BM ? a.T - m0 : (int64_t)BM);
-            constexpr int Q = BN / 4;              // float4 per row segment
-            constexpr int RS = BN + 4;             // padded row stride (floats)
-            float* red = reinterpret_cast<float*>(sm);
-            for (int e4 = threadIdx.x; e4 < rows * Q; e4 += THREADS) {
-                const int rr = e4 / Q, qq = e4 % Q;
-                const float* src = part + (m0 + rr) * E + n0 + 4 * qq;
-                const int64_t zs = a.T * (int64_t)E;
-                float4 acc = __ldcg(reinterpret_cast<const float4*>(src));
-                int zz = 1;
-                for (; zz + 4 <= p.ks; zz += 4) {
-                    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(src + zz * zs));
-                    const float4 v2 = __ldcg(reinterpret_cast<const float4*>(src + (zz + 1) * zs));
-                    const float4 v3 = __ldcg(reinterpret_cast<const float4*>(src + (zz + 2) * zs));
-                    const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + (zz + 3) * zs));
-                    acc.x = (((acc.x + v1.x) + v2.x) + v3.x) + v4.x;
-                    acc.y = (((acc.y + v1.y) + v2.y) + v3.y) + v4.y;
-                    acc.z = (((acc.z + v1.z) + v2.z) + v3.z) + v4.z;
-                    acc.w = (((acc.w + v1.w) + v2.w) + v3.w) + v4.w;
-                }
-                for (; zz < p.ks; ++zz) {
-                    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(src + zz * zs));
-                    acc.x += v1.x; acc.y += v1.y; acc.z += v1.z; acc.w += v1.w;
-                }
-                acc = make_float4(bf16_round(acc.x), bf16_round(acc.y), bf16_round(acc.z),
-                                  bf16_round(acc.w));
-                *reinterpret_cast<float4*>(red + rr * RS + 4 * qq) = acc;
-                if (a.logits)
-                    *reinterpret_cast<float4*>(a.logits + (m0 + rr) * E + n0 + 4 * qq) = acc;
-            }
-            __syncthreads();
-            if (valid && a.ids) {
-                const float* row = red + r * RS;
-#pragma unroll 4
-                for (int j = 0; j < BN; ++j) tk.offer(okey(row[j] + bias_sm[j]), n0 + j, row[j], K);
-                have_row = true;
-            }
-        } else {
-            ok = false;   // another split finishes this tile
+        have = true;
+    }
+    __syncthreads();   // the tile in shared memory is complete
+    if (have && a.logits) {   // the rounded logits, row segments stored coalesced
+        const int rows = (int)(a.T - m0 < BM ? a.T - m0 : (int64_t)BM);
+        constexpr int Q4 = BN / 4;
+        for (int i = threadIdx.x; i < rows * Q4; i += THREADS) {
+            const int rr = i / Q4, qq = i - rr * Q4;
+            reinterpret_cast<float4*>(a.logits + (m0 + rr) * E + n0)[qq] =
+                reinterpret_cast<const float4*>(red + rr * RS)[qq];
         }
     }
 
-    // ---------------- merge the expert tiles and write ids / weights ----------------
-    if (ok && a.ids) {
+    // ---------------- per-tile path: rank this thread's row segment ----------------
+    // tau = the K-th largest 16-column group maximum of s = logit + bias: each of those K
+    // groups holds an element >= tau, so every top-K element is >= tau (a lower bound; all
+    // elements pass when the segment has fewer than K groups).  Only elements >= tau (and NaN,
+    // which ranks first) enter the register top-K, in ascending column order.
+    TopK tk;
+    tk.init();
+    const bool have_row = have && a.ids && valid;
+    if (have_row) {
+        const float* row = red + r * RS;
+        const uint32_t tau = (BN / 16 >= K) ? group_tau<BN>(row, bias_sm, K) : 0u;
+        const float tf = tau == 0u ? -INFINITY : okey_inv(tau);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            unsigned mask = 0u;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 x = reinterpret_cast<const float4*>(row + c)[q];
+                const float4 b = reinterpret_cast<const float4*>(bias_sm + c)[q];
+                const float s0 = x.x + b.x, s1 = x.y + b.y, s2 = x.z + b.z, s3 = x.w + b.w;
+                mask |= (unsigned)((s0 >= tf) | (s0 != s0)) << (4 * q);
+                mask |= (unsigned)((s1 >= tf) | (s1 != s1)) << (4 * q + 1);
+                mask |= (unsigned)((s2 >= tf) | (s2 != s2)) << (4 * q + 2);
+                mask |= (unsigned)((s3 >= tf) | (s3 != s3)) << (4 * q + 3);
+            }
+            while (mask) {
+                const int j = c + __ffs(mask) - 1;
+                mask &= mask - 1u;
+                const float v = row[j];
+                tk.offer(okey(v + bias_sm[j]), n0 + j, v, K);
+            }
+        }
+    }
+
+    // ---------------- per-tile path: merge the expert tiles, write ids / weights ----------
+    if (have && a.ids) {
         if (p.n_tiles == 1) {
             if (have_row) write_row(tk, t, K, a.renorm, a.ids, a.weights);
         } else {
@@ -447,8 +671,8 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
 #pragma unroll
                 for (int j = 0; j < KMAX; ++j)
                     if (j < K) {
-                        ck[o + j] = ((uint64_t)tk.key[j] << 32) | (uint32_t)tk.idx[j];
-                        cr[o + j] = tk.raw[j];
+                        ck[o + j] = ((uint64_t)tk.key_at(j) << 32) | (uint32_t)tk.idx_at(j);
+                        cr[o + j] = tk.raw_at(j);
                     }
             }
             __threadfence();
@@ -465,12 +689,18 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
                 __threadfence();
                 TopK f;
                 f.init();
+#pragma unroll 1
                 for (int nn = 0; nn < p.n_tiles; ++nn) {
+                    // the tile's K candidates are loaded together (one round trip per tile)
                     const int64_t o = ((int64_t)nn * a.T + t) * K;
-                    for (int j = 0; j < K; ++j) {
-                        const uint64_t c = __ldcg(ck + o + j);
-                        f.offer((uint32_t)(c >> 32), (int)(uint32_t)c, __ldcg(cr + o + j), K);
-                    }
+                    uint64_t cv[KMAX];
+                    float rv[KMAX];
+#pragma unroll
+                    for (int j = 0; j < KMAX; ++j)
+                        if (j < K) { cv[j] = __ldcg(ck + o + j); rv[j] = __ldcg(cr + o + j); }
+#pragma unroll
+                    for (int j = 0; j < KMAX; ++j)
+                        if (j < K) f.offer((uint32_t)(cv[j] >> 32), (int)(uint32_t)cv[j], rv[j], K);
                 }
                 write_row(f, t, K, a.renorm, a.ids, a.weights);
             }
@@ -528,11 +758,8 @@ bool make_plan(Plan& p, int64_t T, int H, int E, int K, int sms) {
     p.m_tiles = (T + BM - 1) / BM;
     int bn = env_int("KB_RGEMM_BN", 0);
     int ks = env_int("KB_RGEMM_KS", 0);
-    if (bn == 0) {
-        if (E % 192 == 0 && p.m_tiles * (E / 192) >= sms / 2) bn = 192;
-        else if (E % 128 == 0 && p.m_tiles * (E / 128) >= sms / 2) bn = 128;
-        else bn = 64;
-    }
+    if (bn == 0)   // the widest tile: the fewest re-reads of x and of the gate weight
+        bn = E % 192 == 0 ? 192 : E % 128 == 0 ? 128 : 64;
     if (bn != 64 && bn != 128 && bn != 192 && bn != 256) return false;
     if (E % bn != 0) return false;
     p.bn = bn;
@@ -545,15 +772,21 @@ bool make_plan(Plan& p, int64_t T, int H, int E, int K, int sms) {
             if (nkb % d == 0 && d <= want) ks = d;
     }
     ks = std::max(1, std::min(ks, nkb));
+    // several splits run as one cooperative launch of at most one CTA per SM
+    const int64_t tiles = p.m_tiles * p.n_tiles;
+    if (ks > 1 && tiles * ks > sms) ks = (int)std::max<int64_t>(1, sms / tiles);
     p.ks = ks;
     p.kb_per = (nkb + ks - 1) / ks;
     p.ks = (nkb + p.kb_per - 1) / p.kb_per;   // no empty split
+    // a grid that fits the SMs routes whole tokens after a grid barrier (KB_RGEMM_COOP=0
+    // forces the per-tile path when the hidden dimension is not split: tests)
+    p.coop = (tiles * p.ks <= sms && (p.ks > 1 || env_int("KB_RGEMM_COOP", 1) != 0)) ? 1 : 0;
     const size_t stage = (size_t)A_BYTES + (size_t)bn * BK * 2;
     p.stages = (int)std::max<size_t>(2, std::min<size_t>((size_t)p.kb_per, kSmemCap / stage));
     p.stages = std::min(p.stages, 8);
     const size_t ring = (size_t)p.stages * stage;
     const size_t red = (size_t)BM * (bn + 4) * sizeof(float);
-    p.smem = 1024 + std::max(ring, red) + (size_t)(2 * p.stages + 1) * 8 + 4 + 16 +
+    p.smem = 1024 + std::max(ring, red) + (size_t)(2 * p.stages + 1) * 8 + 4 + 16 + 16 +
              (size_t)bn * sizeof(float);
     p.tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
     // workspace
@@ -563,9 +796,12 @@ bool make_plan(Plan& p, int64_t T, int H, int E, int K, int sms) {
     if (p.tk_m + (size_t)p.m_tiles * sizeof(int) > kZeroBytes) return false;   // T too large
     p.part = p.zero_bytes;
     const size_t part_bytes = p.ks > 1 ? align256((size_t)p.ks * T * E * sizeof(float)) : 0;
-    p.cand = p.part + part_bytes;
+    p.lgs = p.part + part_bytes;
+    const size_t lgs_bytes = p.coop ? align256((size_t)T * E * sizeof(float)) : 0;
+    p.cand = p.lgs + lgs_bytes;
     const size_t cand_bytes =
-        p.n_tiles > 1 ? align256((size_t)p.n_tiles * T * K * (sizeof(uint64_t) + sizeof(float))) : 0;
+        (!p.coop && p.n_tiles > 1)
+            ? align256((size_t)p.n_tiles * T * K * (sizeof(uint64_t) + sizeof(float))) : 0;
     p.total = p.cand + cand_bytes;
     (void)K;
     return true;
@@ -583,7 +819,20 @@ int launch_bn(const CUtensorMap& mx, const CUtensorMap& mw, const Args& a, const
     });
     if (attr_err) return attr_err;
     const dim3 grid((unsigned)p.m_tiles, (unsigned)p.n_tiles, (unsigned)p.ks);
-    return launch(kern, grid, dim3(THREADS), p.smem, stream, mx, mw, a, p);
+    if (!p.coop) return launch(kern, grid, dim3(THREADS), p.smem, stream, mx, mw, a, p);
+    // the CTAs wait for one another at grid barriers: a cooperative launch guarantees that
+    // every CTA is resident (the plan keeps the grid within one CTA per SM)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, mx, mw, a, p));
 }
 
 }  // namespace rg

@@ -9,9 +9,13 @@ full attention without RoPE).  Per layer i, on one stream:
                         (R1_sandwich_norm, :232-234)
   2. Q/K norm + RoPE    q', k' = per-head RMSNorm then NeoX RoPE at the token positions, or
                         the RNoPE identity on full-attention layers (attention(), :190-199)
-  3. router GEMM        logits = (moe_in @ W_g[i]).float()        (gate_gemm, :236-238)
+  3. router GEMM        logits = (moe_in @ W_g[i]).float()        (gate_gemm, :241-242)
   4. router + maps      top-6 of logits + bias, sigmoid weights, counts/offsets/p2u/u2p
-                        (R2_moe_prologue, :240-246)
+                        (R2_moe_prologue, :244-246)
+     gate="tcgen05" (default): kb_router_gemm computes 3 and the router of 4 in one launch
+     (tensor-core GEMM, routing in its epilogue), then kb_expert_maps builds the maps from the
+     ids; gate="cublas": torch.matmul, the cast to fp32 and kb_router_maps, as the reference
+     runs it.
   5. expansion          permuted[r] = moe_in[p2u[r] % T]            (R2, optional)
      or, token-sharded over ranks (ep=PeerExpertParallel), the expert-parallel exchange:
                         count all-gather, dispatch of the routed rows to their owners,
@@ -24,8 +28,8 @@ full attention without RoPE).  Per layer i, on one stream:
 The attention and expert GEMMs are outside this path: attn_out, moe_out and the projected
 q/k are fixed synthetic stand-ins (one buffer each, shared by all layers), while the residual
 stream r and the router inputs flow from layer to layer, so every layer depends on the one
-before.  The router GEMM is a cuBLAS call (torch.matmul); everything else is a
-libkolibri_b200 kernel launched through the C ABI.  `capture()` records the whole chain in
+before.  Every stage is a libkolibri_b200 kernel launched through the C ABI (with gate="cublas"
+the router GEMM is torch.matmul instead).  `capture()` records the whole chain in
 one CUDA graph; launches keep programmatic-dependent-launch edges inside it.
 """
 from __future__ import annotations
@@ -81,10 +85,13 @@ class DecodeChain:
                  seed: int = 5, expansion: bool = True, gate_gemm: bool = True,
                  H: int = wl.HIDDEN, Hq: int = wl.HQ, Hkv: int = wl.HKV, D: int = wl.HEAD_DIM,
                  E: int = wl.NUM_EXPERTS, K: int = wl.TOP_K, eps: float = wl.EPS,
-                 theta: float = wl.ROPE_THETA, ep=None):
+                 theta: float = wl.ROPE_THETA, ep=None, gate: str = "tcgen05"):
         self.T, self.H, self.Hq, self.Hkv, self.D, self.E, self.K = T, H, Hq, Hkv, D, E, K
         self.eps, self.layers, self.device = float(eps), layers, device
         self.expansion, self.gate_gemm = expansion and ep is None, gate_gemm
+        if gate not in ("tcgen05", "cublas"):
+            raise ValueError("gate must be 'tcgen05' or 'cublas'")
+        self.gate = gate if gate_gemm else None
         self.ep = ep
         if ep is not None and (ep.H != H or ep.E != E or ep.K != K or
                                T > ep.pg.max_tokens or ep.dtype != torch.bfloat16):
@@ -122,15 +129,20 @@ class DecodeChain:
         self.u2p = torch.empty(T * K, dtype=torch.int32, device=device)
         self.permuted = torch.empty(T * K, H, dtype=bf, device=device) if self.expansion else None
         self.moe_out_ep = torch.empty(T, H, dtype=bf, device=device) if ep is not None else None
-        self.ws_bytes = int(self.lib.kb_router_maps_workspace_bytes(T, E, K))
+        self.ws_bytes = int(max(self.lib.kb_router_maps_workspace_bytes(T, E, K),
+                                self.lib.kb_expert_maps_workspace_bytes(T, E, K)))
         self.ws = torch.zeros(max(self.ws_bytes, 256), dtype=torch.uint8, device=device)
+        self.gws_bytes = (int(self.lib.kb_router_gemm_workspace_bytes(T, H, E, K))
+                          if self.gate == "tcgen05" else 0)
+        self.gws = (torch.zeros(self.gws_bytes, dtype=torch.uint8, device=device)
+                    if self.gws_bytes else None)
         self.inv_freq = ops.rope_inv_freq(theta, D, device)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
 
     # ------------------------------------------------------------------------------------
     def launches_per_layer(self) -> int:
         """Kernels of this library launched per layer (the cuBLAS GEMM and cast excluded)."""
-        _, launches, _ = self._describe()
+        _, launches, _ = self._describe(route=self.gate != "tcgen05" or self.ep is not None)
         # the exchange: dispatch, combine send + finalize (the count all-gather rides on the
         # router + maps launch on its single-CTA and tile paths, one more launch elsewhere)
         extra = 0
@@ -139,12 +151,13 @@ class DecodeChain:
             fused = p == _lib.KB_MAPS_SINGLE_CTA or (p == _lib.KB_MAPS_MULTI_CTA and
                                                       grid >= self.ep.world)
             extra = 3 + (0 if fused else 1)
-        return 3 + launches + (1 if self.expansion else 0) + extra
+        gate = 1 if self.gate == "tcgen05" else 0     # kb_router_gemm
+        return 3 + gate + launches + (1 if self.expansion else 0) + extra
 
-    def _describe(self):
+    def _describe(self, route: bool = True):
         import ctypes
         p, n, gsz = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
-        _lib.check(self.lib.kb_maps_describe(self.T, self.E, self.K, 1, _lib.KB_MAPS_AUTO,
+        _lib.check(self.lib.kb_maps_describe(self.T, self.E, self.K, int(route), _lib.KB_MAPS_AUTO,
                                              ctypes.byref(p), ctypes.byref(n), ctypes.byref(gsz)),
                    "kb_maps_describe")
         return p.value, n.value, gsz.value
@@ -179,12 +192,25 @@ class DecodeChain:
                 if record:
                     record(i, "qk", dict(q=self.q, k=self.k, gq=L.g_q, gk=L.g_k, pos=pos,
                                          q_out=self.q_out, k_out=self.k_out))
-                if self.gate_gemm:
+                routed = False   # ids and weights already written by kb_router_gemm
+                if self.gate == "cublas":
                     torch.matmul(self.moe_in, L.w_gate_t.t(), out=self.logits_bf)
                     self.logits.copy_(self.logits_bf)
-                    if record:
-                        record(i, "gate", dict(x=self.moe_in, w=L.w_gate_t.t(), logits=self.logits))
-                if self.ep is None:
+                elif self.gate == "tcgen05":
+                    routed = self.ep is None
+                    _lib.check(lib.kb_router_gemm(
+                        self.moe_in.data_ptr(), L.w_gate_t.data_ptr(), L.gate_bias.data_ptr(),
+                        self.logits.data_ptr(), self.ids.data_ptr() if routed else None,
+                        self.w.data_ptr() if routed else None, self.gws.data_ptr(),
+                        self.gws_bytes, T, H, E, K, 0, st), "kb_router_gemm")
+                if self.gate_gemm and record:
+                    record(i, "gate", dict(x=self.moe_in, w=L.w_gate_t.t(), logits=self.logits))
+                if routed:
+                    _lib.check(lib.kb_expert_maps(
+                        self.ids.data_ptr(), self.counts.data_ptr(), self.offsets.data_ptr(),
+                        self.p2u.data_ptr(), self.u2p.data_ptr(), self.ws.data_ptr(),
+                        self.ws_bytes, T, E, K, _lib.KB_MAPS_AUTO, st), "kb_expert_maps")
+                elif self.ep is None:
                     _lib.check(lib.kb_router_maps(
                         self.logits.data_ptr(), L.gate_bias.data_ptr(), self.ids.data_ptr(),
                         self.w.data_ptr(), self.counts.data_ptr(), self.offsets.data_ptr(),

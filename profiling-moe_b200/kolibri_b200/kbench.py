@@ -16,6 +16,13 @@ Algorithmic bytes per unit (the compulsory reads and writes of each kernel):
   finalize          T*K x 12 288 read + T x 12 288 written + T*K x (4 B u2p + 4 B weight)
   router_maps       1632 B/token + 6164 B per call
   expert_maps       72 B/token + 4 616 B per call
+  router_gemm       x read (12 288 B/token) + gate weight read once (E x H x 2 = 4 718 592 B
+                    per call) + logits written (1536 B/token) + ids and weights (48 B/token);
+                    2 x T x H x E flops.  Its roofline is the slower of bytes / HBM peak and
+                    flops / tensor peak (the weight read bounds small T, the flops large T).
+  router_gemm_cublas
+                    the same work as the reference runs it: torch.matmul (cuBLAS, bf16 out),
+                    the cast to fp32 and kb_router on the logits
 """
 from __future__ import annotations
 
@@ -248,6 +255,72 @@ def bench_expert_maps(dev, T: int, peak: float, stream) -> dict:
     return _entry(us, T, T * 72 + 384 * 4 + 385 * 8, peak, n)
 
 
+def _gate_sets(dev, T: int):
+    E, H = wl.NUM_EXPERTS, wl.HIDDEN
+    per_set = T * H * 2 + E * H * 2
+    n = nsets_for(per_set)
+    sets = []
+    for i in range(n):
+        g = torch.Generator(device=dev).manual_seed(40 + i)
+        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        w = (0.02 * torch.randn(E, H, generator=g, device=dev)).to(torch.bfloat16)
+        b = 0.1 * torch.randn(E, generator=g, device=dev)
+        sets.append((x, w, b))
+    return sets, n
+
+
+def _gate_entry(us: float, T: int, peak: float, tflops_peak: float, nsets: int) -> dict:
+    E, K, H = wl.NUM_EXPERTS, wl.TOP_K, wl.HIDDEN
+    nbytes = T * H * 2 + E * H * 2 + T * E * 4 + T * K * 8
+    flops = 2.0 * T * H * E
+    t_hbm, t_tc = nbytes / (peak * 1e9), flops / (tflops_peak * 1e12)
+    e = _entry(us, T, nbytes, peak, nsets)
+    e.update({"TFLOPs": round(flops / (us * 1e-6) / 1e12, 2),
+              "bound": "hbm" if t_hbm >= t_tc else "tensor",
+              "frac": round(max(t_hbm, t_tc) / (us * 1e-6), 4), "flops": flops})
+    return e
+
+
+def bench_router_gemm(dev, T: int, peak: float, stream, tflops_peak: float) -> dict:
+    E, K, H = wl.NUM_EXPERTS, wl.TOP_K, wl.HIDDEN
+    sets, n = _gate_sets(dev, T)
+    lib = _lib.load()
+    logits = torch.empty(T, E, device=dev)
+    ids = torch.empty(T, K, dtype=torch.int32, device=dev)
+    w = torch.empty(T, K, device=dev)
+    wsb = lib.kb_router_gemm_workspace_bytes(T, H, E, K)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+
+    def launch(i):
+        x, wg, b = sets[i]
+        _lib.check(lib.kb_router_gemm(x.data_ptr(), wg.data_ptr(), b.data_ptr(), logits.data_ptr(),
+                                      ids.data_ptr(), w.data_ptr(), ws.data_ptr(), wsb, T, H, E, K,
+                                      0, torch.cuda.current_stream(dev).cuda_stream),
+                   "kb_router_gemm")
+    us = time_calls(launch, n, stream)
+    return _gate_entry(us, T, peak, tflops_peak, n)
+
+
+def bench_router_gemm_cublas(dev, T: int, peak: float, stream, tflops_peak: float) -> dict:
+    E, K = wl.NUM_EXPERTS, wl.TOP_K
+    sets, n = _gate_sets(dev, T)
+    lib = _lib.load()
+    lbf = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
+    logits = torch.empty(T, E, device=dev)
+    ids = torch.empty(T, K, dtype=torch.int32, device=dev)
+    w = torch.empty(T, K, device=dev)
+
+    def launch(i):
+        x, wg, b = sets[i]
+        torch.matmul(x, wg.t(), out=lbf)
+        logits.copy_(lbf)
+        _lib.check(lib.kb_router(logits.data_ptr(), b.data_ptr(), ids.data_ptr(), w.data_ptr(),
+                                 _lib.KB_F32, T, E, K, 0,
+                                 torch.cuda.current_stream(dev).cuda_stream), "kb_router")
+    us = time_calls(launch, n, stream)
+    return _gate_entry(us, T, peak, tflops_peak, n)
+
+
 # The BASELINE token counts of each kernel.
 KERNEL_T: Dict[str, List[int]] = {
     "qk_norm_rope_swa": [1, 8, 64, 256, 4096],
@@ -259,10 +332,12 @@ KERNEL_T: Dict[str, List[int]] = {
     "finalize": [1, 64, 4096],
     "router_maps": [1, 128, 4096, 65536],
     "expert_maps": [1, 64, 4096, 65536],
+    "router_gemm": [1, 32, 256, 4096, 8192],
+    "router_gemm_cublas": [1, 32, 256, 4096, 8192],
 }
 
 
-def run_kernel(name: str, dev, T: int, peak: float, stream) -> dict:
+def run_kernel(name: str, dev, T: int, peak: float, stream, tflops_peak: float = 1677.6) -> dict:
     if name == "qk_norm_rope_swa":
         return bench_qk(dev, T, False, peak, stream)
     if name == "qk_norm_rope_rnope":
@@ -279,4 +354,8 @@ def run_kernel(name: str, dev, T: int, peak: float, stream) -> dict:
         return bench_router_maps(dev, T, peak, stream)
     if name == "expert_maps":
         return bench_expert_maps(dev, T, peak, stream)
+    if name == "router_gemm":
+        return bench_router_gemm(dev, T, peak, stream, tflops_peak)
+    if name == "router_gemm_cublas":
+        return bench_router_gemm_cublas(dev, T, peak, stream, tflops_peak)
     raise ValueError(name)

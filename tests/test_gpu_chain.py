@@ -1,7 +1,7 @@
 """The decode chain on the GPU: every stage of every layer checked against the CPU oracle on
-the inputs that stage actually received (the router GEMM is a cuBLAS call, checked to bf16
-rounding; everything after it is checked on its GPU output), for SWA and RNoPE layers, and
-the CUDA-graph replay checked against the eager run."""
+the inputs that stage actually received (the router GEMM, on the tensor cores by default or on
+cuBLAS, is checked to bf16 rounding; everything after it is checked on its GPU output), for
+SWA and RNoPE layers, and the CUDA-graph replay checked against the eager run."""
 from __future__ import annotations
 
 import numpy as np
@@ -39,7 +39,7 @@ def make_checker(seen, layers_to_check=None):
             assert_bf16_close(c["k_out"], rk, f"layer {i} k")
         elif stage == "gate":
             ref = orc.router_logits_ref(c["x"].float(), c["w"].float())
-            # cuBLAS accumulates in another order; both round to bf16 before the cast.
+            # the GEMM accumulates in another order; both round to bf16 before the cast.
             torch.testing.assert_close(c["logits"], ref, rtol=2.0 ** -7, atol=2e-3)
             assert torch.equal(c["logits"], c["logits"].to(torch.bfloat16).float())
         elif stage == "router_maps":
@@ -56,12 +56,13 @@ def make_checker(seen, layers_to_check=None):
     return check
 
 
-@pytest.mark.parametrize("T", [1, 3, 40])
-def test_chain_stages_match_oracle(T):
+@pytest.mark.parametrize("T,gate", [(1, "tcgen05"), (3, "tcgen05"), (40, "tcgen05"),
+                                    (40, "cublas")])
+def test_chain_stages_match_oracle(T, gate):
     dev = torch.device("cuda")
     layers = dc.make_layers(5, dev)   # layer 4 is the RNoPE (full-attention) layer
     assert [L.rnope for L in layers] == [False, False, False, False, True]
-    chain = dc.DecodeChain(T, layers, dev)
+    chain = dc.DecodeChain(T, layers, dev, gate=gate)
     seen = []
     chain.run_layers(torch.cuda.current_stream(), record=make_checker(seen))
     torch.cuda.synchronize()

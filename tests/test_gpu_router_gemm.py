@@ -86,6 +86,22 @@ def test_router_gemm_forced_tiles(forced, bn, ks, T):
     check(x, w, b)
 
 
+@pytest.mark.parametrize("bn", [64, 128, 192])
+def test_router_gemm_per_tile_path(forced, monkeypatch, bn):
+    # one hidden split, each tile ranked on its own and the tiles merged per token tile (the
+    # path of grids larger than the SMs), forced at a small T
+    forced(bn, 1)
+    monkeypatch.setenv("KB_RGEMM_COOP", "0")
+    x, w, b = inputs(300, seed=bn)
+    check(x, w, b)
+    check(x, w, None, k=8, renorm=True)
+
+
+def test_router_gemm_more_tiles_than_sms():
+    x, w, b = inputs(20000, seed=7)
+    check(x, w, b)
+
+
 @pytest.mark.parametrize("E,k,renorm", [(128, 1, False), (256, 8, True), (512, 6, False),
                                         (448, 4, True), (64, 8, False)])
 def test_router_gemm_shapes(E, k, renorm):
