@@ -42,7 +42,8 @@ namespace rg {
 constexpr int BM = 128;            // tokens per tile (UMMA M)
 constexpr int BK = 64;             // hidden elements per k-block: one 128-byte swizzle row
 constexpr int UK = 16;             // UMMA K of 16-bit inputs
-constexpr int THREADS = 128;       // four warps: TMEM lane quarters 0..3
+constexpr int THREADS = 256;       // eight warps: warp w reads TMEM lane quarter w % 4,
+                                   // warps 4..7 the second half of each row's columns
 constexpr int KMAX = 8;            // largest top-K
 constexpr int A_BYTES = BM * BK * 2;
 constexpr size_t kSmemCap = 200 * 1024;
@@ -379,8 +380,9 @@ __device__ __forceinline__ void coop_epilogue(const Args& a, const Plan& p, uint
     float* out = a.logits ? a.logits : reinterpret_cast<float*>(a.ws + p.lgs);
     const int bn = p.bn;
     const bool split = p.ks > 1;
+    const int half = bn / 2, c_lo = (int)(threadIdx.x >> 7) * half;
 #pragma unroll 1
-    for (int c = 0; c < bn; c += 32) {
+    for (int c = c_lo; c < c_lo + half; c += 32) {
         float v[32];
         tmem_ld32(trow + (uint32_t)c, v);
         if (!split) {
@@ -582,7 +584,8 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     __syncwarp();
 
     // ---------------- epilogue: thread r = TMEM lane r = token m0 + r ----------------
-    const int r = threadIdx.x;
+    const int r = threadIdx.x & (BM - 1);          // TMEM lane = token row of the tile
+    const int ch = threadIdx.x >> 7;               // which half of the row's columns
     const int64_t t = m0 + r;
     const bool valid = t < a.T;
     bool ok = !dead && bar_wait(accum, 0u, err, a.spin);
@@ -590,7 +593,7 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     ok = __syncthreads_and(ok) != 0;
     pdl_launch();
     const int E = a.E, K = a.K;
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     constexpr int RS = BN + 4;                     // padded row stride of the tile (floats)
     float* red = reinterpret_cast<float*>(sm);     // the tile's logits [BM][RS] (ring is free)
     bool have = false;                             // red holds the rounded tile (per-tile path)
@@ -602,7 +605,7 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     } else if (ok) {
         // one hidden split, more tiles than SMs: TMEM -> bf16-rounded row in shared memory
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = ch * (BN / 2); c < (ch + 1) * (BN / 2); c += 32) {
             float v[32];
             tmem_ld32(trow + (uint32_t)c, v);
 #pragma unroll
@@ -632,7 +635,7 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     // which ranks first) enter the register top-K, in ascending column order.
     TopK tk;
     tk.init();
-    const bool have_row = have && a.ids && valid;
+    const bool have_row = have && a.ids && valid && ch == 0;   // one thread per row ranks
     if (have_row) {
         const float* row = red + r * RS;
         const uint32_t tau = (BN / 16 >= K) ? group_tau<BN>(row, bias_sm, K) : 0u;
@@ -685,7 +688,7 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
                 flag[1] = last;
             }
             __syncthreads();
-            if (flag[1] && valid) {
+            if (flag[1] && valid && ch == 0) {
                 __threadfence();
                 TopK f;
                 f.init();
