@@ -710,6 +710,11 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
         }
     }
 
+    // Before its tensor memory is freed, every MMA the CTA issued must have completed: the
+    // MMA thread always commits to `accum`, so after an epilogue wait that gave up this waits
+    // for that phase (bounded by the default limit, not the caller's).
+    if (!dead && threadIdx.x == 64)
+        for (long long it = 0; it < kSpin && !bar_try(accum, 0u); ++it) __nanosleep(32);
     tc_fence_before();
     __syncthreads();
     if (warp == 2)

@@ -9,6 +9,8 @@ Two ways to reach the error path, neither of which faults, traps or hangs a GPU:
     multi-CTA maps kernel and the decode chain's logit all-gather give up on purpose; the call
     returns (bounded), the host reads the error word, and after a re-zero with the default
     limit the same call is correct again.
+The tensor-core router GEMM (kb_router_gemm) is covered the same way: its mbarrier waits and
+grid barriers give up under the one-poll limit, and a poisoned workspace makes it do nothing.
 """
 from __future__ import annotations
 
@@ -177,3 +179,50 @@ def test_noalloc_status_clean_after_calls():
     p2u = torch.empty(64 * K, dtype=torch.int32, device=dev)
     ops.expert_maps_noalloc(ids, c, off, p2u)
     assert ops.workspace_status(None, _lib.KB_WS_NOALLOC, dev) == _lib.KB_WS_CLEAN
+
+
+def _router_gemm_call(lib, x, w, b, ids, wt, ws, T):
+    return lib.kb_router_gemm(x.data_ptr(), w.data_ptr(), b.data_ptr(), None, ids.data_ptr(),
+                              wt.data_ptr(), ws.data_ptr(), ws.numel(), T, wl.HIDDEN, E, K, 0,
+                              torch.cuda.current_stream().cuda_stream)
+
+
+def _gate_inputs(T, dev):
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, wl.HIDDEN, generator=g).to(torch.bfloat16).to(dev)
+    w = (0.02 * torch.randn(E, wl.HIDDEN, generator=g)).to(torch.bfloat16).to(dev)
+    b = (0.1 * torch.randn(E, generator=g)).to(dev)
+    return x, w, b
+
+
+@pytest.mark.parametrize("T", [1, 256, 20000])
+def test_router_gemm_poisoned_and_forced_timeout(T):
+    dev = torch.device("cuda")
+    lib = _lib.load()
+    x, w, b = _gate_inputs(T, dev)
+    ids = torch.full((T, K), -7, dtype=torch.int32, device=dev)
+    wt = torch.empty(T, K, device=dev)
+    ws = torch.zeros(lib.kb_router_gemm_workspace_bytes(T, wl.HIDDEN, E, K), dtype=torch.uint8,
+                     device=dev)
+    # a poisoned workspace: the call does no work and the status reports it
+    ws[:4].view(torch.int32)[0] = _lib.KB_WS_TIMEOUT
+    assert _router_gemm_call(lib, x, w, b, ids, wt, ws, T) == 0
+    assert ops.workspace_status(ws, _lib.KB_WS_RGEMM) == _lib.KB_WS_TIMEOUT
+    assert bool((ids == -7).all())
+    # every wait gives up after one poll: the call returns and the host sees the error
+    ws.zero_()
+    old = ops.set_wait_limit(1)
+    try:
+        assert _router_gemm_call(lib, x, w, b, ids, wt, ws, T) == 0
+        torch.cuda.synchronize()
+    finally:
+        ops.set_wait_limit(old)
+    assert ops.workspace_status(ws, _lib.KB_WS_RGEMM) in (_lib.KB_WS_CLEAN, _lib.KB_WS_TIMEOUT)
+    # zero-filled again, with the default limit: correct
+    ws.zero_()
+    assert _router_gemm_call(lib, x, w, b, ids, wt, ws, T) == 0
+    torch.cuda.synchronize()
+    assert ops.workspace_status(ws, _lib.KB_WS_RGEMM) == _lib.KB_WS_CLEAN
+    _, _, ref = orc.router_gemm_ref(x.cpu(), w.cpu(), b.cpu())
+    rid, _ = orc.router_ref(ref, b.cpu())
+    assert (ids.cpu() == rid).all(1).float().mean().item() > 0.98
