@@ -790,6 +790,53 @@ __global__ void __launch_bounds__(kPW * 32) maps_persistent_kernel(
                 u2p);
 }
 
+// Maps from ids for E in {128, 256, 384} (kb_expert_maps at T > 768): the map phases of the
+// tile kernel (maps_finish_tile: token masks per 32-token tile, the histogram published and the
+// grid barrier entered before the CTA-local placement, staged coalesced writes) on the CTA's
+// ids, loaded as 16-bit experts (ids outside [0, E) become 0xFFFF and are skipped).  One
+// cooperative launch, one CTA of 256 threads per SM.
+// smem: sel (u16)[tpc*K, padded to 8] | hist[E] | totsm[E] | offs[E+1, padded to 4]
+//       | scratch[64] | the map phases' arrays (tile_maps_ints, staged)
+template <int E_>
+__global__ void __launch_bounds__(256) maps_ids_tile_kernel(
+    const int32_t* __restrict__ ids_in, int64_t T, int K, int tpc, int32_t* __restrict__ counts,
+    int64_t* __restrict__ offsets, int32_t* __restrict__ p2u, int32_t* __restrict__ u2p,
+    PersistWs ws) {
+    pdl_wait();
+    extern __shared__ __align__(16) int ism[];
+    const int selw = (int)(tile_align_c((size_t)tpc * K, 8) / 2);
+    uint16_t* sel = reinterpret_cast<uint16_t*>(ism);
+    int* hist = ism + selw;
+    int* totsm = hist + E_;
+    int* offs = totsm + E_;
+    int* scratch = offs + tile_align_c(E_ + 1, 4);
+    int* free_sm = scratch + 64;
+    if (ws_poisoned(ws, E_, offsets)) return;
+    const int c = blockIdx.x;
+    const int64_t t0 = (int64_t)c * tpc;
+    const int64_t t1 = min(T, t0 + tpc);
+    const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
+    const int32_t* src = ids_in + t0 * K;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = __ldg(src + i);
+        sel[i] = (e >= 0 && e < E_) ? (uint16_t)e : (uint16_t)0xFFFFu;
+    }
+    __syncthreads();
+    // The token masks count tokens, so they need a token's experts to be distinct (as a
+    // router's are).  A CTA holding a token that names one expert twice places its selections
+    // with the per-warp counts instead (maps_finish_tile's unstaged placement).
+    bool dup = false;
+    const int ntok = n / K;
+    for (int tk = threadIdx.x; tk < ntok; tk += blockDim.x) {
+        const uint16_t* r = sel + tk * K;
+        for (int a = 1; a < K; ++a)
+            for (int b = 0; b < a; ++b) dup |= (r[a] == r[b]) && (r[a] != 0xFFFFu);
+    }
+    const bool staged = __syncthreads_or(dup) == 0;
+    maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, free_sm, staged, counts,
+                         offsets, p2u, u2p);
+}
+
 // Hybrid-router persistent kernel (see trouter.cuh).
 // smem: bias[E] | wsm[nw][hwarp] (phase 1) = whist[nw][E] (phase 3) | sel_tmp[nw][32]
 //       | sel[tpc*K] | hist[E] | totsm[E] | offs[E+1] | scratch[64]
@@ -1485,7 +1532,7 @@ DevInfo dev_info() {
     return d;
 }
 
-enum class Path { Single, Persistent, TPersistent, Tile, TwoKernel };
+enum class Path { Single, Persistent, TPersistent, Tile, IdsTile, TwoKernel };
 
 struct MapsPlan {
     Path path;
@@ -1905,6 +1952,51 @@ struct MapsLaunchT {
             }
         }
 
+        // Maps from ids through the tile kernel's map phases (E = 32*VPL in {128, 256, 384}).
+        static size_t ids_tile_smem(int tpc, int K) {
+            constexpr int E_ = 32 * VPL;
+            return (tile_align((size_t)tpc * K, 8) / 2 + 2 * (size_t)E_ + tile_align(E_ + 1, 4) +
+                    64 + tile_maps_ints(256, E_, tpc * K, K, true)) * sizeof(int);
+        }
+        static bool plan_ids_tile(MapsPlan& p, int64_t T, int E, int K) {
+            if constexpr (ROUTE || !VEC || 32 * VPL > 384) {
+                return false;
+            } else {
+                constexpr int E_ = 32 * VPL;
+                if (E != E_ || T < kTileRows || T > (int64_t)INT32_MAX) return false;
+                const int sms = dev_info().sms;
+                int grid = (int)std::min<int64_t>(std::min(kMaxPersistGrid, sms),
+                                                  (T + kTileRows - 1) / kTileRows);
+                grid = std::max(grid, 1);
+                const int64_t tpc = (T + grid - 1) / grid;
+                if (tpc * K > kMaxPersistSel) return false;
+                const size_t smem = ids_tile_smem((int)tpc, K);
+                if (smem > kMaxSmem) return false;
+                static std::mutex mu;
+                static std::map<std::tuple<int, size_t>, int> cache;
+                int dev = 0;
+                cudaGetDevice(&dev);
+                {
+                    std::lock_guard<std::mutex> lk(mu);
+                    int& v = cache[std::make_tuple(dev, smem)];
+                    if (v == 0) {
+                        int occ = 0;
+                        auto* kern = maps_ids_tile_kernel<E_>;
+                        allow_smem(kern, smem);
+                        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, smem) !=
+                            cudaSuccess)
+                            occ = 0;
+                        v = occ > 0 ? occ : -1;
+                    }
+                    if (v < 1) return false;
+                }
+                p.grid = (int)((T + tpc - 1) / tpc);
+                p.tpc = (int)tpc;
+                p.smem_persist = smem;
+                return true;
+            }
+        }
+
         static MapsPlan plan(int64_t T, int E, int K, int mode, bool allow_tile = true) {
             MapsPlan p{};
             const bool fits_single = T * K <= kMaxSingleSel;
@@ -1922,6 +2014,12 @@ struct MapsLaunchT {
             const bool hybrid_ok = multi && mode != KB_MAPS_WARP_ROUTER;
             if (tile_ok && allow_tile && plan_tile(p, T, E, K)) {
                 p.path = Path::Tile;
+                p.ws_bytes = persist_ws_bytes(p.grid, E);
+            } else if (!ROUTE && (mode == KB_MAPS_AUTO || mode == KB_MAPS_MULTI_CTA) &&
+                       plan_ids_tile(p, T, E, K)) {
+                // ids only: the tile kernel's map phases (KB_MAPS_WARP_ROUTER / HYBRID_ROUTER
+                // keep the warp-per-token persistent kernel's map phases reachable)
+                p.path = Path::IdsTile;
                 p.ws_bytes = persist_ws_bytes(p.grid, E);
             } else if (hybrid_ok && plan_tpersist(p, T, E, K)) {
                 p.path = Path::TPersistent;
@@ -1976,6 +2074,17 @@ struct MapsLaunchT {
                     return launch_coop(kern, dim3(p.grid), dim3(32 * p.tnw), p.smem_persist, st,
                                        logits, bias, ids_out, w, T, K, renorm, p.tpc, counts,
                                        offsets, p2u, u2p, carve_persist(ws, p.grid, E));
+                }
+            }
+            if constexpr (!ROUTE && VEC && 32 * VPL <= 384) {
+                if (p.path == Path::IdsTile) {
+                    constexpr int E_ = 32 * VPL;
+                    auto* kern = maps_ids_tile_kernel<E_>;
+                    int err = allow_smem(kern, p.smem_persist);
+                    if (err) return err;
+                    return launch_coop(kern, dim3(p.grid), dim3(256), p.smem_persist, st, ids_in, T,
+                                       K, p.tpc, counts, offsets, p2u, u2p,
+                                       carve_persist(ws, p.grid, E));
                 }
             }
             if (p.path == Path::Persistent) {
@@ -2040,6 +2149,8 @@ struct MapsLaunchT {
             if (plan_tpersist(r, T, E, K)) b = std::max(b, persist_ws_bytes(r.grid, E));
             MapsPlan v{};
             if (plan_tile(v, T, E, K)) b = std::max(b, persist_ws_bytes(v.grid, E));
+            MapsPlan u{};
+            if (plan_ids_tile(u, T, E, K)) b = std::max(b, persist_ws_bytes(u.grid, E));
             return b;
         }
 
@@ -2048,7 +2159,7 @@ struct MapsLaunchT {
                              int* grid) {
             const MapsPlan p = plan(T, E, K, mode);
             const bool pers = p.path == Path::Persistent || p.path == Path::TPersistent ||
-                              p.path == Path::Tile;
+                              p.path == Path::Tile || p.path == Path::IdsTile;
             // Routing paths name their router kernel: the hybrid and the warp-per-token router.
             const int pk = p.path == Path::Single ? KB_MAPS_SINGLE_CTA
                          : (ROUTE && p.path == Path::TPersistent) ? KB_MAPS_HYBRID_ROUTER

@@ -271,3 +271,23 @@ def test_router_maps_tile_path_tails():
         assert torch.equal(ids.cpu(), rid), T
         torch.testing.assert_close(w.cpu(), rw, rtol=1e-6, atol=0)
         check_maps(rid, (c, off, p2u, u2p))
+
+
+@pytest.mark.parametrize("T", [800, 4096, 65536])
+@pytest.mark.parametrize("E", [128, 256, 384, 512])
+def test_maps_ids_paths(T, E):
+    """Maps from ids above the single-CTA size: the tile map phases (AUTO, MULTI_CTA; E in
+    {128, 256, 384}) and the warp-per-token persistent kernel's map phases (forced with
+    KB_MAPS_WARP_ROUTER), on routed ids (distinct experts per token), on ids that repeat an
+    expert inside a token and on ids outside [0, E)."""
+    g = torch.Generator().manual_seed(T + E)
+    scores = torch.rand(T, E, generator=g)
+    routed = torch.topk(scores, 6, dim=-1).indices.to(torch.int32)
+    dups = routed.clone()
+    dups[::7, 1] = dups[::7, 0]                  # one expert twice in every 7th token
+    bad = routed.clone()
+    bad[::5, 2] = -1
+    bad[::9, 4] = E + 3
+    for ids in (routed, dups, bad):
+        for mode in (ops.KB_MAPS_AUTO, ops.KB_MAPS_MULTI_CTA, ops.KB_MAPS_WARP_ROUTER):
+            check_maps(ids, ops.expert_maps(ids.cuda(), E, mode=mode), E)
