@@ -594,8 +594,8 @@ __device__ void place_by_masks(const uint16_t* sel, int ntok, int K, int E, cons
 template <int E>
 __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t t0, int n,
                                  const uint16_t* sel, int* hist, int* totsm, int* offs,
-                                 int* scratch, int* free_sm, bool staged, int32_t* counts,
-                                 int64_t* offsets, int32_t* p2u, int32_t* u2p) {
+                                 int* scratch, int* free_sm, bool staged, bool hist_ready,
+                                 int32_t* counts, int64_t* offsets, int32_t* p2u, int32_t* u2p) {
     static_assert(E % 4 == 0, "int4 rows");
     constexpr int Q4 = E / 4;
     const int grid = gridDim.x, c = blockIdx.x, nthr = blockDim.x, tid = threadIdx.x;
@@ -613,6 +613,20 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     unsigned* tmask = reinterpret_cast<unsigned*>(stage_r + n);
     unsigned* tbase = tmask + (size_t)ntiles * E;
     __syncthreads();  // selections complete; the ring is free
+    // Publish the CTA histogram (row of rowhist, group sum) and enter the grid barrier.
+    // Atomics reach L2 at once, so the release of grid_arrive does not wait behind stores
+    // that are still buffered.
+    auto publish_and_arrive = [&]() {
+        for (int e = tid; e < E; e += nthr) {
+            const int v = hist[e];
+            atomicExch(ws.rowhist + (size_t)c * E + e, v);
+            if (v) atomicAdd(ws.gsum + (size_t)g * E + e, v);
+        }
+        grid_arrive(ws);
+    };
+    // hist_ready: the histogram was counted while the selections were made, so it is published
+    // at once and the masks and the CTA-local placement below overlap the other CTAs' arrival.
+    if (hist_ready) publish_and_arrive();
     if (staged) {
         for (int i = tid; i < ntiles * E; i += nthr) tmask[i] = 0u;
         __syncthreads();
@@ -624,14 +638,7 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
         __syncthreads();
         scan_over_warps(E, whist, hist);  // hist = CTA histogram, whist exclusive over warps
     }
-    // Atomics reach L2 at once, so the release of grid_arrive does not wait behind stores
-    // that are still buffered.
-    for (int e = tid; e < E; e += nthr) {
-        const int v = hist[e];
-        atomicExch(ws.rowhist + (size_t)c * E + e, v);
-        if (v) atomicAdd(ws.gsum + (size_t)g * E + e, v);
-    }
-    grid_arrive(ws);
+    if (!hist_ready) publish_and_arrive();
     // While the other CTAs arrive: CTA-local expert offsets, CTA-sorted positions.
     scan_experts(hist, E, loc, scratch);  // barriers inside
     __syncthreads();
@@ -654,17 +661,17 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
         const int4* gs4 = reinterpret_cast<const int4*>(ws.gsum);
         const int4* rh4 = reinterpret_cast<const int4*>(ws.rowhist + (size_t)g * kGS * E);
         int4 bs = make_int4(0, 0, 0, 0), ts = make_int4(0, 0, 0, 0);
-        for (int rb = r0; rb < nrows; rb += 8 * R) {
-            int4 v[8];
+        for (int rb = r0; rb < nrows; rb += 10 * R) {   // kGS + ceil(148/kGS) rows: one round
+            int4 v[10];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 10; ++u) {
                 const int r = rb + u * R;
                 v[u] = make_int4(0, 0, 0, 0);
                 if (r < nrows)
                     v[u] = __ldcg(r < ng ? gs4 + (size_t)r * Q4 + qd : rh4 + (size_t)(r - ng) * Q4 + qd);
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 10; ++u) {
                 const int r = rb + u * R;
                 const bool tot = r < ng, bef = (r < g) || (r >= ng);
                 if (tot) { ts.x += v[u].x; ts.y += v[u].y; ts.z += v[u].z; ts.w += v[u].w; }
@@ -816,10 +823,14 @@ __global__ void __launch_bounds__(256) maps_ids_tile_kernel(
     const int64_t t0 = (int64_t)c * tpc;
     const int64_t t1 = min(T, t0 + tpc);
     const int n = (t1 > t0) ? (int)((t1 - t0) * K) : 0;
+    for (int e = threadIdx.x; e < E_; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
     const int32_t* src = ids_in + t0 * K;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = __ldg(src + i);
-        sel[i] = (e >= 0 && e < E_) ? (uint16_t)e : (uint16_t)0xFFFFu;
+        const bool ok = e >= 0 && e < E_;
+        sel[i] = ok ? (uint16_t)e : (uint16_t)0xFFFFu;
+        if (ok) atomicAdd(&hist[e], 1);   // the CTA histogram, published before the masks
     }
     __syncthreads();
     // The token masks count tokens, so they need a token's experts to be distinct (as a
@@ -833,8 +844,8 @@ __global__ void __launch_bounds__(256) maps_ids_tile_kernel(
             for (int b = 0; b < a; ++b) dup |= (r[a] == r[b]) && (r[a] != 0xFFFFu);
     }
     const bool staged = __syncthreads_or(dup) == 0;
-    maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, free_sm, staged, counts,
-                         offsets, p2u, u2p);
+    maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, free_sm, staged, true,
+                         counts, offsets, p2u, u2p);
 }
 
 // Hybrid-router persistent kernel (see trouter.cuh).
@@ -1105,7 +1116,10 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
         asm volatile("bar.arrive %0, %1;" ::"r"(kTileSetupBar), "r"((int)blockDim.x) : "memory");
     } else {
         const int nt = blockDim.x - 32, t = threadIdx.x - 32;
-        for (int e = t; e < E_; e += nt) bias_sm[e] = bias ? __ldg(bias + e) + 0.0f : 0.0f;
+        for (int e = t; e < E_; e += nt) {
+            bias_sm[e] = bias ? __ldg(bias + e) + 0.0f : 0.0f;
+            if constexpr (MAPS) hist[e] = 0;   // counted as the selections are made
+        }
         asm volatile("bar.sync %0, %1;" ::"r"(kTileSetupBar), "r"((int)blockDim.x) : "memory");
     }
 
@@ -1308,7 +1322,10 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
                     if (i < K) {
                         oi[lane * K + i] = idx[i];
                         ow[lane * K + i] = wv[i];
-                        if constexpr (MAPS) sp[i] = (uint16_t)idx[i];
+                        if constexpr (MAPS) {
+                            sp[i] = (uint16_t)idx[i];
+                            atomicAdd(&hist[idx[i]], 1);
+                        }
                     }
                 }
             }
@@ -1324,7 +1341,10 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
                 if (lane < K) {
                     oi[l * K + lane] = id;
                     ow[l * K + lane] = wl;
-                    if constexpr (MAPS) sel[(int)(tb + l - t0) * K + lane] = (uint16_t)id;
+                    if constexpr (MAPS) {
+                        sel[(int)(tb + l - t0) * K + lane] = (uint16_t)id;
+                        atomicAdd(&hist[id], 1);
+                    }
                 }
                 __syncwarp();
             }
@@ -1353,7 +1373,7 @@ __global__ void __launch_bounds__(kTileMaxThreads, 1) maps_tile_kernel(
     if constexpr (MAPS) {
         const bool staged =
             tile_maps_ints(blockDim.x, E_, n, K, true) <= (size_t)nslot * C::SLOT_FLOATS;
-        maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, whist, staged,
+        maps_finish_tile<E_>(ws, T, K, t0, n, sel, hist, totsm, offs, scratch, whist, staged, true,
                              counts, offsets, p2u, u2p);
     }
 }
