@@ -542,10 +542,22 @@ __device__ void build_tile_masks(const uint16_t* sel, int ntok, int K, int E, un
 
 // Per expert e: tbase[tile][e] = selections of e in the tiles before `tile`; returns the
 // CTA total of e (thread e, e + blockDim, ...).
-__device__ void tile_prefix(const unsigned* mask, int ntiles, int E, unsigned* tbase, int* hist) {
+__device__ void tile_prefix(const unsigned* __restrict__ mask, int ntiles, int E,
+                            unsigned* __restrict__ tbase, int* __restrict__ hist) {
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         unsigned run = 0;
-        for (int t = 0; t < ntiles; ++t) {
+        int t = 0;
+        for (; t + 4 <= ntiles; t += 4) {   // four tiles' masks loaded before they are summed
+            unsigned m[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) m[u] = mask[(size_t)(t + u) * E + e];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                tbase[(size_t)(t + u) * E + e] = run;
+                run += (unsigned)__popc(m[u]);
+            }
+        }
+        for (; t < ntiles; ++t) {
             const unsigned m = mask[(size_t)t * E + e];
             tbase[(size_t)t * E + e] = run;
             run += (unsigned)__popc(m);
@@ -557,8 +569,9 @@ __device__ void tile_prefix(const unsigned* mask, int ntiles, int E, unsigned* t
 // CTA-sorted position of every selection: loc[e] (the CTA's offset of expert e) + the
 // selections of e in earlier tiles + the tile's earlier tokens that selected e.  The order
 // inside each expert is token order, which is selection order.
-__device__ void place_by_masks(const uint16_t* sel, int ntok, int K, int E, const int* loc,
-                               const unsigned* mask, const unsigned* tbase, int* stage_sel) {
+__device__ void place_by_masks(const uint16_t* __restrict__ sel, int ntok, int K, int E,
+                               const int* __restrict__ loc, const unsigned* __restrict__ mask,
+                               const unsigned* __restrict__ tbase, int* __restrict__ stage_sel) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int ntiles = (ntok + 31) >> 5;
     const unsigned lt = (1u << lane) - 1u;
@@ -707,20 +720,29 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
             for (int i = tid; i < n; i += nthr) stage_r[i] = -1;
             __syncthreads();
         }
-        for (int j = tid; j < nvalid; j += nthr) {
-            const int i = stage_sel[j];
-            const int r = hist[sel[i]] + j;
-            const unsigned tl = (unsigned)i / (unsigned)K;
-            const int sl = i - (int)tl * K;
-            p2u[r] = (int32_t)((int64_t)sl * T + t0 + tl);
-            stage_r[i] = r;
+        {
+            const int* __restrict__ ss = stage_sel;
+            const uint16_t* __restrict__ se = sel;
+            const int* __restrict__ hb = hist;
+            int* __restrict__ sr = stage_r;
+#pragma unroll 4
+            for (int j = tid; j < nvalid; j += nthr) {
+                const int i = ss[j];
+                const int r = hb[se[i]] + j;
+                const unsigned tl = (unsigned)i / (unsigned)K;
+                const int sl = i - (int)tl * K;
+                p2u[r] = (int32_t)((int64_t)sl * T + t0 + tl);
+                sr[i] = r;
+            }
         }
         __syncthreads();
         if (u2p) {  // slot-major: consecutive tokens
             const int ntok = n / K;
+            const int* __restrict__ sr = stage_r;
+#pragma unroll 4
             for (int j = tid; j < n; j += nthr) {
                 const int sl = j / ntok, tl = j - sl * ntok;
-                u2p[(int64_t)sl * T + t0 + tl] = stage_r[tl * K + sl];
+                u2p[(int64_t)sl * T + t0 + tl] = sr[tl * K + sl];
             }
         }
     } else {
