@@ -512,12 +512,12 @@ __device__ bool grid_wait(const PersistWs& ws, unsigned target) {
 }
 
 // Shared-memory ints the tile kernel's map phases need beyond the selections: whist, local
-// offsets, prefix partial sums, and (staged writes) the two staging arrays and the token
-// masks and prefixes of the CTA's 32-token tiles.
+// offsets, prefix partial sums, and (staged) the token masks and prefixes of the CTA's 32-token
+// tiles.
 __host__ __device__ constexpr size_t tile_maps_ints(int nthreads, int E, int n, int K, bool staged) {
     return (size_t)(nthreads / 32) * E + tile_align_c(E + 1, 4) +
            (size_t)2 * (nthreads / (E / 4)) * E +
-           (staged ? (size_t)2 * n + (size_t)2 * ((n / (K > 0 ? K : 1) + 31) / 32) * E : 0);
+           (staged ? (size_t)2 * ((n / (K > 0 ? K : 1) + 31) / 32) * E : 0);
 }
 
 // Token masks of the CTA's 32-token tiles: mask[tile][e] bit l is set when token l of the tile
@@ -566,27 +566,6 @@ __device__ void tile_prefix(const unsigned* __restrict__ mask, int ntiles, int E
     }
 }
 
-// CTA-sorted position of every selection: loc[e] (the CTA's offset of expert e) + the
-// selections of e in earlier tiles + the tile's earlier tokens that selected e.  The order
-// inside each expert is token order, which is selection order.
-__device__ void place_by_masks(const uint16_t* __restrict__ sel, int ntok, int K, int E,
-                               const int* __restrict__ loc, const unsigned* __restrict__ mask,
-                               const unsigned* __restrict__ tbase, int* __restrict__ stage_sel) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int ntiles = (ntok + 31) >> 5;
-    const unsigned lt = (1u << lane) - 1u;
-    for (int tile = warp; tile < ntiles; tile += nw) {
-        const int tok = tile * 32 + lane;
-        if (tok >= ntok) continue;
-        for (int k = 0; k < K; ++k) {
-            const int e = (int)sel[tok * K + k];
-            if (e >= E) continue;
-            const size_t te = (size_t)tile * E + e;
-            stage_sel[loc[e] + (int)tbase[te] + __popc(mask[te] & lt)] = tok * K + k;
-        }
-    }
-}
-
 // Maps phases of the tile kernel (E % 4 == 0, blockDim >= E/4), after the CTA's selections
 // sel[0..n) (16-bit experts, tokens t0..) are in shared memory.  free_sm: the ring, free now.
 // As maps_finish, with:
@@ -595,15 +574,14 @@ __device__ void place_by_masks(const uint16_t* __restrict__ sel, int ntok, int K
 //                  atomics and no per-selection warp votes, which serialise on this GPU), and
 //                  per expert the counts of the earlier tiles (tile_prefix), which give the
 //                  CTA histogram
-//   arrive early   the CTA histogram is published and the grid barrier entered; the
-//                  CTA-local expert offsets and the CTA-sorted position of every selection
-//                  (place_by_masks: token order inside each expert) are computed while the
-//                  other CTAs arrive
+//   arrive early   the CTA histogram (counted as the selections were made) is published and
+//                  the grid barrier entered before the masks are built
 //   prefix         every thread issues its 128-bit loads of group sums and earlier rows of
 //                  its group before summing; partial sums meet in shared memory
-//   staged writes  p2u in CTA-sorted order (one run of consecutive rows per expert) and u2p
-//                  slot-major (consecutive tokens): coalesced, instead of one 32-byte sector
-//                  per selection.  Without room for the staging arrays: rank_scatter.
+//   writes         each selection's row from the masks (expert offset + earlier CTAs + the
+//                  tile bases + the tile's earlier tokens), in slot-major order so that u2p is
+//                  written coalesced.  Without room for the masks, or with a token that names
+//                  an expert twice: per-warp counts and rank_scatter.
 template <int E>
 __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t t0, int n,
                                  const uint16_t* sel, int* hist, int* totsm, int* offs,
@@ -619,11 +597,10 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     int* loc = whist + nwarps * E;
     int* part_b = loc + tile_align_c(E + 1, 4);
     int* part_t = part_b + R * E;
-    int* stage_sel = part_t + R * E;
-    int* stage_r = stage_sel + n;
+
     // Tile masks (staged path): [ntiles][E] masks and tile prefixes after the staging arrays.
     const int ntok = n / K, ntiles = (ntok + 31) >> 5;
-    unsigned* tmask = reinterpret_cast<unsigned*>(stage_r + n);
+    unsigned* tmask = reinterpret_cast<unsigned*>(part_t + R * E);
     unsigned* tbase = tmask + (size_t)ntiles * E;
     __syncthreads();  // selections complete; the ring is free
     // Publish the CTA histogram (row of rowhist, group sum) and enter the grid barrier.
@@ -653,12 +630,11 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     }
     if (!hist_ready) publish_and_arrive();
     // While the other CTAs arrive: CTA-local expert offsets, CTA-sorted positions.
-    scan_experts(hist, E, loc, scratch);  // barriers inside
-    __syncthreads();
-    const int nvalid = loc[E];
-    if (staged) {
-        place_by_masks(sel, ntok, K, E, loc, tmask, tbase, stage_sel);
-    } else {
+    // (staged: every selection's row is computed after the barrier from the masks, so no
+    // CTA-local placement here)
+    if (!staged) {
+        scan_experts(hist, E, loc, scratch);  // barriers inside
+        __syncthreads();
         for (int e = tid; e < E; e += nthr) {
             const int l = loc[e];
             for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += l;
@@ -711,41 +687,34 @@ __device__ void maps_finish_tile(const PersistWs& ws, int64_t T, int K, int64_t 
     // Fused count all-gather: CTA q < N stores this rank's totals into rank q's buffer now,
     // so the transfer overlaps the placement below; the last CTA out collects every rank's.
     if (c < ws.cp.world) count_push_send(ws.cp, totsm, c, count_push_tag(ws.cp), tid, nthr);
-    // Global row of CTA-sorted position lpos of expert e = offs[e] + hist[e] + lpos - loc[e].
-    for (int e = tid; e < E; e += nthr) hist[e] = offs[e] + hist[e] - loc[e];
-    __syncthreads();
     if (staged) {
-        // p2u in CTA-sorted order: each expert's rows are consecutive.
-        if (nvalid < n) {  // ids outside [0, E) keep u2p = -1
-            for (int i = tid; i < n; i += nthr) stage_r[i] = -1;
-            __syncthreads();
-        }
-        {
-            const int* __restrict__ ss = stage_sel;
-            const uint16_t* __restrict__ se = sel;
-            const int* __restrict__ hb = hist;
-            int* __restrict__ sr = stage_r;
-#pragma unroll 4
-            for (int j = tid; j < nvalid; j += nthr) {
-                const int i = ss[j];
-                const int r = hb[se[i]] + j;
-                const unsigned tl = (unsigned)i / (unsigned)K;
-                const int sl = i - (int)tl * K;
-                p2u[r] = (int32_t)((int64_t)sl * T + t0 + tl);
-                sr[i] = r;
-            }
-        }
+        // Row of selection (token tl, slot sl) of expert e: the expert's global offset + its
+        // selections in earlier CTAs (hist[e], from the prefix above) + those in this CTA's
+        // earlier tiles (tbase) + this tile's earlier tokens with e (popcount of the mask below
+        // the token's bit).  Slot-major order: u2p is written coalesced; ids outside [0, E)
+        // get u2p = -1.
+        for (int e = tid; e < E; e += nthr) hist[e] = offs[e] + hist[e];
         __syncthreads();
-        if (u2p) {  // slot-major: consecutive tokens
-            const int ntok = n / K;
-            const int* __restrict__ sr = stage_r;
+        const uint16_t* __restrict__ se = sel;
+        const int* __restrict__ hb = hist;
+        const unsigned* __restrict__ tb = tbase;
+        const unsigned* __restrict__ tm = tmask;
 #pragma unroll 4
-            for (int j = tid; j < n; j += nthr) {
-                const int sl = j / ntok, tl = j - sl * ntok;
-                u2p[(int64_t)sl * T + t0 + tl] = sr[tl * K + sl];
+        for (int j = tid; j < n; j += nthr) {
+            const int sl = j / ntok, tl = j - sl * ntok;
+            const int e = (int)se[tl * K + sl];
+            int r = -1;
+            if (e < E) {
+                const size_t te = (size_t)(tl >> 5) * E + e;
+                r = hb[e] + (int)tb[te] + __popc(tm[te] & ((1u << (tl & 31)) - 1u));
+                p2u[r] = (int32_t)((int64_t)sl * T + t0 + tl);
             }
+            if (u2p) u2p[(int64_t)sl * T + t0 + tl] = r;
         }
     } else {
+        // Global row of CTA-sorted position lpos of expert e = offs[e] + hist[e] + lpos - loc[e].
+        for (int e = tid; e < E; e += nthr) hist[e] = offs[e] + hist[e] - loc[e];
+        __syncthreads();
         for (int e = tid; e < E; e += nthr) {
             const int d = hist[e];
             for (int wv = 0; wv < nwarps; ++wv) whist[wv * E + e] += d;
