@@ -488,10 +488,8 @@ __device__ void maps_finish(const PersistWs& ws, int64_t T, int E, int K, int64_
 // Split grid barrier: arrive once this CTA's stores are issued, do local work, then wait.
 __device__ __forceinline__ void grid_arrive(const PersistWs& ws) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ws.bar, 1u);
-    }
+    if (threadIdx.x == 0)   // release: the CTA's writes (ordered before by the barrier) first
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ws.bar) : "memory");
 }
 __device__ bool grid_wait(const PersistWs& ws, unsigned target) {
     __shared__ int ok;
