@@ -112,7 +112,8 @@ struct ChainParams {
 // Shared memory
 // ------------------------------------------------------------------------------------
 struct SmemLayout {
-    size_t bar, gqk, ga, gb, w, bias, layers, xrow, cs, sn, red, cand, sel, perm, flag, total;
+    size_t bar, gqk, ga, gb, w, bias, layers, xrow, cs, sn, red, wmax, cand, ncand, sel, perm,
+        flag, total;
 };
 __host__ __device__ constexpr size_t al128(size_t v) { return (v + 127) & ~size_t(127); }
 __host__ __device__ inline SmemLayout smem_layout(int H, int nown, int L) {
@@ -129,8 +130,10 @@ __host__ __device__ inline SmemLayout smem_layout(int H, int nown, int L) {
     s.cs = o;     o = al128(o + kChainMaxT * kHalfD * sizeof(float));
     s.sn = o;     o = al128(o + kChainMaxT * kHalfD * sizeof(float));
     s.red = o;    o = al128(o + (size_t)2 * kRedVals * 33 * sizeof(float));
-    s.cand = o;   o = al128(o + kCW * 32 * sizeof(unsigned long long));
-    s.sel = o;    o = al128(o + kCW * 32 * sizeof(int));
+    s.wmax = o;   o = al128(o + kChainMaxT * 32 * sizeof(uint32_t));
+    s.cand = o;   o = al128(o + kChainMaxT * 32 * sizeof(unsigned long long));
+    s.ncand = o;  o = al128(o + kChainMaxT * sizeof(int));
+    s.sel = o;    o = al128(o + 32 * sizeof(int));
     s.perm = o;   o = al128(o + 32 * sizeof(int));
     s.flag = o;   o = al128(o + 8 * sizeof(int));
     s.total = o;
@@ -149,8 +152,10 @@ struct Smem {
     float* cs;                 // [kChainMaxT][64]
     float* sn;                 // [kChainMaxT][64]
     float* red;                // [2][kRedVals][33] block reductions, two buffers in turn
-    unsigned long long* cand;  // [kCW][32] router candidates of each warp
-    int* sel;                  // [kCW][32] each warp's copy of the selections, (token, slot) order
+    uint32_t* wmax;            // [kChainMaxT][32] warp maxima of the router keys
+    unsigned long long* cand;  // [kChainMaxT][32] router candidates
+    int* ncand;                // [kChainMaxT]
+    int* sel;                  // [32] selections, (token, slot) order
     int* perm;                 // [32] token of each permuted row
     int* flag;                 // [8]  flag[0]: leave at the end of this layer;
                                //      flag[4 + b]: bulk-copy phases issued on buffer b
@@ -169,7 +174,9 @@ __device__ __forceinline__ Smem carve(unsigned char* base, const SmemLayout& l) 
     s.cs = reinterpret_cast<float*>(base + l.cs);
     s.sn = reinterpret_cast<float*>(base + l.sn);
     s.red = reinterpret_cast<float*>(base + l.red);
+    s.wmax = reinterpret_cast<uint32_t*>(base + l.wmax);
     s.cand = reinterpret_cast<unsigned long long*>(base + l.cand);
+    s.ncand = reinterpret_cast<int*>(base + l.ncand);
     s.sel = reinterpret_cast<int*>(base + l.sel);
     s.perm = reinterpret_cast<int*>(base + l.perm);
     s.flag = reinterpret_cast<int*>(base + l.flag);
@@ -566,7 +573,7 @@ __device__ __forceinline__ void stage_pair(const ChainParams& p, const Smem& s, 
 // Top-K of token t by K rounds over all of its keys (lane l holds experts l, l + 32, ...):
 // each round takes the warp's largest key, the lowest expert among equal keys (redux max,
 // then redux min), and clears it.  The path for rows whose keys tie at the threshold.
-__device__ void topk_rounds(const Smem& s, int t, int E, int K, int* sel) {
+__device__ void topk_rounds(const Smem& s, int t, int E, int K) {
     const int lane = threadIdx.x & 31;
     uint32_t key[kMaxChunks];
 #pragma unroll
@@ -609,71 +616,69 @@ __device__ void topk_rounds(const Smem& s, int t, int E, int K, int* sel) {
             for (int j = 0; j < kMaxChunks; ++j)
                 if (j == bj) key[j] = 0u;
         }
-        if (lane == 0) sel[t * K + r] = (int)widx;
+        if (lane == 0) s.sel[t * K + r] = (int)widx;
     }
 }
 
 // D: exact top-K of every token; the same keys and tie rule as the router kernels: score =
-// logit + (bias + 0), ordered by okey (NaN highest), the lower expert first.  Every warp ranks
-// every token by itself from the gathered logits, so no block barrier is needed between the
-// ranking and the maps, and each warp keeps its own copy of the selections:
-//  1. lane l keys experts l, l + 32, ...; tau = the K-th largest lane maximum: the K lanes with
-//     the largest maxima each hold a key >= tau, so every key of the top K is >= tau (with
-//     fewer than K lanes holding experts, tau = 0: every key is a candidate);
-//  2. the keys >= tau are compacted into the warp's candidate buffer in (lane, chunk) order;
-//  3. with C <= 32 candidates, each one's rank is the number of candidates above it in (key,
-//     then lower expert) order, found in one pass; ranks below K are the output.  More
-//     candidates (ties at tau) take the K rounds of topk_rounds.
-// Writes ids and weights (CTA 0, warp 0).  Ends with a block barrier: the next layer's bias
-// copies may then overwrite the bias every warp has read.
+// logit + (bias + 0), ordered by okey (NaN highest), the lower expert first.
+//  1. (In the all-gather, as each record arrives.)  Thread i keys experts i and i + kCT; each
+//     warp's largest key of token t is its group maximum (warp w's group: experts 32w.. and
+//     kCT + 32w..), in wmax[t][w].
+//  2. tau = the K-th largest group maximum: the K groups with the largest maxima each hold a
+//     key >= tau, so every key of the top K is >= tau.  With fewer than K groups, tau = 0
+//     (every key is a candidate).
+//  3. Keys >= tau are the candidates, appended to the token's list.
+//  4. Warp t: with C <= 32 candidates, each one's rank is the number of candidates above it
+//     in (key, then lower expert) order, found in one pass; ranks below K are the output.
+//     More candidates (ties at tau) take the K rounds of topk_rounds.
+// Leaves sel (all tokens) complete for every thread; writes ids and weights (CTA 0).
 template <int TT>
-__device__ __forceinline__ void stage_route(const ChainParams& p, const Smem& s) {
+__device__ __forceinline__ void stage_route(const ChainParams& p, const Smem& s,
+                                            const uint32_t (&key)[TT][2]) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int E = p.E, K = p.K;
-    unsigned long long* cand = s.cand + warp * 32;
-    int* sel = s.sel + warp * 32;
-    const int ng = min(32, E);  // lanes holding at least one expert
+    const int ng = min(kCW, (E + 31) >> 5);  // warps holding at least one expert
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
-        uint32_t key[kMaxChunks];
-        uint32_t lm = 0u;
+        const uint32_t mj = lane < ng ? s.wmax[t * 32 + lane] : 0u;
+        int above = 0;
 #pragma unroll
-        for (int j = 0; j < kMaxChunks; ++j) {
-            const int e = lane + 32 * j;
-            key[j] = (e < E) ? okey(s.xrow[t * E_MAX + e] + (s.bias[e] + 0.0f)) : 0u;
-            lm = max(lm, key[j]);
+        for (int i = 0; i < kCW; ++i) above += (__shfl_sync(FULL_MASK, mj, i) > mj) ? 1 : 0;
+        const uint32_t tau = (ng >= K)
+            ? __reduce_min_sync(FULL_MASK, (lane < ng && above < K) ? mj : 0xffffffffu) : 0u;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int e = tid + j * kCT;
+            const bool take = e < E && key[t][j] >= tau;
+            const unsigned b = __ballot_sync(FULL_MASK, take);
+            if (b) {  // uniform over the warp
+                int base = 0;
+                if (lane == 0) base = atomicAdd(s.ncand + t, __popc(b));
+                base = __shfl_sync(FULL_MASK, base, 0);
+                const int slot = base + __popc(b & ((1u << lane) - 1u));
+                if (take && slot < 32)
+                    s.cand[t * 32 + slot] =
+                        ((unsigned long long)key[t][j] << 32) | (unsigned)(0xffffffffu - (unsigned)e);
+            }
         }
-        uint32_t tau = 0u;
-        if (ng >= K) {
-            int above = 0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) above += (__shfl_sync(FULL_MASK, lm, i) > lm) ? 1 : 0;
-            tau = __reduce_min_sync(FULL_MASK, (lane < ng && above < K) ? lm : 0xffffffffu);
-        }
-        int cnt = 0;
-#pragma unroll
-        for (int j = 0; j < kMaxChunks; ++j) cnt += (key[j] != 0u && key[j] >= tau) ? 1 : 0;
-        const int incl = warp_incl_scan(cnt, lane);
-        const int C = __shfl_sync(FULL_MASK, incl, 31);
+    }
+    __syncthreads();
+    if (warp < TT) {
+        const int t = warp;
+        const int C = s.ncand[t];
         if (C <= 32) {
-            int pos = incl - cnt;
-#pragma unroll
-            for (int j = 0; j < kMaxChunks; ++j)
-                if (key[j] != 0u && key[j] >= tau)
-                    cand[pos++] = ((unsigned long long)key[j] << 32) |
-                                  (unsigned)(0xffffffffu - (unsigned)(lane + 32 * j));
-            __syncwarp();
-            const unsigned long long mine = lane < C ? cand[lane] : 0ull;
+            const unsigned long long mine = lane < C ? s.cand[t * 32 + lane] : 0ull;
             int rank = 0;
 #pragma unroll 8
-            for (int i = 0; i < C; ++i) rank += (cand[i] > mine) ? 1 : 0;
-            if (lane < C && rank < K) sel[t * K + rank] = (int)(0xffffffffu - (unsigned)mine);
+            for (int j = 0; j < C; ++j) rank += (s.cand[t * 32 + j] > mine) ? 1 : 0;
+            if (lane < C && rank < K) s.sel[t * K + rank] = (int)(0xffffffffu - (unsigned)mine);
         } else {
-            topk_rounds(s, t, E, K, sel);
+            topk_rounds(s, t, E, K);
         }
         __syncwarp();
-        if (lane < K && blockIdx.x == 0 && warp == 0) {
-            const int id = sel[t * K + lane];
+        if (lane < K && blockIdx.x == 0) {
+            const int id = s.sel[t * K + lane];
             p.ids[t * K + lane] = id;
             p.w[t * K + lane] = sigmoid_acc(s.xrow[t * E_MAX + id]);
         }
@@ -693,13 +698,12 @@ __device__ __forceinline__ void stage_maps_expand(const ChainParams& p, const Sm
     const int c = blockIdx.x, G = gridDim.x;
     constexpr int T = TT;
     const int E = p.E, K = p.K, n = T * K, nvec = p.H / 8;
-    const int* sel = s.sel + warp * 32;  // this warp's copy of the selections
     for (int e = c + tid * G; e <= E; e += kCT * G) {
         int below = 0, equal = 0;
 #pragma unroll
         for (int i = 0; i < kChainMaxK * TT; ++i) {
             if (i < n) {
-                const int v = sel[i];
+                const int v = s.sel[i];
                 below += (v < e) ? 1 : 0;
                 equal += (v == e) ? 1 : 0;
             }
@@ -709,12 +713,12 @@ __device__ __forceinline__ void stage_maps_expand(const ChainParams& p, const Sm
     }
     if (TT > 1 || c == 0) {
         if (warp == 0) {
-            const int e = (lane < n) ? sel[lane] : 0x7fffffff;
+            const int e = (lane < n) ? s.sel[lane] : 0x7fffffff;
             int rank = 0;
 #pragma unroll
             for (int i = 0; i < kChainMaxK * TT; ++i) {
                 if (i < n) {
-                    const int v = sel[i];
+                    const int v = s.sel[i];
                     rank += (v < e || (v == e && i < lane)) ? 1 : 0;
                 }
             }
@@ -967,13 +971,25 @@ __global__ void __launch_bounds__(kCT, 1) decode_chain_kernel(const __grid_const
                 }
             }
         }
-        // The gathered logits (every thread's records) and this layer's bias (every thread's
-        // own 4-byte copies) are complete for the whole CTA after this barrier.
+        // Router step 1 on the gathered logits: keys and the warp maxima (this thread's bias
+        // entries are its own 4-byte copies).
         cp_wait_all();
+        uint32_t key[TT][2];
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int e = tid + j * kCT;
+                key[t][j] = e < E ? okey(s.xrow[t * E_MAX + e] + (s.bias[e] + 0.0f)) : 0u;
+            }
+            const uint32_t m = __reduce_max_sync(FULL_MASK, max(key[t][0], key[t][1]));
+            if (lane == 0) s.wmax[t * 32 + warp] = m;
+        }
+        if (tid < TT) s.ncand[tid] = 0;
         __syncthreads();
 
         // ---- D: router, maps; E: expansion ----
-        stage_route<TT>(p, s);
+        stage_route<TT>(p, s, key);
         if (more) issue_bias(p, s, l + 1);  // every bias read is behind stage_route's barrier
         stage_maps_expand<TT>(p, s, x, own_perm);
 
