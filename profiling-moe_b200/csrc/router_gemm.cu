@@ -11,17 +11,20 @@
 //              S-deep shared-memory ring with 2-D tensor copies (128-byte swizzle, rows past T
 //              zero-filled); warp 1 issues tcgen05.mma (M = 128, N = BN, K = 16, bf16 inputs,
 //              fp32 accumulator in tensor memory) and releases each slot with tcgen05.commit.
-//   epilogue   thread r of the CTA owns TMEM lane r = token m*128 + r and reads its BN
-//              accumulators with tcgen05.ld.  With one hidden split they are rounded to bf16
-//              at once; with several, each split stores its fp32 partial tile and the last
-//              split to finish (an atomic ticket per (m, n)) sums the partials in split order,
-//              so the result does not depend on which CTA finishes first.  The rounded logits
-//              are stored (optional), and each thread ranks its row segment: a register top-K
-//              of keys (score order, NaN first) kept sorted by (key desc, expert asc).
-//   merge      with several expert tiles, each tile's K candidates go to the workspace and the
-//              last tile of a token tile to finish (a ticket per m) merges them in tile order
-//              and writes ids and weights.  Exact: every top-K element of the row is a top-K
-//              element of its own tile.
+//   epilogue   TMEM lane r of the CTA is token m*128 + r; warps w and w + 4 read the two
+//              halves of lane quarter w % 4's accumulators with tcgen05.ld into a shared-memory
+//              tile, which leaves for global memory as coalesced row segments.  Two forms:
+//     cooperative (the grid fits the SMs; T <= 9472 at E = 384; coop_epilogue)
+//              the tile goes out rounded to bf16 as the logits, or, with several hidden splits,
+//              as fp32 partials; after a grid barrier every CTA sums a share of the partials in
+//              split order (independent of timing) and rounds it; after a second barrier one
+//              warp per token ranks the whole row with the library's warp router.
+//     per tile (more tiles than SMs; one hidden split)
+//              each thread ranks its row segment: a 16-column group-maximum threshold, then a
+//              register top-K of the candidates, kept sorted by (key desc, expert asc); each
+//              tile's K candidates go to the workspace and the last tile of a token tile to
+//              finish (a ticket per m) merges them in tile order and writes ids and weights.
+//              Exact: every top-K element of the row is a top-K element of its own tile.
 //
 // Every wait is bounded: a wait that gives up sets the workspace error word, the CTA stops
 // issuing work, waits (bounded) for its own tensor copies and frees its tensor memory.
