@@ -60,6 +60,21 @@ def test_host_validation_without_gpu():
                                1e-6, None) == _lib.KB_ERR_UNSUPPORTED
     assert lib.kb_residual_norm_pair(None, None, None, None, None, None, 1, 64, 1e-6, 7, None) == _lib.KB_ERR_UNSUPPORTED
     assert lib.kb_add_rms_norm(None, None, None, None, None, 1, 0, 1e-6, 0, None) == _lib.KB_ERR_INVALID_ARG
+    # kb_router_gemm: (x, w_gate, bias, logits, ids, weights, ws, ws_bytes, T, H, E, K, renorm, st)
+    fake = 1 << 20   # never dereferenced: every call below is refused before any launch
+    rg = lib.kb_router_gemm
+    assert rg(None, fake, None, fake, None, None, fake, 1 << 24, 4, 6144, 384, 6, 0, None) == _lib.KB_ERR_INVALID_ARG
+    assert rg(fake, fake, None, None, None, None, fake, 1 << 24, 4, 6144, 384, 6, 0, None) == _lib.KB_ERR_INVALID_ARG
+    assert rg(fake, fake, None, None, fake, None, fake, 1 << 24, 4, 6144, 384, 6, 0, None) == _lib.KB_ERR_INVALID_ARG
+    assert rg(fake, fake, None, None, fake, fake, fake, 1 << 24, 4, 6144, 384, 9, 0, None) == _lib.KB_ERR_UNSUPPORTED
+    assert rg(fake, fake, None, None, fake, fake, fake, 1 << 24, 4, 6112, 384, 6, 0, None) == _lib.KB_ERR_UNSUPPORTED
+    assert rg(fake, fake, None, None, fake, fake, fake, 1 << 24, 4, 6144, 320 + 8, 6, 0, None) == _lib.KB_ERR_UNSUPPORTED
+    assert rg(fake, fake, None, None, fake, fake, fake, 1 << 24, 4, 6144, 576, 6, 0, None) == _lib.KB_ERR_UNSUPPORTED
+    assert rg(fake, fake, None, None, fake, fake, fake, 1 << 24, 1 << 20, 6144, 384, 6, 0, None) == _lib.KB_ERR_TOO_LARGE
+    assert rg(fake + 8, fake, None, None, fake, fake, fake, 1 << 24, 4, 6144, 384, 6, 0, None) == _lib.KB_ERR_ALIGNMENT
+    assert rg(fake, fake, None, None, fake, fake, fake + 16, 1 << 24, 4, 6144, 384, 6, 0, None) == _lib.KB_ERR_ALIGNMENT
+    need = lib.kb_router_gemm_workspace_bytes(4, 6144, 384, 6)
+    assert rg(fake, fake, None, None, fake, fake, fake, need - 256, 4, 6144, 384, 6, 0, None) == _lib.KB_ERR_WORKSPACE
 
 
 def test_workspace_sizes():
@@ -71,6 +86,10 @@ def test_workspace_sizes():
         assert ws >= prev
         prev = ws
     assert lib.kb_expert_maps_workspace_bytes(65536, 384, 6) > 0
+    # router GEMM: a fixed 256 KB zero zone, then the split partials and rounded logits (small
+    # T) or the tile candidates (more tiles than SMs)
+    for T in (1, 32, 256, 4096, 8192, 65536):
+        assert lib.kb_router_gemm_workspace_bytes(T, 6144, 384, 6) >= 256 * 1024
 
 
 def test_reference_signatures(api):

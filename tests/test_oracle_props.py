@@ -77,3 +77,20 @@ def test_router_ties_and_special_values():
     # renorm sums to one
     _, wn = orc.router_ref(x, b, k=6, renorm=True)
     torch.testing.assert_close(wn.sum(-1), torch.ones(4), rtol=1e-6, atol=1e-6)
+
+
+def test_router_gemm_oracle_matches_the_reference_formula():
+    """router_gemm_ref rounds the exact (fp64) product once to bf16; the reference's eager
+    `(x @ W_g).float()` (router_logits_ref, a bf16 matmul on the CPU) accumulates in fp32 and
+    rounds once too.  They agree within one bf16 ulp everywhere and exactly almost everywhere,
+    and the routing of the oracle is router_ref on its own logits."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(64, 1024, generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(384, 1024, generator=g)).to(torch.bfloat16)
+    b = 0.1 * torch.randn(384, generator=g)
+    ids, wt, lg = orc.router_gemm_ref(x, w, b)
+    ref = orc.router_logits_ref(x, w.t())
+    torch.testing.assert_close(lg, ref, rtol=2 ** -7, atol=1e-4)
+    assert (lg == ref).float().mean().item() > 0.99
+    rid, rw = orc.router_ref(lg, b)
+    assert torch.equal(ids, rid) and torch.equal(wt, rw)
