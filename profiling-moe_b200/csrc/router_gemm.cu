@@ -69,7 +69,7 @@ struct Plan {
     int64_t m_tiles = 0;
     size_t smem = 0;
     // workspace layout
-    size_t tk_mn = 0, tk_m = 0, zero_bytes = 0, part = 0, lgs = 0, cand = 0, total = 0;
+    size_t tk_m = 0, zero_bytes = 0, part = 0, lgs = 0, cand = 0, total = 0;
 };
 
 // ------------------------------------------------------------------------------------
@@ -801,8 +801,7 @@ bool make_plan(Plan& p, int64_t T, int H, int E, int K, int sms) {
              (size_t)bn * sizeof(float);
     p.tmem_cols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
     // workspace
-    p.tk_mn = kTicketOff;
-    p.tk_m = p.tk_mn + (size_t)p.m_tiles * p.n_tiles * sizeof(int);
+    p.tk_m = kTicketOff;   // per token tile: expert tiles merged (per-tile epilogue)
     p.zero_bytes = kZeroBytes;
     if (p.tk_m + (size_t)p.m_tiles * sizeof(int) > kZeroBytes) return false;   // T too large
     p.part = p.zero_bytes;
