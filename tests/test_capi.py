@@ -169,3 +169,18 @@ def test_ep_buffer_bytes():
         rows = N * T * 6 + T * 6
         assert rows * 12288 <= b <= rows * 12288 + 2 * 8 * 384 * 8 + 4096
         assert b % 256 == 0
+
+
+def test_router_gemm_plan():
+    """The router GEMM's tile shape on a 148-SM B200 (the library's fallback count without a
+    GPU): 192-expert tiles, and enough hidden splits for about one CTA per SM while the grid
+    fits the SMs (a cooperative launch); more tiles than SMs take one split."""
+    import ctypes
+    lib = _lib.load()
+    expect = {1: (192, 48, 96), 32: (192, 48, 96), 256: (192, 32, 128), 1024: (192, 8, 128),
+              4096: (192, 2, 128), 8192: (192, 1, 128), 20000: (192, 1, 314)}
+    for T, want in expect.items():
+        bn, ks, grid = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        assert lib.kb_router_gemm_describe(T, 6144, 384, 6, ctypes.byref(bn), ctypes.byref(ks),
+                                           ctypes.byref(grid)) == 0
+        assert (bn.value, ks.value, grid.value) == want, T
